@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 store's train step (and the forward gather).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload ("train step", one step per data-parallel batch, per GPU):
+  dim-64 fp32 table warmed with 10,000,000 int64 keys (splitmix64 sequence),
+  batches of 65,536 keys: 95 % Zipf(alpha=1.05) over the warmed keys, 5 %
+  never-seen keys inserted on miss; gradients N(0, sigma=1e-3) fp32 per row;
+  step = lookup_or_insert -> accumulate_gradients -> optimizer_step(1) with
+  Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1); keys sharded over
+  the GPUs by the hash partitioner (N > 1: all-to-all of keys, rows, grads).
+  Weak scaling: 65,536 keys per GPU per step.
+
+Also reported (rank 0, 1 GPU): the forward-lookup workload - dim-32 fp32
+store warmed with 1,000,000 uint64 keys, 400 batches of 4,096 keys Zipf(1.1).
+
+One JSON line is printed by rank 0. `value` is keys/s over all GPUs with the
+inputs resident in HBM; `e2e` is the same step through the public API with
+host (pinned) inputs and outputs copied inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+DIM = 64
+BATCH = 65_536
+NUM_KEYS = 10_000_000
+FWD_KEYS, FWD_DIM, FWD_BATCH, FWD_BATCHES = 1_000_000, 32, 4096, 400
+KEY_BYTES, M_BYTES = 8, 16
+FALLBACK_HBM_GBS = 6650.0
+# value = train-step keys/s; the forward-lookup figure rides in "forward_lookup".
+METRIC = "forward_lookup Mkeys/s & train-step keys/s at 1/2/4/8 B200; % of HBM peak"
+
+
+def args_parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--num-keys", type=int, default=NUM_KEYS)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-forward", action="store_true")
+    return p.parse_args()
+
+
+def measured_hbm():
+    f = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def owned_keys(keys_i64: np.ndarray, world: int, rank: int) -> np.ndarray:
+    """The warm keys rank `rank` owns under the hash partitioner (GPU kernel)."""
+    if world == 1:
+        return keys_i64
+    import torch
+
+    import sparse_embedding_b200 as se
+
+    d = torch.from_numpy(keys_i64).cuda()
+    ids = se.HashPartitioner(num_shards=world).partition(d)
+    return d[ids.to(torch.int64) == rank].cpu().numpy()
+
+
+def run_ours(args):
+    import torch
+
+    import sparse_embedding_b200 as se
+    from sparse_embedding_b200 import _native as N
+    from sparse_embedding_b200.workloads import ForwardWorkload, TrainWorkload
+
+    world, rank, local = dist_setup(args)
+    K, W = args.steps, args.warmup
+    wl = TrainWorkload(num_keys=args.num_keys, batch=BATCH, dim=DIM, rank=rank)
+    warm = wl.warm_keys()
+    mine = owned_keys(warm, world, rank)
+    new_total = (2 * K + W + 4) * int(round(BATCH * wl.new_fraction)) * world
+    cap = int(len(mine) + new_total / max(1, world) * 1.5 + 65536)
+    store = se.EmbeddingStore(
+        se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap),
+        optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
+    for chunk in np.array_split(mine, max(1, len(mine) // 1_000_000)):
+        store.lookup_or_insert(torch.from_numpy(chunk).cuda(), DIM)
+    torch.cuda.synchronize()
+    api = store
+    if world > 1:
+        from sparse_embedding_b200.sharded import ShardedEmbeddingStore
+
+        api = ShardedEmbeddingStore(store, "sparse_embedding.hash")
+
+    keys_np, _ = wl.make_batches(W + K, start_step=0)
+    keys_d = torch.from_numpy(keys_np).cuda()
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    grads_d = torch.randn((W + K, BATCH, DIM), generator=gen, device="cuda") * 1e-3
+    uniq = [int(np.unique(keys_np[W + s]).size) for s in range(K)]
+
+    def step(s):
+        api.lookup_or_insert(keys_d[s], DIM)
+        api.accumulate_gradients(keys_d[s], grads_d[s])
+        api.optimizer_step(1)
+
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    lib = N.lib()
+    store.profile(True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.se_kernel_launch_count()
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record()
+        for s in range(K):
+            step(W + s)
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = lib.se_kernel_launch_count() - launches0
+    store.profile(False)
+    elapsed = max_over_ranks(start.elapsed_time(end) / 1e3, world)
+    value = world * BATCH * K / elapsed
+
+    # Per-kernel device time inside the timed region.
+    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_step_probe", "cub_sort", "cub_select",
+             "k_apply_long", "k_apply"]
+    times = {}
+    for nm in names:
+        ms, cnt = store.profile_read(nm)
+        times[nm] = (ms, cnt)
+    peak, peak_kind = measured_hbm()
+    R = DIM * 4
+    n_new = int(round(BATCH * wl.new_fraction))
+    # Algorithmic bytes per launch (the figures DESIGN.md states):
+    #   lookup_or_insert: K + M + R (row read) + R (out write) per key, plus
+    #                     R (param) + R (accumulator) initialised per new key;
+    #   accumulate:       K + R read and K + R appended per gradient row;
+    #   apply:            per unique key 2R (param r/w) + 2R (accumulator r/w),
+    #                     plus R per gradient row reduced.
+    mean_u = sum(uniq) / len(uniq)
+    rows_per_owner = BATCH  # weak scaling: each owner receives ~BATCH rows per step
+    alg = {
+        "k_lookup_or_insert": rows_per_owner * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R,
+        "k_accumulate": rows_per_owner * 2 * (KEY_BYTES + R),
+        "k_apply": mean_u * 4 * R + rows_per_owner * R,
+    }
+    kern = []
+    total_ms = sum(t[0] for t in times.values())
+    for nm, (ms, cnt) in times.items():
+        entry = {"kernel": nm, "launches": cnt, "ms_total": round(ms, 4),
+                 "share": round(ms / total_ms, 4) if total_ms else None}
+        if nm in alg and cnt:
+            per = ms / cnt / 1e3
+            entry["algorithmic_bytes_per_launch"] = int(alg[nm])
+            entry["achieved_gbs"] = round(alg[nm] / per / 1e9, 1)
+        kern.append(entry)
+    dom = max((k for k in kern if "achieved_gbs" in k), key=lambda k: k["ms_total"])
+    roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": dom["achieved_gbs"], "peak": peak,
+                "unit": "GB/s", "frac": round(dom["achieved_gbs"] / peak, 4), "traffic": None,
+                "peak_source": peak_kind}
+    step_bytes = alg["k_lookup_or_insert"] + BATCH * (KEY_BYTES + R) + alg["k_apply"] - rows_per_owner * R
+    step_roof = {"algorithmic_bytes_per_step_per_gpu": int(step_bytes),
+                 "achieved_gbs_per_gpu": round(step_bytes * K / (elapsed) / 1e9, 1)}
+    step_roof["frac_of_peak"] = round(step_roof["achieved_gbs_per_gpu"] / peak, 4)
+
+    # e2e through the public API with host (pinned) buffers.
+    keys_e, grads_e = wl.make_batches(K + 1, start_step=10_000)
+    kh = [torch.from_numpy(keys_e[s]).pin_memory() for s in range(K + 1)]
+    gh = [torch.from_numpy(grads_e[s]).pin_memory() for s in range(K + 1)]
+    e2e_value = None
+    if world == 1:
+        def host_step(s):
+            vals, _ = store.lookup_or_insert(kh[s], DIM)  # host in, host out
+            store.accumulate_gradients(kh[s], gh[s])
+            store.optimizer_step(1)
+            return vals
+        host_step(0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for s in range(1, K + 1):
+            host_step(s)
+        torch.cuda.synchronize()
+        e2e_value = BATCH * K / (time.perf_counter() - t0)
+    else:
+        def host_step(s):
+            k = kh[s].cuda(non_blocking=True)
+            g = gh[s].cuda(non_blocking=True)
+            vals = api.lookup_or_insert(k, DIM)
+            api.accumulate_gradients(k, g)
+            api.optimizer_step(1)
+            return vals.cpu()
+        host_step(0)
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        for s in range(1, K + 1):
+            host_step(s)
+        torch.cuda.synchronize()
+        e2e_el = max_over_ranks(time.perf_counter() - t0, world)
+        e2e_value = world * BATCH * K / e2e_el
+    e2e = {"value": e2e_value, "unit": "keys/s", "h2d_bytes_per_step": BATCH * (2 * KEY_BYTES + R) * world,
+           "d2h_bytes_per_step": BATCH * R * world}
+
+    fwd = None
+    if world == 1 and not args.no_forward:
+        fwd = forward_bench(se, torch, N)
+
+    result = {
+        "metric": METRIC,
+        "value": value, "unit": "keys/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "single-table train step: dim 64 fp32, 10M warmed int64 keys, 65,536-key "
+                               "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
+                               "eps 1e-8, init_acc 0.1), hash partitioner",
+                   "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
+                   "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
+        "roofline": roofline, "step_roofline": step_roof, "kernels": kern,
+        "e2e": e2e, "clocks": clocks.summary(), "gpu_launches": int(launches),
+    }
+    if fwd:
+        result["forward_lookup"] = fwd
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(seconds=20.0)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return result if rank == 0 else None
+
+
+def forward_bench(se, torch, N):
+    from sparse_embedding_b200.workloads import ForwardWorkload
+
+    fw = ForwardWorkload(num_keys=FWD_KEYS, dim=FWD_DIM, batch=FWD_BATCH)
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[FWD_DIM], key_dtype="uint64", enable_optimizer=False,
+                                                 initial_capacity=FWD_KEYS))
+    warm = torch.from_numpy(fw.warm_keys()).cuda()
+    store.lookup_or_insert(warm, FWD_DIM)
+    batches = torch.from_numpy(fw.batches(FWD_BATCHES)).cuda()
+    out = torch.empty(FWD_BATCH * FWD_DIM, dtype=torch.float32, device="cuda")
+    lib = N.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    import ctypes
+
+    def run(i):
+        N.check(lib.se_forward_lookup_dim(store._h, batches[i].data_ptr(), FWD_BATCH, FWD_DIM, out.data_ptr(),
+                                          ctypes.c_void_p(st)))
+    for i in range(10):
+        run(i)
+    torch.cuda.synchronize()
+    store.profile(True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(FWD_BATCHES):
+        run(i)
+    b.record()
+    torch.cuda.synchronize()
+    store.profile(False)
+    el = a.elapsed_time(b) / 1e3
+    kms, kcnt = store.profile_read("k_lookup")
+    peak, _ = measured_hbm()
+    per_key = KEY_BYTES + M_BYTES + 2 * FWD_DIM * 4
+    kern_gbs = per_key * FWD_BATCH / (kms / kcnt / 1e3) / 1e9
+    return {"workload": "dim 32 fp32, 1M warmed uint64 keys, 400 batches x 4,096 keys Zipf(1.1)",
+            "value": FWD_BATCH * FWD_BATCHES / el / 1e6, "unit": "Mkeys/s",
+            "us_per_call": el / FWD_BATCHES * 1e6, "kernel_us": kms / kcnt * 1e3,
+            "kernel_achieved_gbs": round(kern_gbs, 1), "kernel_frac": round(kern_gbs / peak, 4),
+            "note": "4,096-key batches are launch-latency bound; the tables fit in L2 partly"}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port on the host cores
+# ---------------------------------------------------------------------------
+
+
+def cpu_train(num_keys: int, steps: int, seconds: float, threads: int):
+    from oracle import oracle as O
+    from sparse_embedding_b200.workloads import TrainWorkload
+
+    wl = TrainWorkload(num_keys=num_keys, batch=BATCH, dim=DIM)
+    s = O.OracleStore([DIM], key_dtype="int64", optimizer="adagrad", lr=0.01, eps=1e-8, initial_accumulator=0.1,
+                      threads=threads)
+    s.reserve(num_keys + 200_000, DIM)
+    s.lookup_or_insert(wl.warm_keys(), DIM)
+    keys, grads = wl.make_batches(steps + 1)
+
+    def one(b):
+        s.lookup_or_insert(keys[b], DIM)
+        s.accumulate_gradients(keys[b], grads[b], DIM)
+        s.optimizer_step(1)
+    one(0)
+    done, t0 = 0, time.perf_counter()
+    for b in range(1, steps + 1):
+        one(b)
+        done += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    el = time.perf_counter() - t0
+    return BATCH * done / el, done
+
+
+def cpu_baseline(seconds: float):
+    from oracle import oracle as O
+
+    threads = O.cpu_count()
+    value, done = cpu_train(NUM_KEYS, 50, seconds, threads)
+    return {"value": value, "unit": "keys/s", "cores": threads, "kind": "port",
+            "sample": f"{done} train steps of 65,536 keys on the 10M-key dim-64 Adagrad table (oracle port, "
+                      f"{threads} threads; insert-on-miss single-threaded as in the reference)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+
+    threads = O.cpu_count()
+    K, W = args.steps, args.warmup
+    value, done = cpu_train(args.num_keys, K + W, 120.0, threads)
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "keys/s", "n_gpus": args.gpus, "steps": done,
+            "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "single-table train step: dim 64 fp32, 10M warmed int64 keys, 65,536-key "
+                                   "batches Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad", "num_keys": args.num_keys},
+            "cpu_baseline": {"value": value, "unit": "keys/s", "cores": threads, "kind": "port",
+                             "sample": f"{done} steps of 65,536 keys (oracle port of the reference store flow; "
+                                       "the reference store itself does not build here)"},
+            "e2e": {"value": value, "unit": "keys/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = args_parse()
+    if args.impl == "reference":
+        out = run_reference(args)
+    else:
+        out = run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * se_gpu.h — C ABI of the B200 sparse-embedding store (libse_gpu.so).
+ *
+ * This is the drop-in boundary for the reference's hot path. Each entry point
+ * names the reference interface it replaces (paths relative to the
+ * sparse_embedding project root). Signatures use plain pointers and sizes
+ * only; no C++ or torch types cross the boundary.
+ *
+ * Memory spaces. Every data pointer (keys, values, gradients, partition ids)
+ * may point to host memory (pageable or pinned) or to device memory on the
+ * store's device. Host inputs are staged to the device inside the call; host
+ * outputs are complete when the call returns. With device pointers the call is
+ * asynchronous on `stream` (a cudaStream_t; NULL is the legacy default
+ * stream) and results are ready when that stream reaches the call.
+ *
+ * Errors. Every function returns 0 on success or a negative SE_ERR_* code,
+ * one per C++ exception class the reference throws for the same condition;
+ * se_last_error() returns the message (the reference's own wording where it
+ * has one) for the calling thread.
+ */
+#ifndef SE_GPU_H_
+#define SE_GPU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SE_OK 0
+#define SE_ERR_INVALID_ARGUMENT (-1) /* std::invalid_argument -> Python ValueError   */
+#define SE_ERR_RUNTIME (-2)          /* std::runtime_error    -> Python RuntimeError */
+#define SE_ERR_OVERFLOW (-3)         /* std::overflow_error   -> Python OverflowError*/
+#define SE_ERR_CUDA (-4)             /* CUDA runtime failure                          */
+#define SE_ERR_OUT_OF_MEMORY (-5)    /* device allocation failed                     */
+#define SE_ERR_TABLE_FULL (-6)       /* bounded probe or row allocation exhausted    */
+#define SE_ERR_NOT_IMPLEMENTED (-7)  /* convention not provided by the GPU store     */
+
+/* Key dtypes, in the order of se::KeyDType (sparse_embedding/src/common/dtypes.hpp:21-26). */
+enum se_key_dtype { SE_KEY_INT32 = 0, SE_KEY_UINT32 = 1, SE_KEY_INT64 = 2, SE_KEY_UINT64 = 3 };
+/* Value dtypes, in the order of se::ValueDType (dtypes.hpp:117-121). */
+enum se_value_dtype { SE_FLOAT32 = 0, SE_FLOAT16 = 1, SE_BFLOAT16 = 2 };
+enum se_optimizer_kind { SE_OPT_NONE = 0, SE_OPT_SGD = 1, SE_OPT_ADAM = 2, SE_OPT_ADAGRAD = 3 };
+enum se_init_kind { SE_INIT_ZEROS = 0, SE_INIT_UNIFORM = 1 };
+/* Registered partitioners: sparse_embedding.{modulo,hash,fast_range}. */
+enum se_partitioner_kind { SE_PART_MODULO = 0, SE_PART_HASH = 1, SE_PART_FAST_RANGE = 2 };
+
+/*
+ * Store configuration: the fields of se::EmbeddingConfig
+ * (sparse_embedding/src/interface/embedding_config.hpp:31-43) plus the
+ * initializer and optimizer configs the Python constructor takes
+ * (sparse_embedding/src/bindings/module.cpp:103-190, optimizer_config.hpp:28-44).
+ */
+typedef struct se_store_config {
+  const int64_t *dims;       /* one table per distinct dim                         */
+  size_t num_dims;
+  int32_t key_dtype;         /* enum se_key_dtype                                  */
+  int32_t value_dtype;       /* enum se_value_dtype (ParamT)                       */
+  int32_t optimizer_dtype;   /* OptT (optimizer state)                             */
+  int32_t gradient_dtype;    /* accumulated gradient storage type                  */
+  float gradient_scale;      /* finite, > 0                                        */
+  int32_t enable_optimizer;
+  int32_t init_kind;         /* enum se_init_kind                                  */
+  float init_min, init_max;  /* Uniform bounds (default -0.05, 0.05)               */
+  int32_t optimizer_kind;    /* enum se_optimizer_kind                             */
+  float lr, beta1, beta2, eps, weight_decay;
+  float initial_accumulator; /* Adagrad accumulator value for a new row            */
+  uint64_t initial_capacity; /* rows reserved per table at creation (0: default)   */
+  int32_t device;            /* CUDA device ordinal                                */
+  int32_t simd_width;        /* float lanes of the mirrored CPU build: 16 or 8     */
+  int32_t internal_shards;   /* value reported by se_store_internal_shard_count    */
+} se_store_config;
+
+typedef struct se_store se_store;
+
+/* Message of the last failing call on this thread ("" after success). */
+const char *se_last_error(void);
+/* Library build identifier. */
+const char *se_version(void);
+/* Number of CUDA kernels this library has launched in this process. */
+uint64_t se_kernel_launch_count(void);
+
+/* Replaces make_store / create_hogwild_store
+ * (sparse_embedding/src/backend/hogwild/store_factory_impl.inl:23-45,
+ *  store_construction.cpp:21-67) for the GPU store. */
+int se_store_create(const se_store_config *config, se_store **out_store);
+int se_store_destroy(se_store *store);
+
+/* EmbeddingTableFacade::forward_lookup / lookup
+ * (sparse_embedding/src/interface/embedding_table_interface.hpp:214-216, 242-244;
+ *  HogwildEmbeddingStoreCore::forward_lookup, hogwild_embedding_store.hpp:4358-4594).
+ * out_values holds num_keys rows of row_lengths[i] ParamT values; rows of keys
+ * that are absent are zero-filled. row_lengths is a host array. */
+int se_forward_lookup(se_store *store, const void *keys, size_t num_keys, void *out_values,
+                      size_t num_out_values, const int64_t *row_lengths, size_t num_row_lengths,
+                      void *stream);
+
+/* EmbeddingTableFacade::lookup_or_insert (embedding_table_interface.hpp:218-220;
+ * hogwild_embedding_store.hpp:4925-4980): absent keys are inserted once each
+ * (duplicates in one batch share one row), initialized from the key, and
+ * every position receives its row. */
+int se_lookup_or_insert(se_store *store, const void *keys, size_t num_keys, void *out_values,
+                        size_t num_out_values, const int64_t *row_lengths,
+                        size_t num_row_lengths, void *stream);
+
+/* Uniform-row-length forms of the two calls above (the Python binding's path,
+ * sparse_embedding/src/bindings/typed/module_typed_sync.inl:12-89). */
+int se_forward_lookup_dim(se_store *store, const void *keys, size_t num_keys, int64_t dim,
+                          void *out_values, void *stream);
+int se_lookup_or_insert_dim(se_store *store, const void *keys, size_t num_keys, int64_t dim,
+                            void *out_values, void *stream);
+
+/* EmbeddingTableFacade::accumulate_gradients (embedding_table_interface.hpp:246-248;
+ * hogwild_embedding_store.hpp:4607-4771). grads are in the store's gradient
+ * dtype, num_keys rows of row_lengths[i] values. Gradients are validated
+ * (GradientAccumulator::validate_input) before anything is accumulated. */
+int se_accumulate_gradients(se_store *store, const void *keys, size_t num_keys, const void *grads,
+                            size_t num_grad_scalars, const int64_t *row_lengths,
+                            size_t num_row_lengths, void *stream);
+int se_accumulate_gradients_dim(se_store *store, const void *keys, size_t num_keys, int64_t dim,
+                                const void *grads, void *stream);
+
+/* EmbeddingTableFacade::optimizer_step (hogwild_embedding_store.hpp:4777-4824):
+ * sums each key's accumulated gradients in arrival order, scales them by
+ * gradient_scale / normalization_steps and applies the optimizer once per
+ * key present in the store. */
+int se_optimizer_step(se_store *store, size_t normalization_steps, void *stream);
+
+/* Metadata conventions (embedding_table_interface.hpp:317-396). */
+int se_store_size(se_store *store, uint64_t *out_size);
+int se_store_dim_size(se_store *store, int64_t dim, uint64_t *out_size);
+int se_store_reserve(se_store *store, size_t keys, int64_t dim);
+int se_store_internal_shard_count(se_store *store, uint64_t *out_count);
+int se_store_entries_per_page(se_store *store, uint64_t *out_entries);
+/* Gradient rows dropped at optimizer_step because their key was absent. */
+int se_store_dropped_gradients(se_store *store, uint64_t *out_count);
+/* Optimizer state of one key, for checks: state holds the optimizer's state
+ * rows (Adam m then v, or the Adagrad accumulator) in OptT; *found is 0 if the
+ * key is absent. Host pointers. */
+int se_store_read_state(se_store *store, int64_t dim, uint64_t key, void *param_out,
+                        void *state_out, uint32_t *step_out, int32_t *found);
+/* Waits for all work the store has queued. */
+int se_store_synchronize(se_store *store);
+/* CUDA-event timing of the store's kernels: enable, then read the summed
+ * device time and launch count of kernels whose name contains `name`. */
+int se_store_profile_enable(se_store *store, int32_t enable);
+int se_store_profile_read(se_store *store, const char *name, double *out_ms, uint64_t *out_launches);
+
+/* PartitionerFacade::partition_span (sparse_embedding/src/ops/partitioner.hpp:48-70,
+ * 72-406) for the three registered algorithms: out[i] = partition of keys[i]. */
+int se_partition(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const void *keys,
+                 size_t num_keys, uint32_t *out_partition_ids, int32_t device, void *stream);
+/* PartitionerFacade::filter_span: out_mask[i] = (partition of keys[i] == target). */
+int se_filter(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const void *keys,
+              size_t num_keys, uint32_t target_partition, uint8_t *out_mask, int32_t device,
+              void *stream);
+
+/*
+ * Exchange routing (no reference counterpart: the reference leaves routing to
+ * the caller, sparse_embedding/partitioner.py:84-100). Device pointers only.
+ * Partitions keys and groups them by destination, stably: send_keys holds the
+ * keys of partition 0 first, each partition in input order; send_positions[j]
+ * is the input position of send_keys[j]; counts[p] is the number of keys of
+ * partition p. Keys are num_keys values of key_dtype; send_keys has the same dtype.
+ */
+int se_partition_route(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const void *keys,
+                       size_t num_keys, void *send_keys, uint32_t *send_positions,
+                       uint32_t *counts, int32_t device, void *stream);
+/* Moves rows between the routed order and the input order. row_bytes per row.
+ * scatter=0: out[positions[j]] = in[j]  (routed -> input order)
+ * scatter=1: out[j] = in[positions[j]]  (input -> routed order) */
+int se_permute_rows(const void *in_rows, void *out_rows, const uint32_t *positions, size_t num_rows,
+                    size_t row_bytes, int32_t scatter, int32_t device, void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SE_GPU_H_ */

@@ -370,12 +370,17 @@ template <class P, class O, class G> struct Table final : TableBase {
   std::vector<O> s0, s1;    // Adam m, v  |  Adagrad acc (s0)
   std::vector<uint32_t> steps;
   std::vector<float> bc1, bc2;
-  // Transient accumulation (TransientArena): key -> slot, sums kept in G.
-  KeyMap tmap;
-  std::vector<uint64_t> tkeys;
-  std::vector<G> tgrads;
+  // Transient accumulation (TransientArena), one shard per worker thread,
+  // a key's shard = splitmix64(key) % shards: key -> slot, sums kept in G.
+  struct Shard {
+    KeyMap tmap;
+    std::vector<uint64_t> tkeys;
+    std::vector<uint64_t> trows;  // gradient rows accumulated into each slot
+    std::vector<G> tgrads;
+  };
+  std::vector<Shard> shards;
 
-  Table(const Config &c, int64_t d) : cfg(c), dim_(d) {
+  Table(const Config &c, int64_t d) : cfg(c), dim_(d), shards(size_t(c.threads > 1 ? c.threads : 1)) {
     const size_t w = size_t(c.simd_width > 0 ? c.simd_width : 1);
     simd_cut = (size_t(d) / w) * w;
   }
@@ -446,29 +451,48 @@ template <class P, class O, class G> struct Table final : TableBase {
     const G *g = static_cast<const G *>(grads);
     const size_t d = size_t(dim_);
     const float scale = cfg.gradient_scale;
-    for (size_t i = 0; i < n * d; ++i) {
-      const float scaled = to_f32(g[i]) / scale;
-      if (!std::isfinite(scaled) || std::fabs(scaled) > dtype_max<G>() ||
-          std::fabs(scaled) > dtype_max<P>()) {
-        g_last_error = "gradient scale storage exceeds configured dtype";
-        return -3;
+    std::atomic<bool> bad{false};
+    parallel_for(n * d, cfg.threads, [&](size_t b, size_t e, int) {
+      for (size_t i = b; i < e; ++i) {
+        const float scaled = to_f32(g[i]) / scale;
+        if (!std::isfinite(scaled) || std::fabs(scaled) > dtype_max<G>() ||
+            std::fabs(scaled) > dtype_max<P>())
+          bad.store(true);
       }
+    });
+    if (bad.load()) {
+      g_last_error = "gradient scale storage exceeds configured dtype";
+      return -3;
     }
-    for (size_t i = 0; i < n; ++i) {
-      const uint64_t key = key_at(cfg.key_dtype, keys, i);
-      uint32_t slot;
-      if (!tmap.find(key, &slot)) {
-        slot = uint32_t(tkeys.size());
-        tmap.insert(key, slot);
-        tkeys.push_back(key);
-        tgrads.resize(tgrads.size() + d, from_f32<G>(0.0f));
+    const size_t ns = shards.size();
+    auto work = [&](size_t sh) {
+      Shard &S = shards[sh];
+      for (size_t i = 0; i < n; ++i) {
+        const uint64_t key = key_at(cfg.key_dtype, keys, i);
+        if (ns > 1 && splitmix64(key) % ns != sh) continue;
+        uint32_t slot;
+        if (!S.tmap.find(key, &slot)) {
+          slot = uint32_t(S.tkeys.size());
+          S.tmap.insert(key, slot);
+          S.tkeys.push_back(key);
+          S.trows.push_back(0);
+          S.tgrads.resize(S.tgrads.size() + d, from_f32<G>(0.0f));
+        }
+        S.trows[slot] += 1;
+        G *dst = S.tgrads.data() + size_t(slot) * d;
+        for (size_t j = 0; j < d; ++j) {
+          float src = scale == 1.0f ? to_f32(g[i * d + j])
+                                    : to_f32(from_f32<G>(to_f32(g[i * d + j]) / scale));
+          dst[j] = from_f32<G>(to_f32(dst[j]) + src);
+        }
       }
-      G *dst = tgrads.data() + size_t(slot) * d;
-      for (size_t j = 0; j < d; ++j) {
-        float src = scale == 1.0f ? to_f32(g[i * d + j])
-                                  : to_f32(from_f32<G>(to_f32(g[i * d + j]) / scale));
-        dst[j] = from_f32<G>(to_f32(dst[j]) + src);
-      }
+    };
+    if (ns == 1 || n < 4096) {
+      for (size_t sh = 0; sh < ns; ++sh) work(sh);
+    } else {
+      std::vector<std::thread> pool;
+      for (size_t sh = 0; sh < ns; ++sh) pool.emplace_back(work, sh);
+      for (auto &th : pool) th.join();
     }
     return 0;
   }
@@ -477,7 +501,8 @@ template <class P, class O, class G> struct Table final : TableBase {
   // GradientAccumulator::with_accumulated_batch (gradient_accumulator.hpp:130-152,
   // GradientBatchView::assign 38-53) -> SlotStore::update_batch (2799-2901) ->
   // AdamOptimizer::step (adam_optimizer.hpp:138-165) / SgdOptimizer::step
-  // (sgd_optimizer.hpp:72-78). A key absent at step time is dropped and counted.
+  // (sgd_optimizer.hpp:72-78). Gradients of a key absent at step time are
+  // dropped; the count is of dropped gradient rows.
   void optimizer_step(size_t nsteps, uint64_t *dropped, int threads) override {
     const size_t d = size_t(dim_);
     const bool raw = std::is_same_v<G, P> && nsteps == 1 && cfg.gradient_scale == 1.0f;
@@ -489,12 +514,12 @@ template <class P, class O, class G> struct Table final : TableBase {
       for (uint32_t s : steps) maxstep = s > maxstep ? s : maxstep;
       extend_bc(size_t(maxstep) + 2);
     }
-    parallel_for(tkeys.size(), threads, [&](size_t b, size_t e, int) {
+    auto work = [&](Shard &S) {
       std::vector<P> gbuf(d);
-      for (size_t s = b; s < e; ++s) {
+      for (size_t s = 0; s < S.tkeys.size(); ++s) {
         uint32_t row;
-        if (!map.find(tkeys[s], &row)) { drop.fetch_add(1); continue; }
-        const G *src = tgrads.data() + s * d;
+        if (!map.find(S.tkeys[s], &row)) { drop.fetch_add(S.trows[s]); continue; }
+        const G *src = S.tgrads.data() + s * d;
         for (size_t j = 0; j < d; ++j)
           gbuf[j] = raw ? from_f32<P>(to_f32(src[j])) : from_f32<P>(to_f32(src[j]) * factor);
         P *p = params.data() + size_t(row) * d;
@@ -516,11 +541,21 @@ template <class P, class O, class G> struct Table final : TableBase {
         default: break;
         }
       }
-    });
+    };
+    if (shards.size() == 1 || threads <= 1) {
+      for (auto &S : shards) work(S);
+    } else {
+      std::vector<std::thread> pool;
+      for (auto &S : shards) pool.emplace_back([&work, &S] { work(S); });
+      for (auto &th : pool) th.join();
+    }
     if (dropped) *dropped += drop.load();
-    tmap.clear();
-    tkeys.clear();
-    tgrads.clear();
+    for (auto &S : shards) {
+      S.tmap.clear();
+      S.tkeys.clear();
+      S.trows.clear();
+      S.tgrads.clear();
+    }
   }
 
   void extend_bc(size_t n) {

@@ -1,0 +1,100 @@
+// Shared device definitions of the B200 store: scalar types, hashes,
+// conversions and small helpers.
+//
+// Build with --fmad=false: products and sums are rounded separately unless a
+// kernel asks for a fused multiply-add with __fmaf_rn, so each formula's fused
+// steps are exactly the ones the reference's compiled CPU code performs.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace se_gpu {
+
+// ---------------------------------------------------------------------------
+// Value types. Each wraps a 16- or 32-bit storage type with float conversions
+// (round to nearest even on the way down, like the reference's
+// _mm512_cvtneps_pbh / _mm512_cvtps_ph stores, simd/intrinsics.hpp:37-60).
+// ---------------------------------------------------------------------------
+
+struct F32 {
+  using T = float;
+  static __device__ __forceinline__ float load(T x) { return x; }
+  static __device__ __forceinline__ T store(float f) { return f; }
+  static constexpr float kMax = 3.40282347e38f;
+};
+struct F16 {
+  using T = __half;
+  static __device__ __forceinline__ float load(T x) { return __half2float(x); }
+  static __device__ __forceinline__ T store(float f) { return __float2half_rn(f); }
+  static constexpr float kMax = 65504.0f;
+};
+struct BF16 {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float load(T x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ T store(float f) { return __float2bfloat16_rn(f); }
+  static constexpr float kMax = 3.38953139e38f;
+};
+
+// ---------------------------------------------------------------------------
+// Hashes
+// ---------------------------------------------------------------------------
+
+// SplitMix64 finalizer (hogwild_embedding_store.hpp:1272-1281; partitioner.hpp:226-234).
+__host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z ^= z >> 30;
+  z *= 0xbf58476d1ce4e5b9ull;
+  z ^= z >> 27;
+  z *= 0x94d049bb133111ebull;
+  z ^= z >> 31;
+  return z;
+}
+
+// Murmur3 fmix32 (partitioner.hpp:250-258; uniform_init_ops.hpp:119-124).
+__host__ __device__ __forceinline__ uint32_t fmix32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x85ebca6bu;
+  x ^= x >> 13;
+  x *= 0xc2b2ae35u;
+  x ^= x >> 16;
+  return x;
+}
+
+// Keys enter the store as uint64 with sign extension (hogwild_embedding_store.hpp:4449).
+__device__ __forceinline__ uint64_t key_u64(int32_t k) { return uint64_t(int64_t(k)); }
+__device__ __forceinline__ uint64_t key_u64(uint32_t k) { return uint64_t(k); }
+__device__ __forceinline__ uint64_t key_u64(int64_t k) { return uint64_t(k); }
+__device__ __forceinline__ uint64_t key_u64(uint64_t k) { return k; }
+
+// ---------------------------------------------------------------------------
+// Error reporting from kernels: bits OR-ed into a device status word that the
+// host reads after the launch. No kernel traps or asserts.
+// ---------------------------------------------------------------------------
+
+enum StatusBits : uint32_t {
+  kStatusTableFull = 1u,       // probe sequence or row arena exhausted
+  kStatusBadGradient = 2u,     // gradient fails validate_input
+  kStatusBadRow = 4u,          // row index outside the arena
+};
+
+__device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bits) {
+  atomicOr(status, bits);
+}
+
+// Loads that bypass L1 (directory words other blocks may be writing).
+__device__ __forceinline__ uint64_t ld_cg(const uint64_t *p) { return __ldcg(p); }
+__device__ __forceinline__ uint32_t ld_cg(const uint32_t *p) { return __ldcg(p); }
+
+template <int G>
+__device__ __forceinline__ unsigned group_mask() {
+  if constexpr (G == 32) {
+    return 0xffffffffu;
+  } else {
+    const unsigned lane = threadIdx.x & 31u;
+    return ((1u << G) - 1u) << (lane & ~unsigned(G - 1));
+  }
+}
+
+}  // namespace se_gpu

@@ -1,0 +1,1312 @@
+// B200 store: kernels for the forward gather, insert-on-miss, gradient
+// accumulation and the fused segment-reduce + optimizer step, and the host
+// object behind the C ABI in include/se_gpu.h.
+//
+// Per-key work is done by a group of LANES threads (4..32, a power of two):
+// every lane of the group probes the same 64-byte bucket (one line, broadcast
+// within the group), then the lanes split the row in 16-byte (VEC = 4
+// elements) or element-wide chunks.
+
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_select.cuh>
+#include <thrust/iterator/counting_iterator.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "se_common.cuh"
+#include "se_host.hpp"
+#include "se_store_kernels.cuh"
+
+namespace se_gpu {
+
+// ===========================================================================
+// Kernels
+// ===========================================================================
+
+template <class V> __device__ __forceinline__ V zero_unit();
+template <> __device__ __forceinline__ uint4 zero_unit<uint4>() { return make_uint4(0, 0, 0, 0); }
+template <> __device__ __forceinline__ uint2 zero_unit<uint2>() { return make_uint2(0, 0); }
+template <> __device__ __forceinline__ uint32_t zero_unit<uint32_t>() { return 0u; }
+template <> __device__ __forceinline__ uint16_t zero_unit<uint16_t>() { return 0; }
+
+// forward_lookup (hogwild_embedding_store.hpp:4406-4534): probe, copy the
+// param section of the row (simd_copy, memory_ops.hpp:31-35), zero on miss
+// (4501-4503). Row copied in units V (16, 4 or 2 bytes).
+template <int LANES, class V>
+__global__ void __launch_bounds__(256)
+k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row_units,
+         const void *__restrict__ keys, int kdt, size_t n, V *__restrict__ out) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t i = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (i >= n) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  V *dst = out + i * row_units;
+  if (row != kNoRow) {
+    const V *src = reinterpret_cast<const V *>(slabs + size_t(row) * stride);
+    for (uint32_t u = lane; u < row_units; u += LANES) dst[u] = src[u];
+  } else {
+    for (uint32_t u = lane; u < row_units; u += LANES) dst[u] = zero_unit<V>();
+  }
+}
+
+// Copies VEC elements (raw bits) of dtype dt. Source loads go to L2 (ld.cg):
+// in the insert kernel a row may have been initialised by another SM during
+// the same launch, so no L1 line may be trusted.
+template <int VEC>
+__device__ __forceinline__ void copy_elems(void *dst, const void *src, int dt, size_t e) {
+  if (dt == SE_FLOAT32) {
+    if constexpr (VEC == 4)
+      reinterpret_cast<uint4 *>(static_cast<float *>(dst) + e)[0] =
+          __ldcg(reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + e));
+    else
+      static_cast<uint32_t *>(dst)[e] = __ldcg(static_cast<const uint32_t *>(src) + e);
+  } else {
+    if constexpr (VEC == 4)
+      reinterpret_cast<uint2 *>(static_cast<uint16_t *>(dst) + e)[0] =
+          __ldcg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(src) + e));
+    else
+      static_cast<uint16_t *>(dst)[e] = __ldcg(static_cast<const unsigned short *>(src) + e);
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void zero_elems(void *dst, int dt, size_t e) {
+  float z[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) z[j] = 0.0f;
+  stv<VEC>(dst, dt, e, z);
+}
+
+// Initialises a freshly claimed slab: param from the initializer (also written
+// to `out_row`), optimizer state from InitSpec, Adam step = 0.
+template <int LANES, int VEC>
+__device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const InitSpec &init,
+                                          uint64_t key, uint32_t lane, void *out_row) {
+  const uint32_t seed = uint32_t(key ^ (key >> 32));
+  for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+    float v[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j)
+      v[j] = init.kind == SE_INIT_UNIFORM ? uniform_value(seed, e + j, init.lo, init.diff) : 0.0f;
+    stv<VEC>(slab, L.pdt, e, v);
+    stv<VEC>(out_row, L.pdt, e, v);
+    if (L.nstate >= 1) {
+      float s[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s[j] = init.state0;
+      stv<VEC>(slab + L.state0, L.odt, e, s);
+    }
+    if (L.nstate >= 2) {
+      float s[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s[j] = 0.0f;
+      stv<VEC>(slab + L.state1, L.odt, e, s);
+    }
+  }
+  if (L.nstate >= 2 && lane == 0) *reinterpret_cast<uint32_t *>(slab + L.step) = 0u;
+}
+
+// lookup_or_insert (hogwild_embedding_store.hpp:4925-4980 ->
+// SlotStore::find_or_insert_batch 3057-3353). One claimant per absent key
+// initialises and publishes its row; other positions of the same key found
+// the claim before the row was published and are finished by k_deferred.
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row,
+                   uint64_t capacity, InitSpec init, const void *__restrict__ keys, int kdt,
+                   size_t n, void *__restrict__ out, uint32_t *def_count, uint32_t *def_pos,
+                   unsigned long long *def_word, uint32_t *status) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t i = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (i >= n) return;
+  const unsigned mask = group_mask<LANES>();
+  const uint64_t key = load_key(keys, kdt, i);
+  int kind = kFound;
+  uint32_t row = kNoRow;
+  uint32_t *word = nullptr;
+  if (lane == 0) {
+    const InsertResult r = dir_find_or_insert(d, key);
+    kind = r.kind;
+    word = r.row_word;
+    if (kind == kInserted) {
+      row = atomicAdd(next_row, 1u);
+      if (row >= capacity) {
+        raise_status(status, kStatusTableFull);
+        kind = kFull;
+      }
+    } else if (kind == kFound) {
+      row = __ldcg(word);
+      if (row == kNoRow) kind = 3;  // claimed in this launch, row not yet published
+    } else {
+      raise_status(status, kStatusTableFull);
+    }
+  }
+  kind = __shfl_sync(mask, kind, 0, LANES);
+  row = __shfl_sync(mask, row, 0, LANES);
+  void *out_row = static_cast<uint8_t *>(out) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
+  if (kind == kFound) {
+    const uint8_t *slab = slabs + size_t(row) * L.stride;
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+  } else if (kind == kInserted) {
+    uint8_t *slab = slabs + size_t(row) * L.stride;
+    init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
+    __threadfence();  // every lane's slab writes are visible device-wide ...
+    __syncwarp(mask);
+    if (lane == 0) atomicExch(word, row);  // ... before the row is published
+  } else if (kind == 3) {
+    if (lane == 0) {
+      const uint32_t j = atomicAdd(def_count, 1u);
+      def_pos[j] = uint32_t(i);
+      def_word[j] = reinterpret_cast<unsigned long long>(word);
+    }
+  } else {
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
+  }
+}
+
+// Positions whose key was claimed by another group in the same launch.
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_count,
+           const uint32_t *def_pos, const unsigned long long *def_word, void *__restrict__ out,
+           uint32_t *status) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  const uint32_t count = *def_count;
+  for (size_t j = t / LANES; j < count; j += groups) {
+    const size_t i = def_pos[j];
+    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
+    void *out_row = static_cast<uint8_t *>(out) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
+    if (row == kNoRow) {
+      if (lane == 0) raise_status(status, kStatusTableFull);
+      for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
+      continue;
+    }
+    const uint8_t *slab = slabs + size_t(row) * L.stride;
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+  }
+}
+
+// accumulate_gradients, append phase: GradientAccumulator::validate_input
+// (gradient_accumulator.hpp:88-104) and the entry scaling of accumulate_hashed
+// (106-128): scaled = g / gradient_scale must be finite and within both the
+// gradient and the parameter dtype; the stored row is g (scale 1) or the
+// scaled value rounded to the gradient dtype.
+template <int VEC>
+__global__ void __launch_bounds__(256)
+k_accumulate(const void *__restrict__ keys, int kdt, size_t n, const void *__restrict__ grads,
+             int gdt, uint32_t dim, float scale, float maxv, unsigned long long *__restrict__ pkeys,
+             void *__restrict__ pgrads, uint32_t *status) {
+  const size_t stride = size_t(gridDim.x) * blockDim.x;
+  const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (size_t i = tid; i < n; i += stride) pkeys[i] = load_key(keys, kdt, i);
+  const size_t chunks = n * dim / VEC;
+  bool bad = false;
+  for (size_t c = tid; c < chunks; c += stride) {
+    const size_t e = c * VEC;
+    float g[VEC];
+    ldv<VEC>(grads, gdt, e, g);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float s = __fdiv_rn(g[j], scale);
+      bad |= !(fabsf(s) <= maxv);
+      if (scale != 1.0f) g[j] = s;
+    }
+    stv<VEC>(pgrads, gdt, e, g);
+  }
+  if (bad) raise_status(status, kStatusBadGradient);
+}
+
+// optimizer_step, phase 1: the row of every pending gradient (sentinel when
+// the key is absent) and its arrival position, as radix-sort input.
+// Gradient rows whose key is absent are counted in `dropped`.
+__global__ void __launch_bounds__(256)
+k_step_probe(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t count, uint32_t sentinel,
+             uint32_t *__restrict__ rows, uint32_t *__restrict__ pos, unsigned long long *dropped) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  bool absent = false;
+  if (i < count) {
+    const uint32_t r = dir_find<false>(d, pkeys[i]);
+    absent = r == kNoRow;
+    rows[i] = absent ? sentinel : r;
+    pos[i] = i;
+  }
+  const unsigned ballot = __ballot_sync(0xffffffffu, absent);
+  if ((threadIdx.x & 31) == 0 && ballot) atomicAdd(dropped, (unsigned long long)__popc(ballot));
+}
+
+struct IsSegmentHead {
+  const uint32_t *rows;
+  __device__ __forceinline__ bool operator()(const uint32_t &j) const {
+    return j == 0 || rows[j] != rows[j - 1];
+  }
+};
+
+struct OptSpec {
+  int kind;
+  float lr, b1, b2, eps, wd, omb1, omb2;
+  uint32_t simd_cut;   // elements below use the reference's vector formulas
+  const float *bc;     // Adam bias corrections: bc[2t], bc[2t+1]
+  float factor;        // gradient_scale / normalization_steps
+  int raw;             // gradient used as stored (GradT == ParamT, factor 1)
+};
+
+// Applies the optimizer to VEC elements [e, e+VEC) of one row, given the
+// reduced gradient in the gradient dtype's precision.
+//   SGD:     simd_sgd_update (sgd_ops.hpp:30-78): g = fma(wd, p, g); p = fma(-lr, g, p).
+//   Adam:    simd_adam_update (adam_ops.hpp:30-232), vector body below
+//            simd_cut, compiled scalar tail above it.
+//   Adagrad: no reference counterpart; acc = fma(g, g, acc),
+//            p = fma(-lr, g / (sqrt(acc) + eps), p).
+template <int VEC>
+__device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, const OptSpec &o,
+                                            uint32_t t, uint32_t e, const float (&gsum)[VEC]) {
+  float g[VEC], p[VEC];
+  // GradientBatchView::assign (gradient_accumulator.hpp:38-53): g * scale / N -> ParamT.
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) g[j] = o.raw ? gsum[j] : round_to(L.pdt, __fmul_rn(gsum[j], o.factor));
+  ldv<VEC>(slab, L.pdt, e, p);
+  if (o.kind == SE_OPT_SGD) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float gg = __fmaf_rn(o.wd, p[j], g[j]);
+      p[j] = __fmaf_rn(-o.lr, gg, p[j]);
+    }
+  } else if (o.kind == SE_OPT_ADAGRAD) {
+    float a[VEC];
+    ldv<VEC>(slab + L.state0, L.odt, e, a);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      float gg = g[j];
+      if (o.wd > 0.0f) gg = __fmaf_rn(o.wd, p[j], gg);
+      a[j] = __fmaf_rn(gg, gg, a[j]);
+      const float denom = __fadd_rn(__fsqrt_rn(a[j]), o.eps);
+      p[j] = __fmaf_rn(-o.lr, __fdiv_rn(gg, denom), p[j]);
+    }
+    stv<VEC>(slab + L.state0, L.odt, e, a);
+  } else if (o.kind == SE_OPT_ADAM) {
+    float m[VEC], v[VEC], ms[VEC], vs[VEC];
+    ldv<VEC>(slab + L.state0, L.odt, e, m);
+    ldv<VEC>(slab + L.state1, L.odt, e, v);
+    const float bc1 = o.bc[2 * t], bc2 = o.bc[2 * t + 1];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      float gg = g[j];
+      if (o.wd > 0.0f) gg = __fmaf_rn(o.wd, p[j], gg);
+      const bool vec_body = e + j < o.simd_cut;
+      const float mi = __fmaf_rn(o.b1, m[j], __fmul_rn(o.omb1, gg));
+      const float addv = vec_body ? __fmul_rn(o.omb2, __fmul_rn(gg, gg))
+                                  : __fmul_rn(__fmul_rn(o.omb2, gg), gg);
+      const float vi = __fmaf_rn(o.b2, v[j], addv);
+      ms[j] = mi;
+      vs[j] = vi;
+      const float m_hat = __fmul_rn(mi, bc1);
+      const float v_hat = __fmul_rn(vi, bc2);
+      const float denom = __fadd_rn(__fsqrt_rn(v_hat), o.eps);
+      if (vec_body) p[j] = __fmaf_rn(-o.lr, __fdiv_rn(m_hat, denom), p[j]);
+      else p[j] = __fsub_rn(p[j], __fdiv_rn(__fmul_rn(o.lr, m_hat), denom));
+    }
+    stv<VEC>(slab + L.state0, L.odt, e, ms);
+    stv<VEC>(slab + L.state1, L.odt, e, vs);
+  }
+  stv<VEC>(slab, L.pdt, e, p);
+}
+
+// Adds the gradient rows spos[k0..k1) (in order) into acc, rounding to the
+// gradient dtype after each add like TransientArena's simd_accumulate
+// (memory_ops.hpp:37-70). Loads run four rows ahead of the adds.
+template <int VEC>
+__device__ __forceinline__ void sum_rows(const void *pgrads, int gdt, uint32_t dim, const uint32_t *spos,
+                                         uint32_t k0, uint32_t k1, uint32_t e, float (&acc)[VEC]) {
+  uint32_t k = k0;
+  for (; k + 4 <= k1; k += 4) {
+    float g0[VEC], g1[VEC], g2[VEC], g3[VEC];
+    ldv<VEC>(pgrads, gdt, size_t(spos[k]) * dim + e, g0);
+    ldv<VEC>(pgrads, gdt, size_t(spos[k + 1]) * dim + e, g1);
+    ldv<VEC>(pgrads, gdt, size_t(spos[k + 2]) * dim + e, g2);
+    ldv<VEC>(pgrads, gdt, size_t(spos[k + 3]) * dim + e, g3);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
+      acc[j] = round_to(gdt, __fadd_rn(acc[j], g1[j]));
+      acc[j] = round_to(gdt, __fadd_rn(acc[j], g2[j]));
+      acc[j] = round_to(gdt, __fadd_rn(acc[j], g3[j]));
+    }
+  }
+  for (; k < k1; ++k) {
+    float g0[VEC];
+    ldv<VEC>(pgrads, gdt, size_t(spos[k]) * dim + e, g0);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
+  }
+}
+
+__device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
+  uint32_t *sp = reinterpret_cast<uint32_t *>(slab + L.step);
+  const uint32_t t = *sp + 1u;
+  *sp = t;
+  return t;
+}
+
+// optimizer_step, phase 3: one group per key (segment of the sorted pending
+// gradients). Short segments are reduced serially in arrival order, exactly
+// as the reference sums them; segments longer than long_threshold go to
+// k_apply_long. Absent keys are dropped and counted
+// (hogwild_embedding_store.hpp:1942-1952).
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
+        const uint32_t *__restrict__ srows, const uint32_t *__restrict__ spos,
+        const uint32_t *__restrict__ seg_starts, const uint32_t *num_segs_p, uint32_t count,
+        uint32_t sentinel, uint32_t long_threshold, uint32_t *long_list, uint32_t *long_count) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  const unsigned mask = group_mask<LANES>();
+  const uint32_t nseg = *num_segs_p;
+  for (size_t s = t / LANES; s < nseg; s += groups) {
+    const uint32_t k0 = seg_starts[s];
+    const uint32_t k1 = s + 1 < nseg ? seg_starts[s + 1] : count;
+    const uint32_t row = srows[k0];
+    if (row == sentinel) continue;  // absent keys: counted by k_step_probe
+    if (k1 - k0 > long_threshold) {
+      if (lane == 0) long_list[atomicAdd(long_count, 1u)] = uint32_t(s);
+      continue;
+    }
+    uint8_t *slab = slabs + size_t(row) * L.stride;
+    uint32_t step = 0;
+    if (o.kind == SE_OPT_ADAM) {
+      if (lane == 0) step = next_step(L, slab);
+      step = __shfl_sync(mask, step, 0, LANES);
+    }
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+      float acc[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
+      sum_rows<VEC>(pgrads, gdt, L.dim, spos, k0, k1, e, acc);
+      apply_chunk<VEC>(L, slab, o, step, e, acc);
+    }
+  }
+}
+
+// Long segments (hot keys): one 1024-thread block per key. Its 1024/LANES
+// groups each reduce a contiguous run of the segment in order; group 0 then
+// adds the partial sums in run order and applies the optimizer. The order is
+// fixed by the launch shape, so results are deterministic.
+constexpr int kLongThreads = 1024;
+
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(kLongThreads)
+k_apply_long(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
+             const uint32_t *__restrict__ srows, const uint32_t *__restrict__ spos,
+             const uint32_t *__restrict__ seg_starts, const uint32_t *num_segs_p, uint32_t count,
+             const uint32_t *long_list, const uint32_t *long_count) {
+  constexpr int NG = kLongThreads / LANES;
+  __shared__ float part[NG][LANES][VEC];
+  __shared__ uint32_t step_s;
+  const uint32_t lane = threadIdx.x % LANES;
+  const uint32_t grp = threadIdx.x / LANES;
+  const uint32_t nseg = *num_segs_p;
+  const uint32_t nlong = *long_count;
+  for (uint32_t x = blockIdx.x; x < nlong; x += gridDim.x) {
+    const uint32_t s = long_list[x];
+    const uint32_t k0 = seg_starts[s];
+    const uint32_t k1 = s + 1 < nseg ? seg_starts[s + 1] : count;
+    const uint32_t row = srows[k0];
+    uint8_t *slab = slabs + size_t(row) * L.stride;
+    if (threadIdx.x == 0) step_s = o.kind == SE_OPT_ADAM ? next_step(L, slab) : 0u;
+    const uint32_t len = k1 - k0;
+    const uint32_t per = (len + NG - 1) / NG;
+    const uint32_t r0 = min(k0 + grp * per, k1), r1 = min(r0 + per, k1);
+    __syncthreads();
+    const uint32_t step = step_s;
+    for (uint32_t base = 0; base < L.dim; base += LANES * VEC) {
+      const uint32_t e = base + lane * VEC;
+      const bool valid = e < L.dim;
+      float acc[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
+      if (valid) sum_rows<VEC>(pgrads, gdt, L.dim, spos, r0, r1, e, acc);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) part[grp][lane][j] = acc[j];
+      __syncthreads();
+      if (grp == 0 && valid) {
+        float tot[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) tot[j] = 0.0f;
+        for (int q = 0; q < NG; ++q)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) tot[j] = round_to(gdt, __fadd_rn(tot[j], part[q][lane][j]));
+        apply_chunk<VEC>(L, slab, o, step, e, tot);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Rebuild into a larger directory.
+__global__ void k_rehash(const Bucket *__restrict__ old_b, uint64_t old_n, Dir nd, uint32_t *status) {
+  const uint64_t slot = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (slot >= old_n * kBucketSlots) return;
+  const Bucket &b = old_b[slot / kBucketSlots];
+  const int s = int(slot % kBucketSlots);
+  const uint64_t key = b.keys[s];
+  if (key == kEmptyKey) return;
+  if (!dir_insert_unique(nd, key, b.rows[s])) raise_status(status, kStatusTableFull);
+}
+
+// Reads the rows of a few keys (state inspection for tests).
+__global__ void k_find_rows(Dir d, const unsigned long long *keys, uint32_t n, uint32_t *rows) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) rows[i] = dir_find<true>(d, keys[i]);
+}
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+constexpr uint64_t kDefaultCapacity = 1u << 16;
+constexpr double kMaxLoadPerBucket = 3.5;  // 70 % of 5 slots
+constexpr uint32_t kLongThreshold = 64;
+
+uint64_t next_pow2(uint64_t x) {
+  uint64_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+uint32_t pick_lanes(uint64_t units) {
+  uint32_t l = 4;
+  while (l < 32 && l < units) l <<= 1;
+  return l;
+}
+
+float host_dtype_max(int dt) {
+  if (dt == SE_FLOAT16) return 65504.0f;
+  if (dt == SE_FLOAT32) return 3.40282347e38f;
+  return 3.38953139e38f;
+}
+
+template <class T> T *dalloc(size_t count) {
+  void *p = nullptr;
+  if (count == 0) count = 1;
+  cuda_check(cudaMalloc(&p, count * sizeof(T)), "cudaMalloc");
+  return static_cast<T *>(p);
+}
+
+void dfree(void *p) {
+  if (p) cudaFree(p);
+}
+
+// Device buffer that only grows; contents are not preserved.
+template <class T> struct Scratch {
+  T *ptr = nullptr;
+  size_t cap = 0;
+  T *get(size_t n) {
+    if (n > cap) {
+      dfree(ptr);
+      ptr = nullptr;
+      cap = std::max(n, cap * 2);
+      ptr = dalloc<T>(cap);
+    }
+    return ptr;
+  }
+  ~Scratch() { dfree(ptr); }
+};
+
+// Counters of a table, one device block.
+enum Ctr : int {
+  kCtrNextRow = 0,
+  kCtrSpecialClaim = 1,
+  kCtrSpecialRow = 2,
+  kCtrDeferred = 3,
+  kCtrLong = 4,
+  kCtrSegments = 5,
+  kCtrStatus = 6,      // insert / directory errors
+  kCtrGradStatus = 7,  // gradient validation of the current accumulate call
+  kCtrDropped = 8,     // u64 at words 8-9
+  kCtrWords = 16,
+};
+
+struct Table {
+  int64_t dim = 0;
+  Layout L{};
+  int vec = 1;
+  uint32_t lanes = 4;
+  // directory
+  Bucket *buckets = nullptr;
+  uint64_t nbuckets = 0;
+  // arena
+  uint8_t *slabs = nullptr;
+  uint64_t capacity = 0;
+  uint64_t rows_bound = 0;  // upper bound of rows in use
+  uint32_t *ctr = nullptr;
+  // pending gradients
+  unsigned long long *pkeys = nullptr;
+  uint8_t *pgrads = nullptr;
+  uint64_t pcap = 0, pcount = 0;
+  // step and insert work buffers
+  Scratch<uint32_t> rows_a, pos_a, rows_b, pos_b, seg_starts, long_list, def_pos;
+  Scratch<unsigned long long> def_word;
+  Scratch<uint8_t> cub_tmp;
+
+  Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
+  ~Table() {
+    dfree(buckets);
+    dfree(slabs);
+    dfree(ctr);
+    dfree(pkeys);
+    dfree(pgrads);
+  }
+};
+
+struct ProfRec {
+  std::string name;
+  cudaEvent_t a, b;
+};
+
+}  // namespace
+
+struct StoreImpl {
+  se_store_config cfg{};
+  std::vector<int64_t> dims;
+  int device = 0;
+  cudaStream_t own = nullptr;
+  std::mutex mu;
+  std::vector<std::unique_ptr<Table>> tables;
+  float *bc = nullptr;  // Adam bias corrections, 2 floats per step
+  uint64_t bc_steps = 0;
+  uint64_t steps_taken = 0;
+  uint32_t *status_host = nullptr;  // pinned
+  uint64_t *u64_host = nullptr;     // pinned
+  Scratch<uint8_t> stage_keys, stage_vals;
+  bool profiling = false;
+  std::vector<ProfRec> prof;
+  std::vector<cudaEvent_t> event_pool;
+
+  ~StoreImpl() {
+    if (own) cudaStreamSynchronize(own);
+    tables.clear();
+    dfree(bc);
+    if (status_host) cudaFreeHost(status_host);
+    if (u64_host) cudaFreeHost(u64_host);
+    for (auto &r : prof) {
+      cudaEventDestroy(r.a);
+      cudaEventDestroy(r.b);
+    }
+    for (auto e : event_pool) cudaEventDestroy(e);
+    if (own) cudaStreamDestroy(own);
+  }
+
+  // NULL is the legacy default stream, as everywhere in CUDA.
+  static cudaStream_t pick(void *s) { return static_cast<cudaStream_t>(s); }
+
+  Table &table(int64_t dim) {
+    for (auto &t : tables)
+      if (t->dim == dim) return *t;
+    throw Error(SE_ERR_RUNTIME, "invalid dim access: no physical table for dim " + std::to_string(dim));
+  }
+
+  // ---- profiling ------------------------------------------------------------
+  cudaEvent_t take_event() {
+    if (event_pool.empty()) {
+      cudaEvent_t e;
+      cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+      return e;
+    }
+    cudaEvent_t e = event_pool.back();
+    event_pool.pop_back();
+    return e;
+  }
+  struct Prof {
+    StoreImpl *s;
+    cudaStream_t st;
+    ProfRec rec{};
+    Prof(StoreImpl *store, const char *name, cudaStream_t stream) : s(store), st(stream) {
+      if (!s->profiling) return;
+      rec.name = name;
+      rec.a = s->take_event();
+      rec.b = s->take_event();
+      cudaEventRecord(rec.a, st);
+    }
+    ~Prof() {
+      if (!s->profiling) return;
+      cudaEventRecord(rec.b, st);
+      s->prof.push_back(rec);
+    }
+  };
+
+  // ---- table construction and growth ---------------------------------------
+  void init_table(Table &t, int64_t dim, uint64_t cap) {
+    const int pdt = cfg.value_dtype, odt = cfg.optimizer_dtype;
+    const uint32_t pb = uint32_t(dim) * uint32_t(value_bytes(pdt));
+    const uint32_t ob = uint32_t(dim) * uint32_t(value_bytes(odt));
+    auto up16 = [](uint32_t x) { return (x + 15u) & ~15u; };
+    uint32_t nstate = 0;
+    if (cfg.enable_optimizer && cfg.optimizer_kind == SE_OPT_ADAGRAD) nstate = 1;
+    if (cfg.enable_optimizer && cfg.optimizer_kind == SE_OPT_ADAM) nstate = 2;
+    t.dim = dim;
+    t.L.dim = uint32_t(dim);
+    t.L.pdt = pdt;
+    t.L.odt = odt;
+    t.L.nstate = nstate;
+    t.L.state0 = up16(pb);
+    t.L.state1 = t.L.state0 + (nstate >= 1 ? up16(ob) : 0u);
+    t.L.step = t.L.state1 + (nstate >= 2 ? up16(ob) : 0u);
+    t.L.stride = t.L.step + (nstate >= 2 ? 16u : 0u);
+    t.vec = dim % 4 == 0 ? 4 : 1;
+    t.lanes = pick_lanes(uint64_t(dim) / uint64_t(t.vec));
+    t.ctr = dalloc<uint32_t>(kCtrWords);
+    cuda_check(cudaMemset(t.ctr, 0, kCtrWords * 4), "memset counters");
+    cuda_check(cudaMemset(t.ctr + kCtrSpecialRow, 0xff, 4), "memset special");
+    t.capacity = std::max<uint64_t>(cap, 64);
+    t.slabs = dalloc<uint8_t>(size_t(t.capacity) * t.L.stride);
+    t.nbuckets = next_pow2(uint64_t(double(t.capacity) / kMaxLoadPerBucket) + 1);
+    t.buckets = dalloc<Bucket>(t.nbuckets);
+    cuda_check(cudaMemset(t.buckets, 0xff, t.nbuckets * sizeof(Bucket)), "memset directory");
+  }
+
+  uint64_t read_rows_used(Table &t, cudaStream_t st) {
+    cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrNextRow, 4, cudaMemcpyDeviceToHost, st), "read rows");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    const uint64_t used = status_host[0];
+    check_status(t, st);
+    return used;
+  }
+
+  // Guarantees room for `extra` more rows in the arena and the directory.
+  void ensure_rows(Table &t, uint64_t extra, cudaStream_t st) {
+    uint64_t need = t.rows_bound + extra;
+    const auto dir_limit = [&](uint64_t nb) { return uint64_t(double(nb) * kMaxLoadPerBucket); };
+    if (need > t.capacity || need > dir_limit(t.nbuckets)) {
+      t.rows_bound = read_rows_used(t, st);
+      need = t.rows_bound + extra;
+      if (need > 0xfffffff0ull) throw Error(SE_ERR_TABLE_FULL, "table exceeds 2^32 rows");
+      if (need > t.capacity) {
+        const uint64_t ncap = std::max<uint64_t>(need, t.capacity * 2);
+        uint8_t *ns = dalloc<uint8_t>(size_t(ncap) * t.L.stride);
+        cuda_check(cudaMemcpyAsync(ns, t.slabs, size_t(t.rows_bound) * t.L.stride,
+                                   cudaMemcpyDeviceToDevice, st), "grow arena");
+        cuda_check(cudaStreamSynchronize(st), "sync");
+        dfree(t.slabs);
+        t.slabs = ns;
+        t.capacity = ncap;
+      }
+      if (need > dir_limit(t.nbuckets)) {
+        uint64_t nb = t.nbuckets;
+        while (dir_limit(nb) < std::max(need, t.capacity)) nb *= 2;
+        Bucket *nbk = dalloc<Bucket>(nb);
+        cuda_check(cudaMemsetAsync(nbk, 0xff, nb * sizeof(Bucket), st), "memset directory");
+        Dir nd{nbk, nb, t.ctr + kCtrSpecialClaim};
+        const uint64_t slots = t.nbuckets * kBucketSlots;
+        k_rehash<<<grid_for(slots, 256, 0x7fffffffu), 256, 0, st>>>(t.buckets, t.nbuckets, nd,
+                                                                   t.ctr + kCtrStatus);
+        launched("k_rehash");
+        cuda_check(cudaStreamSynchronize(st), "sync");
+        dfree(t.buckets);
+        t.buckets = nbk;
+        t.nbuckets = nb;
+      }
+    }
+    t.rows_bound = need;
+  }
+
+  void ensure_pending(Table &t, uint64_t extra, cudaStream_t st) {
+    const uint64_t need = t.pcount + extra;
+    if (need <= t.pcap) return;
+    if (need > 0xffffffffull) throw Error(SE_ERR_RUNTIME, "more than 2^32 pending gradient rows");
+    const uint64_t ncap = std::max<uint64_t>(need, std::max<uint64_t>(t.pcap * 2, 1024));
+    const size_t gb = size_t(t.dim) * value_bytes(cfg.gradient_dtype);
+    auto *nk = dalloc<unsigned long long>(ncap);
+    auto *ng = dalloc<uint8_t>(size_t(ncap) * gb);
+    if (t.pcount) {
+      cuda_check(cudaMemcpyAsync(nk, t.pkeys, t.pcount * 8, cudaMemcpyDeviceToDevice, st), "grow pending");
+      cuda_check(cudaMemcpyAsync(ng, t.pgrads, size_t(t.pcount) * gb, cudaMemcpyDeviceToDevice, st),
+                 "grow pending");
+    }
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    dfree(t.pkeys);
+    dfree(t.pgrads);
+    t.pkeys = nk;
+    t.pgrads = ng;
+    t.pcap = ncap;
+  }
+
+  void ensure_bc(uint64_t steps) {
+    if (steps < bc_steps) return;
+    uint64_t n = std::max<uint64_t>(4096, bc_steps * 2);
+    while (n <= steps) n *= 2;
+    std::vector<float> h(2 * n);
+    h[0] = 1.0f;
+    h[1] = 1.0f;
+    // AdamOptimizer bias-correction table (adam_optimizer.hpp:55-61, and the
+    // same formula past the table, 144-148): std::pow(float, float) is powf.
+    for (uint64_t s = 1; s < n; ++s) {
+      const float sf = float(s);
+      h[2 * s] = 1.0f / (1.0f - std::pow(cfg.beta1, sf));
+      h[2 * s + 1] = 1.0f / (1.0f - std::pow(cfg.beta2, sf));
+    }
+    float *nb = dalloc<float>(2 * n);
+    cuda_check(cudaMemcpy(nb, h.data(), h.size() * 4, cudaMemcpyHostToDevice), "upload bc");
+    dfree(bc);
+    bc = nb;
+    bc_steps = n;
+  }
+
+  // ---- host/device staging ----------------------------------------------------
+  const void *stage_in(Scratch<uint8_t> &buf, const void *p, size_t bytes, cudaStream_t st) {
+    if (bytes == 0 || is_device_ptr(p)) return p;
+    uint8_t *d = buf.get(bytes);
+    cuda_check(cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, st), "stage H2D");
+    return d;
+  }
+
+  // ---- operations ----------------------------------------------------------
+  void lookup(const void *keys, size_t n, int64_t dim, void *out, void *sp, bool insert) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("dim must be > 0");
+    Table &t = table(dim);
+    if (n == 0) return;
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    const size_t vb = value_bytes(cfg.value_dtype);
+    const size_t out_bytes = n * size_t(dim) * vb;
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const bool host_out = !is_device_ptr(out);
+    void *dout = host_out ? stage_vals.get(out_bytes) : out;
+    if (!insert) {
+      const size_t row_bytes = size_t(dim) * vb;
+      const uintptr_t al = uintptr_t(dout) | uintptr_t(row_bytes);
+      const Dir d = t.dir();
+      auto go = [&](auto lanes_tag, auto vtag) {
+        constexpr int LN = decltype(lanes_tag)::value;
+        using V = decltype(vtag);
+        const uint32_t units = uint32_t(row_bytes / sizeof(V));
+        Prof pr(this, "k_lookup", st);
+        k_lookup<LN, V><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+            d, t.slabs, t.L.stride, units, dkeys, cfg.key_dtype, n, static_cast<V *>(dout));
+        launched("k_lookup");
+      };
+      auto by_lanes = [&](auto vtag) {
+        using V = decltype(vtag);
+        const uint32_t ln = pick_lanes(row_bytes / sizeof(V));
+        switch (ln) {
+        case 4: go(std::integral_constant<int, 4>{}, vtag); break;
+        case 8: go(std::integral_constant<int, 8>{}, vtag); break;
+        case 16: go(std::integral_constant<int, 16>{}, vtag); break;
+        default: go(std::integral_constant<int, 32>{}, vtag); break;
+        }
+      };
+      if (al % 16 == 0) by_lanes(uint4{});
+      else if (al % 4 == 0) by_lanes(uint32_t{});
+      else by_lanes(uint16_t{});
+    } else {
+      ensure_rows(t, n, st);
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
+      uint32_t *dpos = t.def_pos.get(n);
+      unsigned long long *dword = t.def_word.get(n);
+      InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
+                    cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
+      const bool vec4 = t.vec == 4 && (uintptr_t(dout) % 16 == 0);
+      auto go = [&](auto lanes_tag, auto vec_tag) {
+        constexpr int LN = decltype(lanes_tag)::value;
+        constexpr int VC = decltype(vec_tag)::value;
+        {
+          Prof pr(this, "k_lookup_or_insert", st);
+          k_lookup_or_insert<LN, VC><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+              t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity, init, dkeys, cfg.key_dtype, n,
+              dout, t.ctr + kCtrDeferred, dpos, dword, t.ctr + kCtrStatus);
+          launched("k_lookup_or_insert");
+        }
+        Prof pr(this, "k_deferred", st);
+        k_deferred<LN, VC><<<grid_for(n * LN, 256, 148 * 4), 256, 0, st>>>(
+            t.L, t.slabs, t.ctr + kCtrDeferred, dpos, dword, dout, t.ctr + kCtrStatus);
+        launched("k_deferred");
+      };
+      auto by_lanes = [&](auto vec_tag) {
+        const uint32_t ln = vec4 ? t.lanes : pick_lanes(uint64_t(dim));
+        switch (ln) {
+        case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+        case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+        case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+        default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+        }
+      };
+      if (vec4) by_lanes(std::integral_constant<int, 4>{});
+      else by_lanes(std::integral_constant<int, 1>{});
+    }
+    if (host_out) {
+      cuda_check(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, st), "copy out");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+      if (insert) check_status(t, st);
+    }
+  }
+
+  // Reads and clears the table's insert status word and raises on
+  // kernel-reported errors. Calls with device outputs do not wait for their
+  // kernels; their errors surface at the next synchronising call.
+  void check_status(Table &t, cudaStream_t st) {
+    cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrStatus, 4, cudaMemcpyDeviceToHost, st), "status");
+    cuda_check(cudaMemsetAsync(t.ctr + kCtrStatus, 0, 4, st), "status clear");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    const uint32_t s = status_host[0];
+    if (s & kStatusTableFull) throw Error(SE_ERR_TABLE_FULL, "embedding table is full");
+    if (s & kStatusBadRow) throw Error(SE_ERR_RUNTIME, "row index outside the arena");
+  }
+
+  void accumulate(const void *keys, size_t n, int64_t dim, const void *grads, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("gradient row length must be positive");
+    Table &t = table(dim);
+    if (n == 0) return;
+    cudaStream_t st = pick(sp);
+    ensure_pending(t, n, st);
+    const size_t gb = value_bytes(cfg.gradient_dtype);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const void *dgrads = stage_in(stage_vals, grads, n * size_t(dim) * gb, st);
+    const float maxv = std::min(host_dtype_max(cfg.gradient_dtype), host_dtype_max(cfg.value_dtype));
+    const bool vec4 = (n * size_t(dim)) % 4 == 0 && uintptr_t(dgrads) % 16 == 0 &&
+                      (size_t(t.pcount) * size_t(dim) * gb) % 16 == 0;
+    cuda_check(cudaMemsetAsync(t.ctr + kCtrGradStatus, 0, 4, st), "status clear");
+    {
+      Prof pr(this, "k_accumulate", st);
+      const size_t chunks = n * size_t(dim) / (vec4 ? 4 : 1);
+      const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 16);
+      uint8_t *dst = t.pgrads + size_t(t.pcount) * size_t(dim) * gb;
+      if (vec4)
+        k_accumulate<4><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv,
+                                              t.pkeys + t.pcount, dst, t.ctr + kCtrGradStatus);
+      else
+        k_accumulate<1><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv,
+                                              t.pkeys + t.pcount, dst, t.ctr + kCtrGradStatus);
+      launched("k_accumulate");
+    }
+    // validate_input throws before anything is accumulated: the rows just
+    // written are only kept when the whole batch passed.
+    cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrGradStatus, 4, cudaMemcpyDeviceToHost, st), "status");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    if (status_host[0] & kStatusBadGradient) {
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrGradStatus, 0, 4, st), "status clear");
+      throw std::overflow_error("gradient scale storage exceeds configured dtype");
+    }
+    t.pcount += n;
+  }
+
+  void optimizer_step(size_t nsteps, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (nsteps == 0) throw std::invalid_argument("normalization_steps must be positive");
+    cudaStream_t st = pick(sp);
+    const bool apply = cfg.enable_optimizer && cfg.optimizer_kind != SE_OPT_NONE;
+    if (apply && cfg.optimizer_kind == SE_OPT_ADAM) ensure_bc(steps_taken + 2);
+    steps_taken += 1;
+    for (auto &tp : tables) {
+      Table &t = *tp;
+      if (t.pcount == 0) continue;
+      if (!apply) {
+        t.pcount = 0;
+        continue;
+      }
+      step_table(t, nsteps, st);
+      t.pcount = 0;
+    }
+  }
+
+  void step_table(Table &t, size_t nsteps, cudaStream_t st) {
+    const uint32_t P = uint32_t(t.pcount);
+    // Rows are < capacity; the sentinel for absent keys sorts last.
+    const uint32_t sentinel = uint32_t(std::min<uint64_t>(t.capacity, 0xfffffffeull));
+    int end_bit = 1;
+    while (end_bit < 32 && (uint64_t(1) << end_bit) <= sentinel) ++end_bit;
+    uint32_t *ra = t.rows_a.get(P), *pa = t.pos_a.get(P), *rb = t.rows_b.get(P), *pb = t.pos_b.get(P);
+    uint32_t *starts = t.seg_starts.get(P), *ll = t.long_list.get(P);
+    {
+      Prof pr(this, "k_step_probe", st);
+      k_step_probe<<<grid_for(P, 256), 256, 0, st>>>(t.dir(), t.pkeys, P, sentinel, ra, pa,
+                                                      reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped));
+      launched("k_step_probe");
+    }
+    size_t sort_bytes = 0, sel_bytes = 0;
+    thrust::counting_iterator<uint32_t> it(0);
+    IsSegmentHead head{rb};
+    cuda_check(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, ra, rb, pa, pb, P, 0, end_bit, st),
+               "sort size");
+    cuda_check(cub::DeviceSelect::If(nullptr, sel_bytes, it, starts, t.ctr + kCtrSegments, P, head, st),
+               "select size");
+    uint8_t *tmp = t.cub_tmp.get(std::max(sort_bytes, sel_bytes));
+    {
+      Prof pr(this, "cub_sort", st);
+      cuda_check(cub::DeviceRadixSort::SortPairs(tmp, sort_bytes, ra, rb, pa, pb, P, 0, end_bit, st),
+                 "sort");
+      g_launches += 4;
+    }
+    {
+      Prof pr(this, "cub_select", st);
+      cuda_check(cub::DeviceSelect::If(tmp, sel_bytes, it, starts, t.ctr + kCtrSegments, P, head, st),
+                 "select");
+      g_launches += 2;
+    }
+    cuda_check(cudaMemsetAsync(t.ctr + kCtrLong, 0, 4, st), "memset");
+    OptSpec o{};
+    o.kind = cfg.optimizer_kind;
+    o.lr = cfg.lr;
+    o.b1 = cfg.beta1;
+    o.b2 = cfg.beta2;
+    o.eps = cfg.eps;
+    o.wd = cfg.weight_decay;
+    o.omb1 = 1.0f - cfg.beta1;
+    o.omb2 = 1.0f - cfg.beta2;
+    const uint32_t w = uint32_t(cfg.simd_width > 0 ? cfg.simd_width : 1);
+    o.simd_cut = (uint32_t(t.dim) / w) * w;
+    o.bc = bc;
+    o.factor = cfg.gradient_scale / float(nsteps);
+    o.raw = cfg.gradient_dtype == cfg.value_dtype && nsteps == 1 && cfg.gradient_scale == 1.0f;
+    const int gdt = cfg.gradient_dtype;
+    auto go = [&](auto lanes_tag, auto vec_tag) {
+      constexpr int LN = decltype(lanes_tag)::value;
+      constexpr int VC = decltype(vec_tag)::value;
+      {
+        Prof pr(this, "k_apply", st);
+        k_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+            t.L, t.slabs, o, gdt, t.pgrads, rb, pb, starts, t.ctr + kCtrSegments, P, sentinel,
+            kLongThreshold, ll, t.ctr + kCtrLong);
+        launched("k_apply");
+      }
+      Prof pr(this, "k_apply_long", st);
+      k_apply_long<LN, VC><<<grid_for(P / kLongThreshold + 1, 1, 148 * 2), kLongThreads, 0, st>>>(
+          t.L, t.slabs, o, gdt, t.pgrads, rb, pb, starts, t.ctr + kCtrSegments, P, ll, t.ctr + kCtrLong);
+      launched("k_apply_long");
+    };
+    auto by_lanes = [&](auto vec_tag) {
+      const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
+      switch (ln) {
+      case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+      case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+      case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+      default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+      }
+    };
+    if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
+    else by_lanes(std::integral_constant<int, 1>{});
+  }
+
+  void read_state(int64_t dim, uint64_t key, void *param_out, void *state_out, uint32_t *step_out,
+                  int32_t *found) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    Table &t = table(dim);
+    cudaStream_t st = own;
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    auto *dk = dalloc<unsigned long long>(1);
+    auto *dr = dalloc<uint32_t>(1);
+    unsigned long long k = key;
+    cuda_check(cudaMemcpy(dk, &k, 8, cudaMemcpyHostToDevice), "copy");
+    k_find_rows<<<1, 32, 0, st>>>(t.dir(), dk, 1, dr);
+    launched("k_find_rows");
+    uint32_t row = kNoRow;
+    cuda_check(cudaMemcpyAsync(&row, dr, 4, cudaMemcpyDeviceToHost, st), "copy");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    dfree(dk);
+    dfree(dr);
+    *found = row != kNoRow;
+    if (row == kNoRow) return;
+    std::vector<uint8_t> slab(t.L.stride);
+    cuda_check(cudaMemcpy(slab.data(), t.slabs + size_t(row) * t.L.stride, t.L.stride,
+                          cudaMemcpyDeviceToHost), "copy slab");
+    const size_t pb = size_t(t.dim) * value_bytes(cfg.value_dtype);
+    const size_t ob = size_t(t.dim) * value_bytes(cfg.optimizer_dtype);
+    if (param_out) std::memcpy(param_out, slab.data(), pb);
+    if (state_out && t.L.nstate >= 1) std::memcpy(state_out, slab.data() + t.L.state0, ob);
+    if (state_out && t.L.nstate >= 2)
+      std::memcpy(static_cast<uint8_t *>(state_out) + ob, slab.data() + t.L.state1, ob);
+    if (step_out) {
+      uint32_t s = 0;
+      if (t.L.nstate >= 2) std::memcpy(&s, slab.data() + t.L.step, 4);
+      *step_out = s;
+    }
+  }
+};
+
+void set_last_error(const std::string &msg) { t_last_error = msg; }
+void clear_last_error() { t_last_error.clear(); }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+}  // namespace se_gpu
+
+struct se_store {
+  se_gpu::StoreImpl impl;
+};
+
+using namespace se_gpu;
+
+namespace {
+
+// Returns the common row length, or throws when lengths differ.
+int64_t uniform_dim(const int64_t *row_lengths, size_t n, size_t num_row_lengths, bool gradient) {
+  if (num_row_lengths != n)
+    throw std::invalid_argument(gradient ? "gradient key and row-length counts must match"
+                                         : "row_lengths count must match keys");
+  if (n == 0) return 0;
+  const int64_t d = row_lengths[0];
+  for (size_t i = 0; i < n; ++i) {
+    if (gradient && row_lengths[i] <= 0) throw std::invalid_argument("gradient row length must be positive");
+    if (row_lengths[i] != d)
+      throw Error(SE_ERR_NOT_IMPLEMENTED, "mixed row lengths in one call are not supported by the GPU store");
+  }
+  return d;
+}
+
+se_store *checked(se_store *s) {
+  if (!s) throw std::invalid_argument("store handle is null");
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *se_last_error(void) { return se_gpu::t_last_error.c_str(); }
+const char *se_version(void) { return "se_gpu sm_100a 0.1"; }
+uint64_t se_kernel_launch_count(void) { return se_gpu::g_launches.load(); }
+
+int se_store_create(const se_store_config *config, se_store **out_store) {
+  return guarded([&] {
+    if (!config || !out_store) throw std::invalid_argument("null config or output handle");
+    const se_store_config &c = *config;
+    if (c.num_dims == 0 || !c.dims) throw std::invalid_argument("dims must not be empty");
+    for (size_t i = 0; i < c.num_dims; ++i)
+      if (c.dims[i] <= 0) throw std::invalid_argument("dims must be positive");
+    if (c.key_dtype < SE_KEY_INT32 || c.key_dtype > SE_KEY_UINT64)
+      throw std::invalid_argument("unsupported key dtype code");
+    for (int dt : {c.value_dtype, c.optimizer_dtype, c.gradient_dtype})
+      if (dt < SE_FLOAT32 || dt > SE_BFLOAT16) throw std::invalid_argument("unsupported value dtype");
+    if (!std::isfinite(c.gradient_scale) || c.gradient_scale <= 0.0f)
+      throw std::invalid_argument("gradient_scale must be finite and greater than zero");
+    auto s = std::make_unique<se_store>();
+    StoreImpl &st = s->impl;
+    st.cfg = c;
+    st.device = c.device;
+    DeviceGuard dg(c.device);
+    cuda_check(cudaStreamCreateWithFlags(&st.own, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaMallocHost(&st.status_host, 64), "cudaMallocHost");
+    cuda_check(cudaMallocHost(&st.u64_host, 64), "cudaMallocHost");
+    for (size_t i = 0; i < c.num_dims; ++i) {
+      bool dup = false;
+      for (auto &t : st.tables) dup |= t->dim == c.dims[i];
+      if (dup) continue;
+      st.dims.push_back(c.dims[i]);
+      auto t = std::make_unique<Table>();
+      st.init_table(*t, c.dims[i], c.initial_capacity ? c.initial_capacity : kDefaultCapacity);
+      st.tables.push_back(std::move(t));
+    }
+    if (c.enable_optimizer && c.optimizer_kind == SE_OPT_ADAM) st.ensure_bc(1);
+    cuda_check(cudaDeviceSynchronize(), "create sync");
+    *out_store = s.release();
+  });
+}
+
+int se_store_destroy(se_store *store) {
+  return guarded([&] {
+    if (!store) return;
+    DeviceGuard dg(store->impl.device);
+    delete store;
+  });
+}
+
+int se_forward_lookup_dim(se_store *store, const void *keys, size_t n, int64_t dim, void *out,
+                          void *stream) {
+  return guarded([&] { checked(store)->impl.lookup(keys, n, dim, out, stream, false); });
+}
+
+int se_lookup_or_insert_dim(se_store *store, const void *keys, size_t n, int64_t dim, void *out,
+                            void *stream) {
+  return guarded([&] { checked(store)->impl.lookup(keys, n, dim, out, stream, true); });
+}
+
+int se_forward_lookup(se_store *store, const void *keys, size_t n, void *out, size_t num_out,
+                      const int64_t *row_lengths, size_t num_row_lengths, void *stream) {
+  return guarded([&] {
+    const int64_t d = uniform_dim(row_lengths, n, num_row_lengths, false);
+    if (n == 0) return;
+    if (num_out != n * size_t(d)) throw std::invalid_argument("output size does not match row lengths");
+    checked(store)->impl.lookup(keys, n, d, out, stream, false);
+  });
+}
+
+int se_lookup_or_insert(se_store *store, const void *keys, size_t n, void *out, size_t num_out,
+                        const int64_t *row_lengths, size_t num_row_lengths, void *stream) {
+  return guarded([&] {
+    const int64_t d = uniform_dim(row_lengths, n, num_row_lengths, false);
+    if (n == 0) return;
+    if (num_out != n * size_t(d)) throw std::invalid_argument("output size does not match row lengths");
+    checked(store)->impl.lookup(keys, n, d, out, stream, true);
+  });
+}
+
+int se_accumulate_gradients_dim(se_store *store, const void *keys, size_t n, int64_t dim,
+                                const void *grads, void *stream) {
+  return guarded([&] { checked(store)->impl.accumulate(keys, n, dim, grads, stream); });
+}
+
+int se_accumulate_gradients(se_store *store, const void *keys, size_t n, const void *grads,
+                            size_t num_grad_scalars, const int64_t *row_lengths,
+                            size_t num_row_lengths, void *stream) {
+  return guarded([&] {
+    const int64_t d = uniform_dim(row_lengths, n, num_row_lengths, true);
+    if (n == 0) return;
+    if (num_grad_scalars != n * size_t(d))
+      throw std::invalid_argument("flat gradient scalar count does not match row lengths");
+    checked(store)->impl.accumulate(keys, n, d, grads, stream);
+  });
+}
+
+int se_optimizer_step(se_store *store, size_t normalization_steps, void *stream) {
+  return guarded([&] { checked(store)->impl.optimizer_step(normalization_steps, stream); });
+}
+
+int se_store_size(se_store *store, uint64_t *out) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    uint64_t total = 0;
+    for (auto &t : s.tables) total += s.read_rows_used(*t, s.own);
+    *out = total;
+  });
+}
+
+int se_store_dim_size(se_store *store, int64_t dim, uint64_t *out) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    *out = s.read_rows_used(s.table(dim), s.own);
+  });
+}
+
+int se_store_reserve(se_store *store, size_t keys, int64_t dim) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    if (dim <= 0) throw std::invalid_argument("dim must be > 0");
+    Table &t = s.table(dim);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    const uint64_t used = s.read_rows_used(t, s.own);
+    if (keys > used) {
+      t.rows_bound = used;
+      s.ensure_rows(t, keys - used, s.own);
+      t.rows_bound = used;
+    }
+  });
+}
+
+int se_store_internal_shard_count(se_store *store, uint64_t *out) {
+  return guarded([&] {
+    const int32_t n = checked(store)->impl.cfg.internal_shards;
+    *out = uint64_t(n > 0 ? n : 1);
+  });
+}
+
+int se_store_entries_per_page(se_store *store, uint64_t *out) {
+  return guarded([&] {
+    checked(store);
+    *out = 4096;  // reporting unit of the slab arena; the reference's default page geometry
+  });
+}
+
+int se_store_dropped_gradients(se_store *store, uint64_t *out) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    uint64_t total = 0;
+    for (auto &t : s.tables) {
+      cuda_check(cudaMemcpyAsync(s.u64_host, t->ctr + kCtrDropped, 8, cudaMemcpyDeviceToHost, s.own), "copy");
+      cuda_check(cudaStreamSynchronize(s.own), "sync");
+      total += s.u64_host[0];
+    }
+    *out = total;
+  });
+}
+
+int se_store_read_state(se_store *store, int64_t dim, uint64_t key, void *param_out, void *state_out,
+                        uint32_t *step_out, int32_t *found) {
+  return guarded([&] { checked(store)->impl.read_state(dim, key, param_out, state_out, step_out, found); });
+}
+
+int se_store_synchronize(se_store *store) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    for (auto &t : s.tables) s.check_status(*t, s.own);
+  });
+}
+
+int se_store_profile_enable(se_store *store, int32_t enable) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    s.profiling = enable != 0;
+    if (s.profiling && s.event_pool.size() < 4096) {
+      while (s.event_pool.size() < 4096) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+        s.event_pool.push_back(e);
+      }
+    }
+  });
+}
+
+int se_store_profile_read(se_store *store, const char *name, double *out_ms, uint64_t *out_launches) {
+  return guarded([&] {
+    StoreImpl &s = checked(store)->impl;
+    std::lock_guard<std::mutex> lock(s.mu);
+    DeviceGuard dg(s.device);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    double ms = 0;
+    uint64_t count = 0;
+    std::vector<ProfRec> keep;
+    for (auto &r : s.prof) {
+      if (name && r.name.find(name) == std::string::npos) {
+        keep.push_back(r);
+        continue;
+      }
+      float x = 0;
+      cuda_check(cudaEventElapsedTime(&x, r.a, r.b), "elapsed");
+      ms += x;
+      ++count;
+      s.event_pool.push_back(r.a);
+      s.event_pool.push_back(r.b);
+    }
+    s.prof.swap(keep);
+    *out_ms = ms;
+    *out_launches = count;
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+"""Seeded synthetic workloads with the shapes of the hot path's benchmark configs.
+
+All inputs are synthetic (the reference publishes no dataset): keys are the
+SplitMix64 sequence, hot-key skew is a Zipf law over a seeded permutation of
+the warmed keys, gradients are Gaussian.
+
+  splitmix64_sequence(i) = fmix64((i + 1) * 0x9e3779b97f4a7c15 mod 2^64),
+  the i-th output of the SplitMix64 generator seeded with 0 (a bijection of i).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+
+
+def fmix64(z: np.ndarray) -> np.ndarray:
+    z = np.asarray(z, dtype=np.uint64).copy()
+    with np.errstate(over="ignore"):
+        z ^= z >> np.uint64(30)
+        z *= np.uint64(0xBF58476D1CE4E5B9)
+        z ^= z >> np.uint64(27)
+        z *= np.uint64(0x94D049BB133111EB)
+        z ^= z >> np.uint64(31)
+    return z
+
+
+def splitmix64_sequence(idx) -> np.ndarray:
+    i = np.asarray(idx, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        return fmix64((i + np.uint64(1)) * GOLDEN)
+
+
+class Zipf:
+    """Inverse-CDF sampler of ranks 1..n with weights r^-alpha, mapped through
+    a seeded permutation so hot items are scattered over the key space."""
+
+    def __init__(self, n: int, alpha: float, seed: int):
+        w = np.arange(1, n + 1, dtype=np.float64) ** (-alpha)
+        self.cdf = np.cumsum(w)
+        self.cdf /= self.cdf[-1]
+        self.perm = np.random.default_rng(seed).permutation(n)
+
+    def sample(self, rng: np.random.Generator, size: int) -> np.ndarray:
+        u = rng.random(size)
+        r = np.searchsorted(self.cdf, u, side="right")
+        r = np.minimum(r, len(self.cdf) - 1)
+        return self.perm[r]
+
+
+@dataclass
+class ForwardWorkload:
+    """Forward-only lookup: dim-32 fp32 store warmed with `num_keys`
+    splitmix64 keys; batches of `batch` keys Zipf(alpha) over them."""
+
+    num_keys: int = 1_000_000
+    dim: int = 32
+    batch: int = 4096
+    alpha: float = 1.1
+    seed: int = 0x5EED5CA1E
+
+    def warm_keys(self) -> np.ndarray:
+        return splitmix64_sequence(np.arange(self.num_keys))
+
+    def batches(self, count: int) -> np.ndarray:
+        z = Zipf(self.num_keys, self.alpha, self.seed)
+        rng = np.random.default_rng(self.seed)
+        idx = z.sample(rng, count * self.batch).reshape(count, self.batch)
+        return splitmix64_sequence(idx)
+
+
+@dataclass
+class TrainWorkload:
+    """Single-table train step: dim-64 fp32, `num_keys` warmed int64 keys;
+    batches of `batch` keys, (1 - new_fraction) Zipf(alpha) over the warmed
+    keys and new_fraction never-seen keys inserted on miss; gradients
+    N(0, sigma) with sigma = 1e-3 (standard deviation)."""
+
+    num_keys: int = 10_000_000
+    dim: int = 64
+    batch: int = 65536
+    alpha: float = 1.05
+    new_fraction: float = 0.05
+    sigma: float = 1e-3
+    seed: int = 0xC0FFEE
+    rank: int = 0
+
+    def warm_keys(self) -> np.ndarray:
+        return splitmix64_sequence(np.arange(self.num_keys)).view(np.int64)
+
+    def make_batches(self, count: int, start_step: int = 0):
+        """(keys[count, batch] int64, grads[count, batch, dim] float32)."""
+        z = Zipf(self.num_keys, self.alpha, self.seed)
+        rng = np.random.default_rng([self.seed, self.rank, start_step])
+        n_new = int(round(self.batch * self.new_fraction))
+        n_old = self.batch - n_new
+        keys = np.empty((count, self.batch), dtype=np.int64)
+        for s in range(count):
+            old = splitmix64_sequence(z.sample(rng, n_old))
+            base = self.num_keys + ((start_step + s) * 1024 + self.rank) * n_new
+            new = splitmix64_sequence(np.arange(base, base + n_new, dtype=np.uint64))
+            k = np.concatenate([old, new])
+            rng.shuffle(k)
+            keys[s] = k.view(np.int64)
+        grads = (rng.standard_normal((count, self.batch, self.dim), dtype=np.float32) * np.float32(self.sigma))
+        return keys, grads
