@@ -168,6 +168,26 @@ int se_filter(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const vo
 int se_partition_route(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const void *keys,
                        size_t num_keys, void *send_keys, uint32_t *send_positions,
                        uint32_t *counts, int32_t device, void *stream);
+/*
+ * se_partition_route without any device allocation. It has no counterpart in
+ * the reference. Same arguments, results and errors as se_partition_route,
+ * for callers that cannot allocate device memory during a step: a host
+ * framework whose own allocator has reserved (nearly) all device memory, or a
+ * serving loop that must not fail or stall on an allocation mid-batch.
+ * Its scratch (per-tile partition counts and offsets) is a fixed array
+ * compiled into the library and held by every GPU that loads it until the
+ * process exits: 2 x 256 KiB. Limit: ceil(num_keys / 2048) * num_partitions
+ * <= 65536 (e.g. up to 16,777,216 keys over 8 partitions) and
+ * num_partitions <= 1024; larger inputs fail with SE_ERR_INVALID_ARGUMENT.
+ * The first call on a device looks up the scratch array's device address on
+ * that device; make that first call before any stream capture. All calls share
+ * the one array, so calls that overlap on the GPU (different streams, or
+ * different host threads, on one device) race; serialise them.
+ */
+int se_partition_route_noalloc(int32_t kind, uint32_t num_partitions, int32_t key_dtype,
+                               const void *keys, size_t num_keys, void *send_keys,
+                               uint32_t *send_positions, uint32_t *counts, int32_t device,
+                               void *stream);
 /* Moves rows between the routed order and the input order. row_bytes per row.
  * scatter=0: out[positions[j]] = in[j]  (routed -> input order)
  * scatter=1: out[j] = in[positions[j]]  (input -> routed order) */

@@ -92,6 +92,7 @@ _SIGNATURES = {
     "se_partition": [_i32, _u32, _i32, _vp, _sz, _vp, _i32, _vp],
     "se_filter": [_i32, _u32, _i32, _vp, _sz, _u32, _vp, _i32, _vp],
     "se_partition_route": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],
+    "se_partition_route_noalloc": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],
     "se_permute_rows": [_vp, _vp, _vp, _sz, _sz, _i32, _i32, _vp],
 }
 _RESTYPES = {"se_last_error": C.c_char_p, "se_version": C.c_char_p, "se_kernel_launch_count": _u64}

@@ -375,3 +375,81 @@ extern "C" int se_permute_rows(const void *in_rows, void *out_rows, const uint32
     else run(uint8_t{});
   });
 }
+
+// ---------------------------------------------------------------------------
+// se_partition_route_noalloc: the same three route kernels, with their scratch
+// in a fixed device array instead of stream-ordered allocations, for callers
+// that cannot allocate device memory during a step (a host framework that owns
+// nearly all device memory through its own allocator, or a serving loop that
+// must not fail or stall on an allocation mid-batch).
+// ---------------------------------------------------------------------------
+
+namespace se_gpu {
+namespace {
+
+// Per-tile partition counts followed by per-tile offsets; every word a call
+// reads was written earlier in that call (k_route_count writes all counts of
+// every tile, k_route_scan all offsets), so nothing needs clearing between
+// calls. 2 x 65536 u32 = 512 KiB per device, kept until the process exits.
+constexpr size_t kNoAllocWords = 65536;
+static __device__ __align__(256) uint32_t g_route_scratch[2 * kNoAllocWords];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+uint32_t *g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_route_scratch on `device` (current), looked up once per
+// device. In host code the symbol itself only names a host-side stand-in.
+uint32_t *route_scratch(int device) {
+  if (device < 0 || device >= kMaxDevices) throw std::invalid_argument("device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[device]) {
+    void *p = nullptr;
+    cuda_check(cudaGetSymbolAddress(&p, g_route_scratch), "cudaGetSymbolAddress(route scratch)");
+    g_scratch_ptr[device] = static_cast<uint32_t *>(p);
+  }
+  return g_scratch_ptr[device];
+}
+
+}  // namespace
+}  // namespace se_gpu
+
+extern "C" int se_partition_route_noalloc(int32_t kind, uint32_t num_partitions, int32_t key_dtype,
+                                          const void *keys, size_t num_keys, void *send_keys,
+                                          uint32_t *send_positions, uint32_t *counts, int32_t device,
+                                          void *stream_ptr) {
+  return guarded([&] {
+    const PartSpec s = make_spec(kind, num_partitions);
+    check_key_dtype(key_dtype);
+    if (num_partitions > kRouteMaxPartitions)
+      throw std::invalid_argument("route supports at most 1024 partitions");
+    const uint64_t tiles = (uint64_t(num_keys) + kRouteTile - 1) / kRouteTile;
+    if (tiles * num_partitions > kNoAllocWords)
+      throw std::invalid_argument("se_partition_route_noalloc: ceil(num_keys / 2048) * num_partitions = " +
+                                  std::to_string(tiles * num_partitions) +
+                                  " exceeds its fixed scratch of 65536 entries; use se_partition_route");
+    DeviceGuard dg(device);
+    uint32_t *scratch = route_scratch(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
+    if (num_keys == 0) {
+      cuda_check(cudaMemsetAsync(counts, 0, 4 * size_t(num_partitions), st), "memset counts");
+      return;
+    }
+    if (!is_device_ptr(keys) || !is_device_ptr(send_keys) || !is_device_ptr(send_positions) ||
+        !is_device_ptr(counts))
+      throw std::invalid_argument("se_partition_route_noalloc takes device pointers only");
+    uint32_t *tile_counts = scratch;
+    uint32_t *tile_offsets = scratch + kNoAllocWords;
+    dispatch_key(key_dtype, [&](auto tag) {
+      using K = decltype(tag);
+      const K *k = static_cast<const K *>(keys);
+      k_route_count<K><<<unsigned(tiles), kRouteThreads, num_partitions * 4, st>>>(s, k, num_keys, tile_counts);
+      launched("k_route_count");
+      k_route_scan<<<1, 1024, 0, st>>>(tile_counts, uint32_t(tiles), num_partitions, tile_offsets, counts);
+      launched("k_route_scan");
+      k_route_scatter<K><<<unsigned(tiles), kRouteThreads, kRouteWarps * num_partitions * 4, st>>>(
+          s, k, num_keys, tile_offsets, static_cast<K *>(send_keys), send_positions);
+      launched("k_route_scatter");
+    });
+  });
+}
