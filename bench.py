@@ -74,55 +74,78 @@ def measured_hbm():
 
 
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and clock-event reasons through NVML every 2 ms while
+    the timed region runs (read-only queries); summary() keeps the samples
+    taken between mark_start() and mark_end()."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self.t0 = self.t1 = None
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self.nv = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except FileNotFoundError:
-            self.proc = None
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.nv = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
+        self._stop.set()
+        if self.nv is not None:
+            self.thread.join(timeout=2)
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = max(mx, float(parts[1]))
-            except ValueError:
-                continue
-            for name, v in zip(names, parts[3:7]):
-                if v.lower().startswith("active"):
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "unavailable"}
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        win = [x for x in self.samples if t0 <= x[0] <= t1]
+        reasons = set()
+        for _, _, rs in win:
+            for name, attr in self.REASONS:
+                if rs & int(getattr(self.nv, attr, 0)):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [x[1] for x in win]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 2 ms, timed region only"}
 
 
 # ---------------------------------------------------------------------------
@@ -222,8 +245,9 @@ def run_ours(args):
     uniq = [int(np.unique(keys_np[W + s]).size) for s in range(K)]
 
     def step(s):
-        api.lookup_or_insert(keys_d[s], DIM)
-        api.accumulate_gradients(keys_d[s], grads_d[s])
+        k = keys_d[s]
+        api.lookup_or_insert(k, DIM)
+        api.accumulate_gradients(k, grads_d[s])
         api.optimizer_step(1)
 
     for s in range(W):
@@ -238,11 +262,13 @@ def run_ours(args):
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         barrier(world)
+        clocks.mark_start()
         start.record()
         for s in range(K):
             step(W + s)
         end.record()
         torch.cuda.synchronize()
+        clocks.mark_end()
         barrier(world)
     launches = lib.se_kernel_launch_count() - launches0
     store.profile(False)

@@ -9,6 +9,9 @@
 
 #include <cub/block/block_scan.cuh>
 
+#include <algorithm>
+#include <map>
+#include <tuple>
 #include <mutex>
 #include <string>
 
@@ -234,17 +237,34 @@ template <class F> void dispatch_key(int key_dtype, F &&f) {
   }
 }
 
-// Device copies of host inputs/outputs for one call, freed stream-ordered.
-struct Staged {
-  void *ptr = nullptr;
-  cudaStream_t stream = nullptr;
-  Staged(size_t bytes, cudaStream_t s) : stream(s) {
-    cuda_check(cudaMallocAsync(&ptr, bytes ? bytes : 16, s), "cudaMallocAsync");
+
+// Scratch cached per (device, stream, use): calls on one stream are ordered,
+// so they can share a buffer; a buffer only grows, and lives until the
+// process exits. (Per-call stream-ordered allocation stalled multi-GPU steps.)
+std::mutex g_route_mu;
+std::map<std::tuple<int, cudaStream_t, int>, std::pair<void *, size_t>> g_route_bufs;
+
+enum ScratchUse { kUseRoute = 0, kUseKeysIn = 1, kUseIdsOut = 2 };
+
+// Host-memory partition/filter calls stage through shared buffers and wait for
+// their result, so they run one at a time.
+std::mutex g_host_call_mu;
+
+void *stream_scratch(int device, cudaStream_t st, int use, size_t bytes) {
+  std::lock_guard<std::mutex> lock(g_route_mu);
+  auto &b = g_route_bufs[{device, st, use}];
+  if (b.second < bytes) {
+    if (b.first) {
+      cuda_check(cudaStreamSynchronize(st), "route scratch sync");
+      cuda_check(cudaFree(b.first), "cudaFree");
+      b.first = nullptr;
+    }
+    const size_t cap = std::max<size_t>(bytes, std::max<size_t>(2 * b.second, 1 << 16));
+    cuda_check(cudaMalloc(&b.first, cap), "cudaMalloc(stream scratch)");
+    b.second = cap;
   }
-  ~Staged() {
-    if (ptr) cudaFreeAsync(ptr, stream);
-  }
-};
+  return b.first;
+}
 
 }  // namespace
 
@@ -263,13 +283,15 @@ extern "C" int se_partition(int32_t kind, uint32_t num_partitions, int32_t key_d
     cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
     const size_t kb = key_bytes(key_dtype) * num_keys, ob = 4 * num_keys;
     const bool dk = is_device_ptr(keys), dout = is_device_ptr(out);
-    Staged sk(dk ? 0 : kb, st), so(dout ? 0 : ob, st);
+    std::unique_lock<std::mutex> host_lock(g_host_call_mu, std::defer_lock);
+    if (!dk || !dout) host_lock.lock();
     const void *dkeys = keys;
     if (!dk) {
-      cuda_check(cudaMemcpyAsync(sk.ptr, keys, kb, cudaMemcpyHostToDevice, st), "copy keys");
-      dkeys = sk.ptr;
+      void *sk = stream_scratch(device, st, kUseKeysIn, kb);
+      cuda_check(cudaMemcpyAsync(sk, keys, kb, cudaMemcpyHostToDevice, st), "copy keys");
+      dkeys = sk;
     }
-    uint32_t *dres = dout ? out : static_cast<uint32_t *>(so.ptr);
+    uint32_t *dres = dout ? out : static_cast<uint32_t *>(stream_scratch(device, st, kUseIdsOut, ob));
     dispatch_key(key_dtype, [&](auto tag) {
       using K = decltype(tag);
       k_partition<K><<<grid_for(num_keys, 256, 148 * 16), 256, 0, st>>>(
@@ -294,13 +316,15 @@ extern "C" int se_filter(int32_t kind, uint32_t num_partitions, int32_t key_dtyp
     cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
     const size_t kb = key_bytes(key_dtype) * num_keys;
     const bool dk = is_device_ptr(keys), dout = is_device_ptr(mask);
-    Staged sk(dk ? 0 : kb, st), so(dout ? 0 : num_keys, st);
+    std::unique_lock<std::mutex> host_lock(g_host_call_mu, std::defer_lock);
+    if (!dk || !dout) host_lock.lock();
     const void *dkeys = keys;
     if (!dk) {
-      cuda_check(cudaMemcpyAsync(sk.ptr, keys, kb, cudaMemcpyHostToDevice, st), "copy keys");
-      dkeys = sk.ptr;
+      void *sk = stream_scratch(device, st, kUseKeysIn, kb);
+      cuda_check(cudaMemcpyAsync(sk, keys, kb, cudaMemcpyHostToDevice, st), "copy keys");
+      dkeys = sk;
     }
-    uint8_t *dres = dout ? mask : static_cast<uint8_t *>(so.ptr);
+    uint8_t *dres = dout ? mask : static_cast<uint8_t *>(stream_scratch(device, st, kUseIdsOut, num_keys));
     dispatch_key(key_dtype, [&](auto tag) {
       using K = decltype(tag);
       k_filter<K><<<grid_for(num_keys, 256, 148 * 16), 256, 0, st>>>(
@@ -334,19 +358,18 @@ extern "C" int se_partition_route(int32_t kind, uint32_t num_partitions, int32_t
         !is_device_ptr(counts))
       throw std::invalid_argument("se_partition_route takes device pointers only");
     const uint32_t tiles = uint32_t((num_keys + kRouteTile - 1) / kRouteTile);
-    Staged tc(size_t(tiles) * num_partitions * 4, st), to(size_t(tiles) * num_partitions * 4, st);
+    const size_t words = size_t(tiles) * num_partitions;
+    uint32_t *tile_counts = static_cast<uint32_t *>(stream_scratch(device, st, kUseRoute, 2 * words * 4));
+    uint32_t *tile_offsets = tile_counts + words;
     dispatch_key(key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
-      k_route_count<K><<<tiles, kRouteThreads, num_partitions * 4, st>>>(
-          s, k, num_keys, static_cast<uint32_t *>(tc.ptr));
+      k_route_count<K><<<tiles, kRouteThreads, num_partitions * 4, st>>>(s, k, num_keys, tile_counts);
       launched("k_route_count");
-      k_route_scan<<<1, 1024, 0, st>>>(static_cast<uint32_t *>(tc.ptr), tiles, num_partitions,
-                                       static_cast<uint32_t *>(to.ptr), counts);
+      k_route_scan<<<1, 1024, 0, st>>>(tile_counts, tiles, num_partitions, tile_offsets, counts);
       launched("k_route_scan");
       k_route_scatter<K><<<tiles, kRouteThreads, kRouteWarps * num_partitions * 4, st>>>(
-          s, k, num_keys, static_cast<uint32_t *>(to.ptr), static_cast<K *>(send_keys),
-          send_positions);
+          s, k, num_keys, tile_offsets, static_cast<K *>(send_keys), send_positions);
       launched("k_route_scatter");
     });
   });
