@@ -50,12 +50,13 @@ METRIC = "forward_lookup Mkeys/s & train-step keys/s at 1/2/4/8 B200; % of HBM p
 def args_parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--num-keys", type=int, default=NUM_KEYS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-forward", action="store_true")
+    p.add_argument("--eager", action="store_true", help="time eager API calls instead of CUDA graphs")
     return p.parse_args()
 
 
@@ -74,7 +75,7 @@ def measured_hbm():
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML every 2 ms while
+    """Samples SM clock and clock-event reasons through NVML every 1 ms while
     the timed region runs (read-only queries); summary() keeps the samples
     taken between mark_start() and mark_end()."""
 
@@ -115,7 +116,7 @@ class ClockSampler:
                 self.samples.append((time.perf_counter(), sm, rs))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.001)
 
     def mark_start(self):
         self.t0 = time.perf_counter()
@@ -138,6 +139,12 @@ class ClockSampler:
         t0 = self.t0 if self.t0 is not None else float("-inf")
         t1 = self.t1 if self.t1 is not None else float("inf")
         win = [x for x in self.samples if t0 <= x[0] <= t1]
+        where = "timed region"
+        if not win and self.samples:
+            # a short timed region may fall between two samples: take the
+            # nearest ones around it
+            win = [x for x in self.samples if t0 - 0.05 <= x[0] <= t1 + 0.05]
+            where = "timed region +- 50 ms"
         reasons = set()
         for _, _, rs in win:
             for name, attr in self.REASONS:
@@ -145,7 +152,7 @@ class ClockSampler:
                     reasons.add(name)
         sm = [x[1] for x in win]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 2 ms, timed region only"}
+                "reasons": sorted(reasons), "samples": len(sm), "source": f"nvml every 1 ms, {where}"}
 
 
 # ---------------------------------------------------------------------------
@@ -224,8 +231,9 @@ def run_ours(args):
     wl = TrainWorkload(num_keys=args.num_keys, batch=BATCH, dim=DIM, rank=rank)
     warm = wl.warm_keys()
     mine = owned_keys(warm, world, rank)
-    new_total = (2 * K + W + 4) * int(round(BATCH * wl.new_fraction)) * world
-    cap = int(len(mine) + new_total / max(1, world) * 1.5 + 65536)
+    # Room for every row the run can create, plus the host-side upper bound
+    # the store reserves per insert call while graphs are captured.
+    cap = int(len(mine) + (W + 2 * K + 8) * BATCH)
     store = se.EmbeddingStore(
         se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap),
         optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
@@ -257,27 +265,46 @@ def run_ours(args):
 
     lib = N.lib()
     store.profile(True)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # One GPU: every timed step is a CUDA graph captured from the same API
+    # calls (one graph per batch, the store's per-kernel timing events inside
+    # it), so the timed region holds the kernels and not the Python launch
+    # path. Several GPUs: eager calls (the exchange needs host-side splits).
+    use_graphs = world == 1 and not args.eager
+    graphs = []
     launches0 = lib.se_kernel_launch_count()
+    if use_graphs:
+        pool = torch.cuda.graph_pool_handle()
+        for s in range(K):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool, capture_error_mode="relaxed"):
+                step(W + s)
+            graphs.append(g)
+        torch.cuda.synchronize()
+    launches = lib.se_kernel_launch_count() - launches0  # kernels captured (graphs) ...
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         barrier(world)
         clocks.mark_start()
         start.record()
         for s in range(K):
-            step(W + s)
+            if use_graphs:
+                graphs[s].replay()
+            else:
+                step(W + s)
         end.record()
         torch.cuda.synchronize()
         clocks.mark_end()
         barrier(world)
-    launches = lib.se_kernel_launch_count() - launches0
+    if not use_graphs:
+        launches = lib.se_kernel_launch_count() - launches0  # ... or launched eagerly
     store.profile(False)
     elapsed = max_over_ranks(start.elapsed_time(end) / 1e3, world)
     value = world * BATCH * K / elapsed
 
     # Per-kernel device time inside the timed region.
-    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_step_probe", "cub_sort", "cub_select",
-             "k_apply_long", "k_apply"]
+    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
+             "k_group_place", "k_group_apply", "k_group_hot"]
     times = {}
     for nm in names:
         ms, cnt = store.profile_read(nm)
@@ -285,34 +312,40 @@ def run_ours(args):
     peak, peak_kind = measured_hbm()
     R = DIM * 4
     n_new = int(round(BATCH * wl.new_fraction))
-    # Algorithmic bytes per launch (the figures DESIGN.md states):
+    # Algorithmic bytes per launch:
     #   lookup_or_insert: K + M + R (row read) + R (out write) per key, plus
     #                     R (param) + R (accumulator) initialised per new key;
     #   accumulate:       K + R read and K + R appended per gradient row;
-    #   apply:            per unique key 2R (param r/w) + 2R (accumulator r/w),
+    #   apply (k_group_apply + k_group_hot, one launch each per step):
+    #                     per unique key 2R (param r/w) + 2R (accumulator r/w),
     #                     plus R per gradient row reduced.
     mean_u = sum(uniq) / len(uniq)
     rows_per_owner = BATCH  # weak scaling: each owner receives ~BATCH rows per step
-    alg = {
-        "k_lookup_or_insert": rows_per_owner * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R,
-        "k_accumulate": rows_per_owner * 2 * (KEY_BYTES + R),
-        "k_apply": mean_u * 4 * R + rows_per_owner * R,
+    units = {
+        "k_lookup_or_insert": (["k_lookup_or_insert"],
+                               rows_per_owner * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R),
+        "k_accumulate": (["k_accumulate"], rows_per_owner * 2 * (KEY_BYTES + R)),
+        "k_group_apply+k_group_hot": (["k_group_apply", "k_group_hot"], mean_u * 4 * R + rows_per_owner * R),
     }
     kern = []
     total_ms = sum(t[0] for t in times.values())
     for nm, (ms, cnt) in times.items():
-        entry = {"kernel": nm, "launches": cnt, "ms_total": round(ms, 4),
-                 "share": round(ms / total_ms, 4) if total_ms else None}
-        if nm in alg and cnt:
-            per = ms / cnt / 1e3
-            entry["algorithmic_bytes_per_launch"] = int(alg[nm])
-            entry["achieved_gbs"] = round(alg[nm] / per / 1e9, 1)
-        kern.append(entry)
-    dom = max((k for k in kern if "achieved_gbs" in k), key=lambda k: k["ms_total"])
+        kern.append({"kernel": nm, "launches": cnt, "ms_total": round(ms, 4),
+                     "share": round(ms / total_ms, 4) if total_ms else None})
+    rooflines = []
+    for label, (members, nbytes) in units.items():
+        ms = sum(times[m][0] for m in members)
+        cnt = times[members[0]][1]
+        if not cnt:
+            continue
+        per = ms / cnt / 1e3
+        rooflines.append({"kernel": label, "ms_total": ms, "algorithmic_bytes_per_launch": int(nbytes),
+                          "achieved_gbs": round(nbytes / per / 1e9, 1)})
+    dom = max(rooflines, key=lambda k: k["ms_total"])
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": dom["achieved_gbs"], "peak": peak,
                 "unit": "GB/s", "frac": round(dom["achieved_gbs"] / peak, 4), "traffic": None,
-                "peak_source": peak_kind}
-    step_bytes = alg["k_lookup_or_insert"] + BATCH * (KEY_BYTES + R) + alg["k_apply"] - rows_per_owner * R
+                "peak_source": peak_kind, "per_kernel": rooflines}
+    step_bytes = units["k_lookup_or_insert"][1] + BATCH * (KEY_BYTES + R) + mean_u * 4 * R
     step_roof = {"algorithmic_bytes_per_step_per_gpu": int(step_bytes),
                  "achieved_gbs_per_gpu": round(step_bytes * K / (elapsed) / 1e9, 1)}
     step_roof["frac_of_peak"] = round(step_roof["achieved_gbs_per_gpu"] / peak, 4)
@@ -369,6 +402,8 @@ def run_ours(args):
                                "eps 1e-8, init_acc 0.1), hash partitioner",
                    "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
                    "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
+        "timing": "CUDA graph replay per step (captured from the public API calls)" if use_graphs
+                  else "eager API calls",
         "roofline": roofline, "step_roofline": step_roof, "kernels": kern,
         "e2e": e2e, "clocks": clocks.summary(), "gpu_launches": int(launches),
     }

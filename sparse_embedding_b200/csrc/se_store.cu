@@ -7,9 +7,8 @@
 // within the group), then the lanes split the row in 16-byte (VEC = 4
 // elements) or element-wide chunks.
 
-#include <cub/device/device_radix_sort.cuh>
-#include <cub/device/device_select.cuh>
-#include <thrust/iterator/counting_iterator.h>
+#include <cub/block/block_reduce.cuh>
+#include <cub/block/block_scan.cuh>
 
 #include <algorithm>
 #include <cmath>
@@ -226,31 +225,6 @@ k_accumulate(const void *__restrict__ keys, int kdt, size_t n, const void *__res
   if (bad) raise_status(status, kStatusBadGradient);
 }
 
-// optimizer_step, phase 1: the row of every pending gradient (sentinel when
-// the key is absent) and its arrival position, as radix-sort input.
-// Gradient rows whose key is absent are counted in `dropped`.
-__global__ void __launch_bounds__(256)
-k_step_probe(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t count, uint32_t sentinel,
-             uint32_t *__restrict__ rows, uint32_t *__restrict__ pos, unsigned long long *dropped) {
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  bool absent = false;
-  if (i < count) {
-    const uint32_t r = dir_find<false>(d, pkeys[i]);
-    absent = r == kNoRow;
-    rows[i] = absent ? sentinel : r;
-    pos[i] = i;
-  }
-  const unsigned ballot = __ballot_sync(0xffffffffu, absent);
-  if ((threadIdx.x & 31) == 0 && ballot) atomicAdd(dropped, (unsigned long long)__popc(ballot));
-}
-
-struct IsSegmentHead {
-  const uint32_t *rows;
-  __device__ __forceinline__ bool operator()(const uint32_t &j) const {
-    return j == 0 || rows[j] != rows[j - 1];
-  }
-};
-
 struct OptSpec {
   int kind;
   float lr, b1, b2, eps, wd, omb1, omb2;
@@ -258,6 +232,7 @@ struct OptSpec {
   const float *bc;     // Adam bias corrections: bc[2t], bc[2t+1]
   float factor;        // gradient_scale / normalization_steps
   int raw;             // gradient used as stored (GradT == ParamT, factor 1)
+  const uint32_t *poison;  // nonzero: the window holds a batch that failed validation
 };
 
 // Applies the optimizer to VEC elements [e, e+VEC) of one row, given the
@@ -350,6 +325,96 @@ __device__ __forceinline__ void sum_rows(const void *pgrads, int gdt, uint32_t d
   }
 }
 
+// ---------------------------------------------------------------------------
+// optimizer_step: grouping of the pending gradient rows by key without a
+// sort. Per-row counters in HBM (zero between steps) give each key present
+// this step a segment; rows are placed into their segment by atomics, and
+// each segment's positions are put back in arrival order before it is
+// reduced, so every key is summed in the reference's order (per key, arrival
+// order, from +0.0) regardless of placement order.
+// ---------------------------------------------------------------------------
+
+struct GroupWs {
+  uint32_t *rows;      // [P] row of each pending entry, kNoRow when its key is absent
+  uint32_t *row_cnt;   // [capacity] entries of a row this step (all zero between steps)
+  uint32_t *row_seg;   // [capacity] segment of a row this step
+  uint32_t *seg_row;   // [P] row of each segment
+  uint32_t *seg_cnt;   // [P] entries of each segment
+  uint32_t *seg_off;   // [P] first slot of each segment in pos
+  uint32_t *seg_fill;  // [P] placement counters (all zero between steps)
+  uint32_t *pos;       // [P] entry positions grouped by segment
+  uint4 *items;        // work items of k_group_hot: (segment, part, parts, first item)
+  float *partials;     // [items][dim] partial sums of multi-part segments
+  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items
+};
+
+// Phase 1: row of every entry (absent keys dropped and counted,
+// hogwild_embedding_store.hpp:1942-1952); per-row counts; the first entry to
+// count a row registers it as a new segment.
+__global__ void __launch_bounds__(256)
+k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t count, GroupWs w,
+              unsigned long long *dropped) {
+  __shared__ uint32_t s_rows[256];
+  __shared__ uint32_t s_n, s_base;
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31u;
+  uint32_t row = kNoRow;
+  if (i < count) {
+    row = dir_find<false>(d, pkeys[i]);
+    w.rows[i] = row;
+  }
+  const unsigned absent = __ballot_sync(0xffffffffu, i < count && row == kNoRow);
+  if (lane == 0 && absent) atomicAdd(dropped, (unsigned long long)__popc(absent));
+  const unsigned peers = __match_any_sync(0xffffffffu, row);
+  if (row != kNoRow && (peers & ((1u << lane) - 1u)) == 0) {
+    const uint32_t old = atomicAdd(&w.row_cnt[row], uint32_t(__popc(peers)));
+    if (old == 0) s_rows[atomicAdd(&s_n, 1u)] = row;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && s_n) s_base = atomicAdd(&w.ctr[0], s_n);
+  __syncthreads();
+  if (threadIdx.x < s_n) {
+    const uint32_t sid = s_base + threadIdx.x, r = s_rows[threadIdx.x];
+    w.seg_row[sid] = r;
+    w.row_seg[r] = sid;
+  }
+}
+
+// Phase 2: a contiguous slot range per segment (block-aggregated allocation).
+__global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
+  using Scan = cub::BlockScan<uint32_t, 256>;
+  __shared__ typename Scan::TempStorage tmp;
+  __shared__ uint32_t s_base;
+  const uint32_t nseg = w.ctr[0];
+  const uint32_t sid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (blockIdx.x * blockDim.x >= nseg) return;  // whole block past the end
+  const uint32_t cnt = sid < nseg ? w.row_cnt[w.seg_row[sid]] : 0u;
+  uint32_t excl, total;
+  Scan(tmp).ExclusiveSum(cnt, excl, total);
+  if (threadIdx.x == 0) s_base = atomicAdd(&w.ctr[1], total);
+  __syncthreads();
+  if (sid < nseg) {
+    w.seg_off[sid] = s_base + excl;
+    w.seg_cnt[sid] = cnt;
+  }
+}
+
+// Phase 3: every entry takes a slot of its segment (warp-aggregated).
+__global__ void __launch_bounds__(256) k_group_place(uint32_t count, GroupWs w) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t row = i < count ? w.rows[i] : kNoRow;
+  const uint32_t sid = row != kNoRow ? w.row_seg[row] : 0xffffffffu;
+  const unsigned peers = __match_any_sync(0xffffffffu, sid);
+  const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+  uint32_t base = 0;
+  if (sid != 0xffffffffu && rank == 0) base = atomicAdd(&w.seg_fill[sid], uint32_t(__popc(peers)));
+  base = __shfl_sync(0xffffffffu, base, __ffs(peers) - 1);
+  if (sid != 0xffffffffu) w.pos[w.seg_off[sid] + base + rank] = i;
+}
+
 __device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
   uint32_t *sp = reinterpret_cast<uint32_t *>(slab + L.step);
   const uint32_t t = *sp + 1u;
@@ -357,33 +422,53 @@ __device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
   return t;
 }
 
-// optimizer_step, phase 3: one group per key (segment of the sorted pending
-// gradients). Short segments are reduced serially in arrival order, exactly
-// as the reference sums them; segments longer than long_threshold go to
-// k_apply_long. Absent keys are dropped and counted
-// (hogwild_embedding_store.hpp:1942-1952).
+constexpr int kBlockThreads = 1024;
+constexpr uint32_t kSerialMax = 64;          // rows summed serially (bit-exact order)
+constexpr uint32_t kPartEntries = 512;       // target rows per k_group_hot work item
+constexpr uint32_t kHotWindowBits = 1u << 17;  // positions per bitmap window
+constexpr uint32_t kRoundEntries = 2048;     // rows compacted per round
+
+// Phase 4: one group per segment of at most LANES rows: its positions are
+// ranked inside the group, summed serially in arrival order and the
+// optimizer is applied. Larger segments go to k_group_block.
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256)
-k_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
-        const uint32_t *__restrict__ srows, const uint32_t *__restrict__ spos,
-        const uint32_t *__restrict__ seg_starts, const uint32_t *num_segs_p, uint32_t count,
-        uint32_t sentinel, uint32_t long_threshold, uint32_t *long_list, uint32_t *long_count) {
+k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
+              GroupWs w, uint32_t count) {
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
   const unsigned mask = group_mask<LANES>();
-  const uint32_t nseg = *num_segs_p;
+  const uint32_t nseg = w.ctr[0];
+  const bool poisoned = *o.poison != 0u;
   for (size_t s = t / LANES; s < nseg; s += groups) {
-    const uint32_t k0 = seg_starts[s];
-    const uint32_t k1 = s + 1 < nseg ? seg_starts[s + 1] : count;
-    const uint32_t row = srows[k0];
-    if (row == sentinel) continue;  // absent keys: counted by k_step_probe
-    if (k1 - k0 > long_threshold) {
-      if (lane == 0) long_list[atomicAdd(long_count, 1u)] = uint32_t(s);
+    const uint32_t cnt = w.seg_cnt[s];
+    if (cnt > LANES) {
+      if (lane == 0) {
+        // Work items of k_group_hot: windows of the batch's positions.
+        const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
+        const uint32_t base = atomicAdd(&w.ctr[2], nparts);
+        for (uint32_t q = 0; q < nparts; ++q) w.items[base + q] = make_uint4(uint32_t(s), q, nparts, base);
+      }
       continue;
+    }
+    const uint32_t off = w.seg_off[s], row = w.seg_row[s];
+    const uint32_t p = lane < cnt ? w.pos[off + lane] : 0xffffffffu;
+    uint32_t rank = 0;
+    for (int j = 0; j < LANES; ++j) rank += __shfl_sync(mask, p, j, LANES) < p ? 1u : 0u;
+    // ord[k] = position of rank k (arrival order); group lanes only.
+    const int first_lane = int(threadIdx.x & 31u) & ~(LANES - 1);
+    uint32_t ord[LANES];
+#pragma unroll
+    for (int k = 0; k < LANES; ++k) {
+      const unsigned hit = __ballot_sync(mask, lane < cnt && rank == uint32_t(k));
+      ord[k] = __shfl_sync(mask, p, hit ? __ffs(hit) - 1 : first_lane);
     }
     uint8_t *slab = slabs + size_t(row) * L.stride;
     uint32_t step = 0;
+    if (poisoned || cnt == 0) {
+      // a batch of this window failed validation: nothing is applied
+    } else {
     if (o.kind == SE_OPT_ADAM) {
       if (lane == 0) step = next_step(L, slab);
       step = __shfl_sync(mask, step, 0, LANES);
@@ -392,64 +477,176 @@ k_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *_
       float acc[VEC];
 #pragma unroll
       for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
-      sum_rows<VEC>(pgrads, gdt, L.dim, spos, k0, k1, e, acc);
+      uint32_t k = 0;
+      for (; k + 4 <= cnt; k += 4) {
+        float g0[VEC], g1[VEC], g2[VEC], g3[VEC];
+        ldv<VEC>(pgrads, gdt, size_t(ord[k]) * L.dim + e, g0);
+        ldv<VEC>(pgrads, gdt, size_t(ord[k + 1]) * L.dim + e, g1);
+        ldv<VEC>(pgrads, gdt, size_t(ord[k + 2]) * L.dim + e, g2);
+        ldv<VEC>(pgrads, gdt, size_t(ord[k + 3]) * L.dim + e, g3);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
+          acc[j] = round_to(gdt, __fadd_rn(acc[j], g1[j]));
+          acc[j] = round_to(gdt, __fadd_rn(acc[j], g2[j]));
+          acc[j] = round_to(gdt, __fadd_rn(acc[j], g3[j]));
+        }
+      }
+      for (; k < cnt; ++k) {
+        float g0[VEC];
+        ldv<VEC>(pgrads, gdt, size_t(ord[k]) * L.dim + e, g0);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
+      }
       apply_chunk<VEC>(L, slab, o, step, e, acc);
+    }
+    }
+    if (lane == 0) {
+      w.row_cnt[row] = 0u;
+      w.seg_fill[s] = 0u;
     }
   }
 }
 
-// Long segments (hot keys): one 1024-thread block per key. Its 1024/LANES
-// groups each reduce a contiguous run of the segment in order; group 0 then
-// adds the partial sums in run order and applies the optimizer. The order is
-// fixed by the launch shape, so results are deterministic.
-constexpr int kLongThreads = 1024;
-
+// Phase 5: segments of more than LANES rows. Each segment is cut into parts
+// by windows of batch positions; one 1024-thread block per part finds the
+// segment's rows inside its window in arrival order (bitmap over the
+// window), reduces them, and either applies the optimizer (one part) or
+// leaves a partial sum for the last part to finish, which adds the partial
+// sums in window order. A single-part segment of at most kSerialMax rows is
+// summed serially (the reference's order); larger ones in runs of
+// 1024/LANES groups whose sums are added in run order. Everything is fixed by
+// the shapes, so results are deterministic.
 template <int LANES, int VEC>
-__global__ void __launch_bounds__(kLongThreads)
-k_apply_long(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
-             const uint32_t *__restrict__ srows, const uint32_t *__restrict__ spos,
-             const uint32_t *__restrict__ seg_starts, const uint32_t *num_segs_p, uint32_t count,
-             const uint32_t *long_list, const uint32_t *long_count) {
-  constexpr int NG = kLongThreads / LANES;
+__global__ void __launch_bounds__(kBlockThreads)
+k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
+            GroupWs w, uint32_t count) {
+  using Scan = cub::BlockScan<uint32_t, kBlockThreads>;
+  constexpr int NG = kBlockThreads / LANES;
+  constexpr uint32_t WPT = kHotWindowBits / 32 / kBlockThreads;  // bitmap words per thread
+  __shared__ uint32_t bitmap[kHotWindowBits / 32];
+  __shared__ typename Scan::TempStorage scan_tmp;
+  __shared__ uint32_t s_pos[kRoundEntries];
   __shared__ float part[NG][LANES][VEC];
-  __shared__ uint32_t step_s;
+  __shared__ uint32_t s_last, s_step;
   const uint32_t lane = threadIdx.x % LANES;
   const uint32_t grp = threadIdx.x / LANES;
-  const uint32_t nseg = *num_segs_p;
-  const uint32_t nlong = *long_count;
-  for (uint32_t x = blockIdx.x; x < nlong; x += gridDim.x) {
-    const uint32_t s = long_list[x];
-    const uint32_t k0 = seg_starts[s];
-    const uint32_t k1 = s + 1 < nseg ? seg_starts[s + 1] : count;
-    const uint32_t row = srows[k0];
-    uint8_t *slab = slabs + size_t(row) * L.stride;
-    if (threadIdx.x == 0) step_s = o.kind == SE_OPT_ADAM ? next_step(L, slab) : 0u;
-    const uint32_t len = k1 - k0;
-    const uint32_t per = (len + NG - 1) / NG;
-    const uint32_t r0 = min(k0 + grp * per, k1), r1 = min(r0 + per, k1);
+  const uint32_t nitems = w.ctr[2];
+  const bool poisoned = *o.poison != 0u;
+  for (uint32_t x = blockIdx.x; x < nitems; x += gridDim.x) {
+    const uint4 it = w.items[x];
+    const uint32_t s = it.x, q = it.y, nparts = it.z, first = it.w;
+    const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
+    uint32_t win = (count + nparts - 1) / nparts;
+    win = (win + 31u) & ~31u;
+    const uint32_t w0 = min(q * win, count), w1 = min(w0 + win, count);
+    const uint32_t nwords = (w1 - w0 + 31u) / 32u;
+    // The segment's rows inside [w0, w1), as a bitmap over the window.
+    for (uint32_t j = 0; j < WPT; ++j) bitmap[threadIdx.x * WPT + j] = 0u;
     __syncthreads();
-    const uint32_t step = step_s;
+    for (uint32_t k = threadIdx.x; k < cnt; k += kBlockThreads) {
+      const uint32_t p = w.pos[off + k];
+      if (p >= w0 && p < w1) atomicOr(&bitmap[(p - w0) >> 5], 1u << ((p - w0) & 31u));
+    }
+    __syncthreads();
+    uint32_t bits = 0;
+    for (uint32_t j = 0; j < WPT; ++j) {
+      const uint32_t wi = threadIdx.x * WPT + j;
+      bits += wi < nwords ? __popc(bitmap[wi]) : 0u;
+    }
+    uint32_t excl, total;
+    Scan(scan_tmp).ExclusiveSum(bits, excl, total);
+    // Compacts the window's rows of rank [r0, r0 + kRoundEntries) into s_pos.
+    auto compact = [&](uint32_t r0) {
+      uint32_t rank = excl;
+      for (uint32_t j = 0; j < WPT; ++j) {
+        const uint32_t wi = threadIdx.x * WPT + j;
+        uint32_t word = wi < nwords ? bitmap[wi] : 0u;
+        while (word) {
+          const uint32_t b = __ffs(word) - 1;
+          word &= word - 1;
+          if (rank >= r0 && rank - r0 < kRoundEntries) s_pos[rank - r0] = w0 + wi * 32u + b;
+          ++rank;
+        }
+      }
+    };
+    const bool one_round = total <= kRoundEntries;
+    const bool serial = nparts == 1 && cnt <= kSerialMax;
+    uint8_t *slab = slabs + size_t(row) * L.stride;
+    if (one_round) compact(0);
+    if (threadIdx.x == 0) s_step = (nparts == 1 && !poisoned && o.kind == SE_OPT_ADAM) ? next_step(L, slab) : 0u;
+    __syncthreads();
     for (uint32_t base = 0; base < L.dim; base += LANES * VEC) {
       const uint32_t e = base + lane * VEC;
-      const bool valid = e < L.dim;
-      float acc[VEC];
+      float acc[VEC];  // running sum of the window (group 0)
 #pragma unroll
       for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
-      if (valid) sum_rows<VEC>(pgrads, gdt, L.dim, spos, r0, r1, e, acc);
+      for (uint32_t r0 = 0; r0 < total; r0 += kRoundEntries) {
+        if (!one_round) {
+          __syncthreads();
+          compact(r0);
+          __syncthreads();
+        }
+        const uint32_t n = min(total - r0, kRoundEntries);
+        if (serial) {
+          if (grp == 0 && e < L.dim) sum_rows<VEC>(pgrads, gdt, L.dim, s_pos, 0, n, e, acc);
+        } else {
+          const uint32_t per = (n + NG - 1) / NG;
+          const uint32_t k0 = min(grp * per, n), k1 = min(k0 + per, n);
+          float a[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) part[grp][lane][j] = acc[j];
+          for (int j = 0; j < VEC; ++j) a[j] = 0.0f;
+          if (e < L.dim) sum_rows<VEC>(pgrads, gdt, L.dim, s_pos, k0, k1, e, a);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) part[grp][lane][j] = a[j];
+          __syncthreads();
+          if (grp == 0)
+            for (int g = 0; g < NG; ++g)
+#pragma unroll
+              for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], part[g][lane][j]));
+          __syncthreads();
+        }
+      }
+      if (grp == 0 && e < L.dim) {
+        if (nparts == 1) {
+          if (!poisoned) apply_chunk<VEC>(L, slab, o, s_step, e, acc);
+        } else {
+          float *dst = w.partials + size_t(first + q) * L.dim;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) dst[e + j] = acc[j];
+        }
+      }
+    }
+    if (nparts > 1) {
+      // The last part to finish adds the parts' sums in window order.
+      __threadfence();
       __syncthreads();
-      if (grp == 0 && valid) {
-        float tot[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) tot[j] = 0.0f;
-        for (int q = 0; q < NG; ++q)
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) tot[j] = round_to(gdt, __fadd_rn(tot[j], part[q][lane][j]));
-        apply_chunk<VEC>(L, slab, o, step, e, tot);
+      if (threadIdx.x == 0) {
+        const uint32_t old = atomicAdd(&w.seg_fill[s], 1u);  // placement left it at cnt
+        s_last = old == cnt + nparts - 1 ? 1u : 0u;
+        s_step = (s_last && !poisoned && o.kind == SE_OPT_ADAM) ? next_step(L, slab) : 0u;
       }
       __syncthreads();
+      if (s_last && grp == 0 && !poisoned) {
+        __threadfence();
+        for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+          float tot[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) tot[j] = 0.0f;
+          for (uint32_t g = 0; g < nparts; ++g) {
+            const float *src = w.partials + size_t(first + g) * L.dim + e;
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) tot[j] = round_to(gdt, __fadd_rn(tot[j], __ldcg(src + j)));
+          }
+          apply_chunk<VEC>(L, slab, o, s_step, e, tot);
+        }
+      }
     }
+    if (threadIdx.x == 0 && (nparts == 1 || s_last)) {
+      w.row_cnt[row] = 0u;
+      w.seg_fill[s] = 0u;
+    }
+    __syncthreads();
   }
 }
 
@@ -481,7 +678,6 @@ std::atomic<uint64_t> g_launches{0};
 
 constexpr uint64_t kDefaultCapacity = 1u << 16;
 constexpr double kMaxLoadPerBucket = 3.5;  // 70 % of 5 slots
-constexpr uint32_t kLongThreshold = 64;
 
 uint64_t next_pow2(uint64_t x) {
   uint64_t p = 1;
@@ -534,11 +730,11 @@ enum Ctr : int {
   kCtrSpecialClaim = 1,
   kCtrSpecialRow = 2,
   kCtrDeferred = 3,
-  kCtrLong = 4,
-  kCtrSegments = 5,
-  kCtrStatus = 6,      // insert / directory errors
-  kCtrGradStatus = 7,  // gradient validation of the current accumulate call
-  kCtrDropped = 8,     // u64 at words 8-9
+  kCtrGroup = 4,       // words 4-5-6 (+7 spare): GroupWs counters, cleared each step
+  kCtrStatus = 12,      // insert / directory errors
+  kCtrGradStatus = 13,  // gradient validation of the current accumulate call
+  kCtrDropped = 8,      // u64 at words 8-9
+  kCtrPoison = 10,      // sticky: a device-input gradient batch failed validation
   kCtrWords = 16,
 };
 
@@ -559,10 +755,14 @@ struct Table {
   unsigned long long *pkeys = nullptr;
   uint8_t *pgrads = nullptr;
   uint64_t pcap = 0, pcount = 0;
+  // per-row grouping counters of optimizer_step (capacity entries each)
+  uint32_t *row_cnt = nullptr, *row_seg = nullptr;
   // step and insert work buffers
-  Scratch<uint32_t> rows_a, pos_a, rows_b, pos_b, seg_starts, long_list, def_pos;
+  Scratch<uint32_t> g_rows, g_seg_row, g_seg_cnt, g_seg_off, g_seg_fill, g_pos, def_pos;
+  Scratch<uint4> g_items;
+  Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
-  Scratch<uint8_t> cub_tmp;
+  uint64_t seg_fill_zeroed = 0;  // entries of g_seg_fill known to be zero
 
   Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
   ~Table() {
@@ -571,6 +771,8 @@ struct Table {
     dfree(ctr);
     dfree(pkeys);
     dfree(pgrads);
+    dfree(row_cnt);
+    dfree(row_seg);
   }
 };
 
@@ -636,16 +838,24 @@ struct StoreImpl {
     StoreImpl *s;
     cudaStream_t st;
     ProfRec rec{};
+    // Inside stream capture the records become external event nodes, which
+    // are recorded (and can be timed) every time the graph is launched.
+    static void record(cudaEvent_t e, cudaStream_t st) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cs);
+      if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+      else cudaEventRecord(e, st);
+    }
     Prof(StoreImpl *store, const char *name, cudaStream_t stream) : s(store), st(stream) {
       if (!s->profiling) return;
       rec.name = name;
       rec.a = s->take_event();
       rec.b = s->take_event();
-      cudaEventRecord(rec.a, st);
+      record(rec.a, st);
     }
     ~Prof() {
       if (!s->profiling) return;
-      cudaEventRecord(rec.b, st);
+      record(rec.b, st);
       s->prof.push_back(rec);
     }
   };
@@ -675,9 +885,19 @@ struct StoreImpl {
     cuda_check(cudaMemset(t.ctr + kCtrSpecialRow, 0xff, 4), "memset special");
     t.capacity = std::max<uint64_t>(cap, 64);
     t.slabs = dalloc<uint8_t>(size_t(t.capacity) * t.L.stride);
+    alloc_row_arrays(t, t.capacity);
     t.nbuckets = next_pow2(uint64_t(double(t.capacity) / kMaxLoadPerBucket) + 1);
     t.buckets = dalloc<Bucket>(t.nbuckets);
     cuda_check(cudaMemset(t.buckets, 0xff, t.nbuckets * sizeof(Bucket)), "memset directory");
+  }
+
+  // Per-row grouping counters, zero between steps.
+  void alloc_row_arrays(Table &t, uint64_t cap) {
+    dfree(t.row_cnt);
+    dfree(t.row_seg);
+    t.row_cnt = dalloc<uint32_t>(cap);
+    t.row_seg = dalloc<uint32_t>(cap);
+    cuda_check(cudaMemset(t.row_cnt, 0, cap * 4), "memset row counters");
   }
 
   uint64_t read_rows_used(Table &t, cudaStream_t st) {
@@ -705,6 +925,7 @@ struct StoreImpl {
         dfree(t.slabs);
         t.slabs = ns;
         t.capacity = ncap;
+        alloc_row_arrays(t, ncap);
       }
       if (need > dir_limit(t.nbuckets)) {
         uint64_t nb = t.nbuckets;
@@ -862,11 +1083,20 @@ struct StoreImpl {
   // kernels; their errors surface at the next synchronising call.
   void check_status(Table &t, cudaStream_t st) {
     cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrStatus, 4, cudaMemcpyDeviceToHost, st), "status");
+    cuda_check(cudaMemcpyAsync(status_host + 1, t.ctr + kCtrPoison, 4, cudaMemcpyDeviceToHost, st), "status");
     cuda_check(cudaMemsetAsync(t.ctr + kCtrStatus, 0, 4, st), "status clear");
     cuda_check(cudaStreamSynchronize(st), "sync");
     const uint32_t s = status_host[0];
     if (s & kStatusTableFull) throw Error(SE_ERR_TABLE_FULL, "embedding table is full");
     if (s & kStatusBadRow) throw Error(SE_ERR_RUNTIME, "row index outside the arena");
+    if (status_host[1] && t.pcount == 0) {
+      // the poisoned window has been stepped (and discarded): report it once
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrPoison, 0, 4, st), "status clear");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+      throw std::overflow_error(
+          "gradient scale storage exceeds configured dtype (a device gradient batch failed validation; "
+          "its accumulation window was discarded)");
+    }
   }
 
   void accumulate(const void *keys, size_t n, int64_t dim, const void *grads, void *sp) {
@@ -883,7 +1113,14 @@ struct StoreImpl {
     const float maxv = std::min(host_dtype_max(cfg.gradient_dtype), host_dtype_max(cfg.value_dtype));
     const bool vec4 = (n * size_t(dim)) % 4 == 0 && uintptr_t(dgrads) % 16 == 0 &&
                       (size_t(t.pcount) * size_t(dim) * gb) % 16 == 0;
-    cuda_check(cudaMemsetAsync(t.ctr + kCtrGradStatus, 0, 4, st), "status clear");
+    // Host inputs: validate_input semantics of the reference - the call waits
+    // for its check and raises before anything is accumulated. Device inputs:
+    // the check runs on the device without stalling the stream; a failing
+    // batch poisons the window (optimizer_step then applies nothing) and the
+    // error is raised by the next synchronising call.
+    const bool device_inputs = dkeys == keys && dgrads == grads;
+    uint32_t *status_word = t.ctr + (device_inputs ? kCtrPoison : kCtrGradStatus);
+    if (!device_inputs) cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
     {
       Prof pr(this, "k_accumulate", st);
       const size_t chunks = n * size_t(dim) / (vec4 ? 4 : 1);
@@ -892,20 +1129,21 @@ struct StoreImpl {
       if (vec4)
         k_accumulate<4><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv,
-                                              t.pkeys + t.pcount, dst, t.ctr + kCtrGradStatus);
+                                              t.pkeys + t.pcount, dst, status_word);
       else
         k_accumulate<1><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv,
-                                              t.pkeys + t.pcount, dst, t.ctr + kCtrGradStatus);
+                                              t.pkeys + t.pcount, dst, status_word);
       launched("k_accumulate");
     }
-    // validate_input throws before anything is accumulated: the rows just
-    // written are only kept when the whole batch passed.
-    cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrGradStatus, 4, cudaMemcpyDeviceToHost, st), "status");
-    cuda_check(cudaStreamSynchronize(st), "sync");
-    if (status_host[0] & kStatusBadGradient) {
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrGradStatus, 0, 4, st), "status clear");
-      throw std::overflow_error("gradient scale storage exceeds configured dtype");
+    if (!device_inputs) {
+      // the rows just written are only kept when the whole batch passed
+      cuda_check(cudaMemcpyAsync(status_host, status_word, 4, cudaMemcpyDeviceToHost, st), "status");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+      if (status_host[0] & kStatusBadGradient) {
+        cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+        throw std::overflow_error("gradient scale storage exceeds configured dtype");
+      }
     }
     t.pcount += n;
   }
@@ -932,39 +1170,47 @@ struct StoreImpl {
 
   void step_table(Table &t, size_t nsteps, cudaStream_t st) {
     const uint32_t P = uint32_t(t.pcount);
-    // Rows are < capacity; the sentinel for absent keys sorts last.
-    const uint32_t sentinel = uint32_t(std::min<uint64_t>(t.capacity, 0xfffffffeull));
-    int end_bit = 1;
-    while (end_bit < 32 && (uint64_t(1) << end_bit) <= sentinel) ++end_bit;
-    uint32_t *ra = t.rows_a.get(P), *pa = t.pos_a.get(P), *rb = t.rows_b.get(P), *pb = t.pos_b.get(P);
-    uint32_t *starts = t.seg_starts.get(P), *ll = t.long_list.get(P);
-    {
-      Prof pr(this, "k_step_probe", st);
-      k_step_probe<<<grid_for(P, 256), 256, 0, st>>>(t.dir(), t.pkeys, P, sentinel, ra, pa,
-                                                      reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped));
-      launched("k_step_probe");
+    GroupWs w{};
+    w.rows = t.g_rows.get(P);
+    w.row_cnt = t.row_cnt;
+    w.row_seg = t.row_seg;
+    w.seg_row = t.g_seg_row.get(P);
+    w.seg_cnt = t.g_seg_cnt.get(P);
+    w.seg_off = t.g_seg_off.get(P);
+    const size_t fill_cap_before = t.g_seg_fill.cap;
+    w.seg_fill = t.g_seg_fill.get(P);
+    if (t.g_seg_fill.cap != fill_cap_before || t.seg_fill_zeroed < P) {
+      // placement counters are reset by the apply kernels after use; a new
+      // or grown buffer starts from zero
+      cuda_check(cudaMemsetAsync(w.seg_fill, 0, t.g_seg_fill.cap * 4, st), "memset seg_fill");
+      t.seg_fill_zeroed = t.g_seg_fill.cap;
     }
-    size_t sort_bytes = 0, sel_bytes = 0;
-    thrust::counting_iterator<uint32_t> it(0);
-    IsSegmentHead head{rb};
-    cuda_check(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, ra, rb, pa, pb, P, 0, end_bit, st),
-               "sort size");
-    cuda_check(cub::DeviceSelect::If(nullptr, sel_bytes, it, starts, t.ctr + kCtrSegments, P, head, st),
-               "select size");
-    uint8_t *tmp = t.cub_tmp.get(std::max(sort_bytes, sel_bytes));
+    w.pos = t.g_pos.get(P);
+    // Upper bound on k_group_hot work items: segments of more than `lanes`
+    // rows, each cut into max(ceil(rows / kPartEntries), ceil(P / window)) parts.
+    const uint64_t min_parts = (uint64_t(P) + kHotWindowBits - 1) / kHotWindowBits;
+    const uint64_t max_items = uint64_t(P) / kPartEntries + 1 + (uint64_t(P) / 5 + 1) * (min_parts + 1);
+    w.items = reinterpret_cast<uint4 *>(t.g_items.get(max_items));
+    w.partials = t.g_partials.get(max_items * uint64_t(t.dim));
+    w.ctr = t.ctr + kCtrGroup;
+    cuda_check(cudaMemsetAsync(w.ctr, 0, 16, st), "memset group counters");
+    auto *dropped = reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped);
+    const unsigned g = grid_for(P, 256);
     {
-      Prof pr(this, "cub_sort", st);
-      cuda_check(cub::DeviceRadixSort::SortPairs(tmp, sort_bytes, ra, rb, pa, pb, P, 0, end_bit, st),
-                 "sort");
-      g_launches += 4;
+      Prof pr(this, "k_group_count", st);
+      k_group_count<<<g, 256, 0, st>>>(t.dir(), t.pkeys, P, w, dropped);
+      launched("k_group_count");
     }
     {
-      Prof pr(this, "cub_select", st);
-      cuda_check(cub::DeviceSelect::If(tmp, sel_bytes, it, starts, t.ctr + kCtrSegments, P, head, st),
-                 "select");
-      g_launches += 2;
+      Prof pr(this, "k_group_alloc", st);
+      k_group_alloc<<<g, 256, 0, st>>>(w);
+      launched("k_group_alloc");
     }
-    cuda_check(cudaMemsetAsync(t.ctr + kCtrLong, 0, 4, st), "memset");
+    {
+      Prof pr(this, "k_group_place", st);
+      k_group_place<<<g, 256, 0, st>>>(P, w);
+      launched("k_group_place");
+    }
     OptSpec o{};
     o.kind = cfg.optimizer_kind;
     o.lr = cfg.lr;
@@ -974,26 +1220,25 @@ struct StoreImpl {
     o.wd = cfg.weight_decay;
     o.omb1 = 1.0f - cfg.beta1;
     o.omb2 = 1.0f - cfg.beta2;
-    const uint32_t w = uint32_t(cfg.simd_width > 0 ? cfg.simd_width : 1);
-    o.simd_cut = (uint32_t(t.dim) / w) * w;
+    const uint32_t wdt = uint32_t(cfg.simd_width > 0 ? cfg.simd_width : 1);
+    o.simd_cut = (uint32_t(t.dim) / wdt) * wdt;
     o.bc = bc;
     o.factor = cfg.gradient_scale / float(nsteps);
     o.raw = cfg.gradient_dtype == cfg.value_dtype && nsteps == 1 && cfg.gradient_scale == 1.0f;
+    o.poison = t.ctr + kCtrPoison;
     const int gdt = cfg.gradient_dtype;
     auto go = [&](auto lanes_tag, auto vec_tag) {
       constexpr int LN = decltype(lanes_tag)::value;
       constexpr int VC = decltype(vec_tag)::value;
       {
-        Prof pr(this, "k_apply", st);
-        k_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 0x7fffffffu), 256, 0, st>>>(
-            t.L, t.slabs, o, gdt, t.pgrads, rb, pb, starts, t.ctr + kCtrSegments, P, sentinel,
-            kLongThreshold, ll, t.ctr + kCtrLong);
-        launched("k_apply");
+        Prof pr(this, "k_group_apply", st);
+        k_group_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+            t.L, t.slabs, o, gdt, t.pgrads, w, P);
+        launched("k_group_apply");
       }
-      Prof pr(this, "k_apply_long", st);
-      k_apply_long<LN, VC><<<grid_for(P / kLongThreshold + 1, 1, 148 * 2), kLongThreads, 0, st>>>(
-          t.L, t.slabs, o, gdt, t.pgrads, rb, pb, starts, t.ctr + kCtrSegments, P, ll, t.ctr + kCtrLong);
-      launched("k_apply_long");
+      Prof pr(this, "k_group_hot", st);
+      k_group_hot<LN, VC><<<148 * 2, kBlockThreads, 0, st>>>(t.L, t.slabs, o, gdt, t.pgrads, w, P);
+      launched("k_group_hot");
     };
     auto by_lanes = [&](auto vec_tag) {
       const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));

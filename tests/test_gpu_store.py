@@ -230,6 +230,46 @@ def test_hot_key_long_segments_within_tolerance():
     _compare_state(gpu, orc, pool[:20], 64, 1, exact=False)
 
 
+@pytest.mark.parametrize("dim,opt", [(64, "sgd"), (256, "adagrad"), (64, "adam")])
+def test_hot_key_many_parts_and_rounds(dim, opt):
+    """A key with thousands of rows packed into one stretch of the batch (its
+    window holds more rows than one compaction round), spread over several
+    accumulate calls; plus a moderately hot key spread over the batch.
+
+    SGD and Adagrad parameters are compared at 1e-5. Adam divides the first
+    moment by the root of the second, so an element whose summed gradient is
+    near zero amplifies the summation-order difference without bound; for
+    Adam the moments (linear in the sum) are compared instead."""
+    okw = {"lr": 1e-3} if opt != "adagrad" else {"lr": 0.01, "initial_accumulator_value": 0.1}
+    gpu, orc = pair([dim], key_dtype="uint64", opt=opt, **okw)
+    rng = np.random.default_rng(17)
+    pool = splitmix64_sequence(np.arange(2000))
+    gpu.lookup_or_insert(pool, dim)
+    orc.lookup_or_insert(pool, dim)
+    for call in range(3):
+        keys = rng.choice(pool, size=60_000)
+        keys[10_000:13_500] = pool[0]   # 3,500 consecutive rows of one key
+        keys[rng.choice(60_000, 900, replace=False)] = pool[1]
+        g = (rng.standard_normal((len(keys), dim)) * 1e-3).astype(np.float32)
+        gpu.accumulate_gradients(keys, g)
+        orc.accumulate_gradients(keys, g, dim)
+    gpu.optimizer_step(3)
+    orc.optimizer_step(3)
+    nstate = {"sgd": 0, "adagrad": 1, "adam": 2}[opt]
+    if opt != "adam":
+        got, _ = gpu.lookup(pool, dim)
+        np.testing.assert_allclose(got, orc.lookup(pool, dim), rtol=RTOL_FP32, atol=ATOL_FP32)
+        _compare_state(gpu, orc, pool[:8], dim, nstate, exact=False)
+    else:
+        for k in pool[:8]:
+            f1, _, s1, t1 = gpu.read_state(int(k), dim)
+            f2, _, s2, t2 = orc.read_row(int(k), dim, nstate)
+            assert f1 and f2 and t1 == t2 == 1
+            # normwise: |dm| <= 1e-5 * max|m| (a near-zero sum has no relative accuracy)
+            for a, b in ((s1[:dim], s2[:dim]), (s1[dim:], s2[dim:])):
+                np.testing.assert_allclose(a, b, rtol=RTOL_FP32, atol=RTOL_FP32 * np.abs(b).max())
+
+
 def test_gradient_overflow_rejected_and_not_accumulated():
     # test_mixed_precision.py:457-472
     gpu = se.EmbeddingStore(se.EmbeddingConfig(dims=[1], value_dtype="float16", optimizer_dtype="float32",
@@ -243,6 +283,29 @@ def test_gradient_overflow_rejected_and_not_accumulated():
     gpu.optimizer_step(1)
     vals, _ = gpu.lookup(key, 1)
     np.testing.assert_array_equal(np.asarray(vals).astype(np.float32), [-2.0])
+
+
+def test_device_gradient_overflow_poisons_window():
+    """CUDA gradient inputs are validated on the device without a stall: a
+    failing batch discards its accumulation window and the OverflowError is
+    raised by the next synchronising call; training then continues."""
+    gpu = se.EmbeddingStore(se.EmbeddingConfig(dims=[4], value_dtype="float16", optimizer_dtype="float32",
+                                               gradient_dtype="float32", key_dtype="int64"),
+                            optimizer_config=se.Sgd(lr=1.0), initializer_config=se.Zeros())
+    keys = torch.tensor([1, 2], dtype=torch.int64, device="cuda")
+    gpu.lookup_or_insert(keys, 4)
+    gpu.accumulate_gradients(keys, torch.ones((2, 4), device="cuda"))
+    gpu.accumulate_gradients(keys, torch.full((2, 4), 1e6, device="cuda"))  # above float16 range
+    gpu.optimizer_step(1)
+    with pytest.raises(OverflowError, match="gradient"):
+        gpu.synchronize()
+    vals, _ = gpu.lookup(keys, 4)
+    assert torch.equal(vals.cpu().float(), torch.zeros(8))  # the whole window was discarded
+    gpu.accumulate_gradients(keys, torch.ones((2, 4), device="cuda"))
+    gpu.optimizer_step(1)
+    gpu.synchronize()
+    vals, _ = gpu.lookup(keys, 4)
+    assert torch.equal(vals.cpu().float(), -torch.ones(8))
 
 
 @pytest.mark.parametrize("n", [1, 2, 3])
