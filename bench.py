@@ -233,7 +233,7 @@ def run_ours(args):
     mine = owned_keys(warm, world, rank)
     # Room for every row the run can create, plus the host-side upper bound
     # the store reserves per insert call while graphs are captured.
-    cap = int(len(mine) + (W + 2 * K + 8) * BATCH)
+    cap = int(len(mine) + (W + 4 * K + 8) * BATCH)
     store = se.EmbeddingStore(
         se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap),
         optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
@@ -246,11 +246,11 @@ def run_ours(args):
 
         api = ShardedEmbeddingStore(store, "sparse_embedding.hash")
 
-    keys_np, _ = wl.make_batches(W + K, start_step=0)
+    keys_np, _ = wl.make_batches(W + 2 * K, start_step=0)
     keys_d = torch.from_numpy(keys_np).cuda()
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    grads_d = torch.randn((W + K, BATCH, DIM), generator=gen, device="cuda") * 1e-3
-    uniq = [int(np.unique(keys_np[W + s]).size) for s in range(K)]
+    grads_d = torch.randn((W + 2 * K, BATCH, DIM), generator=gen, device="cuda") * 1e-3
+    uniq = [int(np.unique(keys_np[W + K + s]).size) for s in range(K)]
 
     def step(s):
         k = keys_d[s]
@@ -264,43 +264,51 @@ def run_ours(args):
     barrier(world)
 
     lib = N.lib()
-    store.profile(True)
     # One GPU: every timed step is a CUDA graph captured from the same API
-    # calls (one graph per batch, the store's per-kernel timing events inside
-    # it), so the timed region holds the kernels and not the Python launch
-    # path. Several GPUs: eager calls (the exchange needs host-side splits).
+    # calls (one graph per batch), so the timed region holds the kernels and
+    # not the Python launch path. Several GPUs: eager calls (the exchange
+    # needs host-side splits). Two timed passes over different batches:
+    # pass 1 gives `value` (no instrumentation); pass 2 repeats it with the
+    # store's CUDA events around every kernel, on the launching stream, for
+    # the per-kernel durations of the roofline.
     use_graphs = world == 1 and not args.eager
-    graphs = []
-    launches0 = lib.se_kernel_launch_count()
-    if use_graphs:
-        pool = torch.cuda.graph_pool_handle()
-        for s in range(K):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, pool=pool, capture_error_mode="relaxed"):
-                step(W + s)
-            graphs.append(g)
-        torch.cuda.synchronize()
-    launches = lib.se_kernel_launch_count() - launches0  # kernels captured (graphs) ...
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        torch.cuda.synchronize()
-        barrier(world)
-        clocks.mark_start()
-        start.record()
-        for s in range(K):
-            if use_graphs:
-                graphs[s].replay()
-            else:
-                step(W + s)
-        end.record()
-        torch.cuda.synchronize()
-        clocks.mark_end()
-        barrier(world)
-    if not use_graphs:
-        launches = lib.se_kernel_launch_count() - launches0  # ... or launched eagerly
-    store.profile(False)
-    elapsed = max_over_ranks(start.elapsed_time(end) / 1e3, world)
+
+    def timed_pass(first, profiled):
+        store.profile(profiled)
+        graphs = []
+        launches0 = lib.se_kernel_launch_count()
+        if use_graphs:
+            pool = torch.cuda.graph_pool_handle()
+            for s in range(K):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=pool, capture_error_mode="relaxed"):
+                    step(first + s)
+                graphs.append(g)
+            torch.cuda.synchronize()
+        captured = lib.se_kernel_launch_count() - launches0
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            torch.cuda.synchronize()
+            barrier(world)
+            clocks.mark_start()
+            start.record()
+            for s in range(K):
+                if use_graphs:
+                    graphs[s].replay()
+                else:
+                    step(first + s)
+            end.record()
+            torch.cuda.synchronize()
+            clocks.mark_end()
+            barrier(world)
+        launches = captured if use_graphs else lib.se_kernel_launch_count() - launches0
+        store.profile(False)
+        del graphs
+        return max_over_ranks(start.elapsed_time(end) / 1e3, world), launches, clocks
+
+    elapsed, launches, clocks = timed_pass(W, False)
     value = world * BATCH * K / elapsed
+    elapsed_prof, _, _ = timed_pass(W + K, True)
 
     # Per-kernel device time inside the timed region.
     names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
@@ -402,8 +410,9 @@ def run_ours(args):
                                "eps 1e-8, init_acc 0.1), hash partitioner",
                    "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
                    "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
-        "timing": "CUDA graph replay per step (captured from the public API calls)" if use_graphs
-                  else "eager API calls",
+        "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
+                   else "eager API calls"),
+        "profiled_pass_ms_per_step": elapsed_prof / K * 1e3,
         "roofline": roofline, "step_roofline": step_roof, "kernels": kern,
         "e2e": e2e, "clocks": clocks.summary(), "gpu_launches": int(launches),
     }

@@ -202,12 +202,18 @@ k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_coun
 // scaled value rounded to the gradient dtype.
 template <int VEC>
 __global__ void __launch_bounds__(256)
-k_accumulate(const void *__restrict__ keys, int kdt, size_t n, const void *__restrict__ grads,
+k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n, const void *__restrict__ grads,
              int gdt, uint32_t dim, float scale, float maxv, unsigned long long *__restrict__ pkeys,
-             void *__restrict__ pgrads, uint32_t *status) {
+             uint32_t *__restrict__ prows, void *__restrict__ pgrads, uint32_t *status) {
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (size_t i = tid; i < n; i += stride) pkeys[i] = load_key(keys, kdt, i);
+  // Keys and their rows (the directory probe overlaps the gradient copy; a
+  // key absent now is probed again by optimizer_step).
+  for (size_t i = tid; i < n; i += stride) {
+    const uint64_t key = load_key(keys, kdt, i);
+    pkeys[i] = key;
+    prows[i] = dir_find<false>(d, key);
+  }
   const size_t chunks = n * dim / VEC;
   bool bad = false;
   for (size_t c = tid; c < chunks; c += stride) {
@@ -242,14 +248,28 @@ struct OptSpec {
 //            simd_cut, compiled scalar tail above it.
 //   Adagrad: no reference counterpart; acc = fma(g, g, acc),
 //            p = fma(-lr, g / (sqrt(acc) + eps), p).
+// Parameters and optimizer state of VEC elements of one row, loaded ahead of
+// the gradient reduction so their latency overlaps it.
+template <int VEC> struct RowState {
+  float p[VEC], s0[VEC], s1[VEC];
+};
+
 template <int VEC>
-__device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, const OptSpec &o,
-                                            uint32_t t, uint32_t e, const float (&gsum)[VEC]) {
-  float g[VEC], p[VEC];
+__device__ __forceinline__ void load_state(const Layout &L, const uint8_t *slab, const OptSpec &o, uint32_t e,
+                                           RowState<VEC> &r) {
+  ldv<VEC>(slab, L.pdt, e, r.p);
+  if (o.kind == SE_OPT_ADAGRAD || o.kind == SE_OPT_ADAM) ldv<VEC>(slab + L.state0, L.odt, e, r.s0);
+  if (o.kind == SE_OPT_ADAM) ldv<VEC>(slab + L.state1, L.odt, e, r.s1);
+}
+
+template <int VEC>
+__device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, const OptSpec &o, uint32_t t,
+                                             uint32_t e, const float (&gsum)[VEC], RowState<VEC> &r) {
+  float g[VEC];
+  float (&p)[VEC] = r.p;
   // GradientBatchView::assign (gradient_accumulator.hpp:38-53): g * scale / N -> ParamT.
 #pragma unroll
   for (int j = 0; j < VEC; ++j) g[j] = o.raw ? gsum[j] : round_to(L.pdt, __fmul_rn(gsum[j], o.factor));
-  ldv<VEC>(slab, L.pdt, e, p);
   if (o.kind == SE_OPT_SGD) {
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
@@ -257,8 +277,7 @@ __device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, cons
       p[j] = __fmaf_rn(-o.lr, gg, p[j]);
     }
   } else if (o.kind == SE_OPT_ADAGRAD) {
-    float a[VEC];
-    ldv<VEC>(slab + L.state0, L.odt, e, a);
+    float (&a)[VEC] = r.s0;
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       float gg = g[j];
@@ -269,9 +288,9 @@ __device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, cons
     }
     stv<VEC>(slab + L.state0, L.odt, e, a);
   } else if (o.kind == SE_OPT_ADAM) {
-    float m[VEC], v[VEC], ms[VEC], vs[VEC];
-    ldv<VEC>(slab + L.state0, L.odt, e, m);
-    ldv<VEC>(slab + L.state1, L.odt, e, v);
+    const float (&m)[VEC] = r.s0;
+    const float (&v)[VEC] = r.s1;
+    float ms[VEC], vs[VEC];
     const float bc1 = o.bc[2 * t], bc2 = o.bc[2 * t + 1];
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
@@ -296,26 +315,29 @@ __device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, cons
   stv<VEC>(slab, L.pdt, e, p);
 }
 
+template <int VEC>
+__device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, const OptSpec &o,
+                                            uint32_t t, uint32_t e, const float (&gsum)[VEC]) {
+  RowState<VEC> r;
+  load_state<VEC>(L, slab, o, e, r);
+  apply_loaded<VEC>(L, slab, o, t, e, gsum, r);
+}
+
 // Adds the gradient rows spos[k0..k1) (in order) into acc, rounding to the
 // gradient dtype after each add like TransientArena's simd_accumulate
-// (memory_ops.hpp:37-70). Loads run four rows ahead of the adds.
-template <int VEC>
+// (memory_ops.hpp:37-70). Loads run eight rows ahead of the adds.
+template <int VEC, int AHEAD = 8>
 __device__ __forceinline__ void sum_rows(const void *pgrads, int gdt, uint32_t dim, const uint32_t *spos,
                                          uint32_t k0, uint32_t k1, uint32_t e, float (&acc)[VEC]) {
   uint32_t k = k0;
-  for (; k + 4 <= k1; k += 4) {
-    float g0[VEC], g1[VEC], g2[VEC], g3[VEC];
-    ldv<VEC>(pgrads, gdt, size_t(spos[k]) * dim + e, g0);
-    ldv<VEC>(pgrads, gdt, size_t(spos[k + 1]) * dim + e, g1);
-    ldv<VEC>(pgrads, gdt, size_t(spos[k + 2]) * dim + e, g2);
-    ldv<VEC>(pgrads, gdt, size_t(spos[k + 3]) * dim + e, g3);
+  for (; k + AHEAD <= k1; k += AHEAD) {
+    float g[AHEAD][VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
-      acc[j] = round_to(gdt, __fadd_rn(acc[j], g1[j]));
-      acc[j] = round_to(gdt, __fadd_rn(acc[j], g2[j]));
-      acc[j] = round_to(gdt, __fadd_rn(acc[j], g3[j]));
-    }
+    for (int u = 0; u < AHEAD; ++u) ldv<VEC>(pgrads, gdt, size_t(spos[k + u]) * dim + e, g[u]);
+#pragma unroll
+    for (int u = 0; u < AHEAD; ++u)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], g[u][j]));
   }
   for (; k < k1; ++k) {
     float g0[VEC];
@@ -344,13 +366,14 @@ struct GroupWs {
   uint32_t *seg_fill;  // [P] placement counters (all zero between steps)
   uint32_t *pos;       // [P] entry positions grouped by segment
   uint4 *items;        // work items of k_group_hot: (segment, part, parts, first item)
+  uint32_t *mid;       // [P] segments of LANES+1 .. kApplySlots*LANES rows
   float *partials;     // [items][dim] partial sums of multi-part segments
-  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items
+  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] mid segments
 };
 
-// Phase 1: row of every entry (absent keys dropped and counted,
-// hogwild_embedding_store.hpp:1942-1952); per-row counts; the first entry to
-// count a row registers it as a new segment.
+// Phase 1: row of every entry (probed at accumulate time; absent keys are
+// probed again, then dropped and counted, hogwild_embedding_store.hpp:1942-1952);
+// per-row counts; the first entry to count a row registers it as a new segment.
 __global__ void __launch_bounds__(256)
 k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t count, GroupWs w,
               unsigned long long *dropped) {
@@ -362,8 +385,11 @@ k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t coun
   const uint32_t lane = threadIdx.x & 31u;
   uint32_t row = kNoRow;
   if (i < count) {
-    row = dir_find<false>(d, pkeys[i]);
-    w.rows[i] = row;
+    row = w.rows[i];  // probed by accumulate_gradients
+    if (row == kNoRow) {
+      row = dir_find<false>(d, pkeys[i]);  // inserted since?
+      if (row != kNoRow) w.rows[i] = row;
+    }
   }
   const unsigned absent = __ballot_sync(0xffffffffu, i < count && row == kNoRow);
   if (lane == 0 && absent) atomicAdd(dropped, (unsigned long long)__popc(absent));
@@ -428,22 +454,78 @@ constexpr uint32_t kPartEntries = 512;       // target rows per k_group_hot work
 constexpr uint32_t kHotWindowBits = 1u << 17;  // positions per bitmap window
 constexpr uint32_t kRoundEntries = 2048;     // rows compacted per round
 
-// Phase 4: one group per segment of at most LANES rows: its positions are
-// ranked inside the group, summed serially in arrival order and the
-// optimizer is applied. Larger segments go to k_group_block.
+// Sums a segment of at most kApplySlots * LANES rows in the reference's
+// order and applies the optimizer, by one group of LANES lanes: the group
+// ranks the positions (arrival order) into `ord` (shared memory), and loads
+// the row's parameters and state before the sum so both latencies overlap.
+constexpr int kApplySlots = 4;
+
+template <int LANES, int VEC, int SLOTS, int AHEAD>
+__device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, const OptSpec &o, int gdt,
+                                              const void *pgrads, const GroupWs &w, uint32_t s, uint32_t cnt,
+                                              uint32_t off, uint32_t row, uint32_t lane, unsigned mask,
+                                              uint32_t *ord) {
+  uint8_t *slab = slabs + size_t(row) * L.stride;
+  const uint32_t e0 = lane * VEC;
+  RowState<VEC> rs;
+  if (e0 < L.dim) load_state<VEC>(L, slab, o, e0, rs);
+  const uint32_t nslots = (cnt + LANES - 1) / LANES;
+  uint32_t p[SLOTS], rank[SLOTS];
+#pragma unroll
+  for (int j = 0; j < SLOTS; ++j) {
+    const uint32_t idx = lane + uint32_t(j) * LANES;
+    p[j] = idx < cnt ? w.pos[off + idx] : 0xffffffffu;
+    rank[j] = 0;
+  }
+#pragma unroll
+  for (int jj = 0; jj < SLOTS; ++jj) {
+    if (uint32_t(jj) < nslots) {
+      for (int q = 0; q < LANES; ++q) {
+        const uint32_t v = __shfl_sync(mask, p[jj], q, LANES);
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) rank[j] += v < p[j] ? 1u : 0u;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < SLOTS; ++j)
+    if (lane + uint32_t(j) * LANES < cnt) ord[rank[j]] = p[j];
+  __syncwarp(mask);
+  uint32_t step = 0;
+  if (o.kind == SE_OPT_ADAM) {
+    if (lane == 0) step = next_step(L, slab);
+    step = __shfl_sync(mask, step, 0, LANES);
+  }
+  for (uint32_t e = e0; e < L.dim; e += LANES * VEC) {
+    float acc[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
+    sum_rows<VEC, AHEAD>(pgrads, gdt, L.dim, ord, 0, cnt, e, acc);
+    if (e == e0) apply_loaded<VEC>(L, slab, o, step, e, acc, rs);
+    else apply_chunk<VEC>(L, slab, o, step, e, acc);
+  }
+  __syncwarp(mask);
+}
+
+// Phase 4: one group per segment of at most LANES rows (the bulk of the
+// keys). Segments of up to kApplySlots * LANES rows are listed for the
+// group pass of k_group_hot, larger ones become its block work items.
 template <int LANES, int VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, uint32_t count) {
+  constexpr int GPB = 256 / LANES;
+  __shared__ uint32_t s_ord[GPB][LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
+  const uint32_t gib = threadIdx.x / LANES;
   const unsigned mask = group_mask<LANES>();
   const uint32_t nseg = w.ctr[0];
   const bool poisoned = *o.poison != 0u;
   for (size_t s = t / LANES; s < nseg; s += groups) {
-    const uint32_t cnt = w.seg_cnt[s];
-    if (cnt > LANES) {
+    const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
+    if (cnt > uint32_t(kApplySlots * LANES)) {
       if (lane == 0) {
         // Work items of k_group_hot: windows of the batch's positions.
         const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
@@ -452,55 +534,13 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
       }
       continue;
     }
-    const uint32_t off = w.seg_off[s], row = w.seg_row[s];
-    const uint32_t p = lane < cnt ? w.pos[off + lane] : 0xffffffffu;
-    uint32_t rank = 0;
-    for (int j = 0; j < LANES; ++j) rank += __shfl_sync(mask, p, j, LANES) < p ? 1u : 0u;
-    // ord[k] = position of rank k (arrival order); group lanes only.
-    const int first_lane = int(threadIdx.x & 31u) & ~(LANES - 1);
-    uint32_t ord[LANES];
-#pragma unroll
-    for (int k = 0; k < LANES; ++k) {
-      const unsigned hit = __ballot_sync(mask, lane < cnt && rank == uint32_t(k));
-      ord[k] = __shfl_sync(mask, p, hit ? __ffs(hit) - 1 : first_lane);
+    if (cnt > uint32_t(LANES)) {
+      if (lane == 0) w.mid[atomicAdd(&w.ctr[3], 1u)] = uint32_t(s);
+      continue;
     }
-    uint8_t *slab = slabs + size_t(row) * L.stride;
-    uint32_t step = 0;
-    if (poisoned || cnt == 0) {
-      // a batch of this window failed validation: nothing is applied
-    } else {
-    if (o.kind == SE_OPT_ADAM) {
-      if (lane == 0) step = next_step(L, slab);
-      step = __shfl_sync(mask, step, 0, LANES);
-    }
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
-      float acc[VEC];
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
-      uint32_t k = 0;
-      for (; k + 4 <= cnt; k += 4) {
-        float g0[VEC], g1[VEC], g2[VEC], g3[VEC];
-        ldv<VEC>(pgrads, gdt, size_t(ord[k]) * L.dim + e, g0);
-        ldv<VEC>(pgrads, gdt, size_t(ord[k + 1]) * L.dim + e, g1);
-        ldv<VEC>(pgrads, gdt, size_t(ord[k + 2]) * L.dim + e, g2);
-        ldv<VEC>(pgrads, gdt, size_t(ord[k + 3]) * L.dim + e, g3);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
-          acc[j] = round_to(gdt, __fadd_rn(acc[j], g1[j]));
-          acc[j] = round_to(gdt, __fadd_rn(acc[j], g2[j]));
-          acc[j] = round_to(gdt, __fadd_rn(acc[j], g3[j]));
-        }
-      }
-      for (; k < cnt; ++k) {
-        float g0[VEC];
-        ldv<VEC>(pgrads, gdt, size_t(ord[k]) * L.dim + e, g0);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], g0[j]));
-      }
-      apply_chunk<VEC>(L, slab, o, step, e, acc);
-    }
-    }
+    if (cnt > 0 && !poisoned)
+      group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
+                                      s_ord[gib]);
     if (lane == 0) {
       w.row_cnt[row] = 0u;
       w.seg_fill[s] = 0u;
@@ -508,15 +548,15 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
   }
 }
 
-// Phase 5: segments of more than LANES rows. Each segment is cut into parts
+// Phase 5: segments of more than kApplySlots * LANES rows. Each segment is cut into parts
 // by windows of batch positions; one 1024-thread block per part finds the
 // segment's rows inside its window in arrival order (bitmap over the
 // window), reduces them, and either applies the optimizer (one part) or
 // leaves a partial sum for the last part to finish, which adds the partial
 // sums in window order. A single-part segment of at most kSerialMax rows is
 // summed serially (the reference's order); larger ones in runs of
-// 1024/LANES groups whose sums are added in run order. Everything is fixed by
-// the shapes, so results are deterministic.
+// 1024/LANES groups whose sums are added by a fixed pairwise tree. Everything
+// is fixed by the shapes, so results are deterministic.
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
@@ -589,21 +629,28 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
         }
         const uint32_t n = min(total - r0, kRoundEntries);
         if (serial) {
-          if (grp == 0 && e < L.dim) sum_rows<VEC>(pgrads, gdt, L.dim, s_pos, 0, n, e, acc);
+          if (grp == 0 && e < L.dim) sum_rows<VEC, 4>(pgrads, gdt, L.dim, s_pos, 0, n, e, acc);
         } else {
           const uint32_t per = (n + NG - 1) / NG;
           const uint32_t k0 = min(grp * per, n), k1 = min(k0 + per, n);
           float a[VEC];
 #pragma unroll
           for (int j = 0; j < VEC; ++j) a[j] = 0.0f;
-          if (e < L.dim) sum_rows<VEC>(pgrads, gdt, L.dim, s_pos, k0, k1, e, a);
+          if (e < L.dim) sum_rows<VEC, 4>(pgrads, gdt, L.dim, s_pos, k0, k1, e, a);
 #pragma unroll
           for (int j = 0; j < VEC; ++j) part[grp][lane][j] = a[j];
           __syncthreads();
-          if (grp == 0)
-            for (int g = 0; g < NG; ++g)
+          // fixed pairwise tree over the runs, then into the window's sum
+          for (int half = NG / 2; half > 0; half >>= 1) {
+            if (int(grp) < half)
 #pragma unroll
-              for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], part[g][lane][j]));
+              for (int j = 0; j < VEC; ++j)
+                part[grp][lane][j] = round_to(gdt, __fadd_rn(part[grp][lane][j], part[grp + half][lane][j]));
+            __syncthreads();
+          }
+          if (grp == 0)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], part[0][lane][j]));
           __syncthreads();
         }
       }
@@ -647,6 +694,20 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
       w.seg_fill[s] = 0u;
     }
     __syncthreads();
+  }
+  // Group pass: segments of LANES+1 .. kApplySlots*LANES rows, one group each.
+  const uint32_t nmid = w.ctr[3];
+  const unsigned mask = group_mask<LANES>();
+  uint32_t *ord = reinterpret_cast<uint32_t *>(bitmap) + grp * (kApplySlots * LANES);
+  for (uint32_t m = blockIdx.x * NG + grp; m < nmid; m += gridDim.x * NG) {
+    const uint32_t s = w.mid[m];
+    const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
+    if (!poisoned)
+      group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, s, cnt, off, row, lane, mask, ord);
+    if (lane == 0) {
+      w.row_cnt[row] = 0u;
+      w.seg_fill[s] = 0u;
+    }
   }
 }
 
@@ -753,12 +814,13 @@ struct Table {
   uint32_t *ctr = nullptr;
   // pending gradients
   unsigned long long *pkeys = nullptr;
+  uint32_t *prows = nullptr;  // row of each pending key at accumulate time
   uint8_t *pgrads = nullptr;
   uint64_t pcap = 0, pcount = 0;
   // per-row grouping counters of optimizer_step (capacity entries each)
   uint32_t *row_cnt = nullptr, *row_seg = nullptr;
   // step and insert work buffers
-  Scratch<uint32_t> g_rows, g_seg_row, g_seg_cnt, g_seg_off, g_seg_fill, g_pos, def_pos;
+  Scratch<uint32_t> g_seg_row, g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_mid, def_pos;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -770,6 +832,7 @@ struct Table {
     dfree(slabs);
     dfree(ctr);
     dfree(pkeys);
+    dfree(prows);
     dfree(pgrads);
     dfree(row_cnt);
     dfree(row_seg);
@@ -953,16 +1016,20 @@ struct StoreImpl {
     const uint64_t ncap = std::max<uint64_t>(need, std::max<uint64_t>(t.pcap * 2, 1024));
     const size_t gb = size_t(t.dim) * value_bytes(cfg.gradient_dtype);
     auto *nk = dalloc<unsigned long long>(ncap);
+    auto *nr = dalloc<uint32_t>(ncap);
     auto *ng = dalloc<uint8_t>(size_t(ncap) * gb);
     if (t.pcount) {
       cuda_check(cudaMemcpyAsync(nk, t.pkeys, t.pcount * 8, cudaMemcpyDeviceToDevice, st), "grow pending");
+      cuda_check(cudaMemcpyAsync(nr, t.prows, t.pcount * 4, cudaMemcpyDeviceToDevice, st), "grow pending");
       cuda_check(cudaMemcpyAsync(ng, t.pgrads, size_t(t.pcount) * gb, cudaMemcpyDeviceToDevice, st),
                  "grow pending");
     }
     cuda_check(cudaStreamSynchronize(st), "sync");
     dfree(t.pkeys);
+    dfree(t.prows);
     dfree(t.pgrads);
     t.pkeys = nk;
+    t.prows = nr;
     t.pgrads = ng;
     t.pcap = ncap;
   }
@@ -1127,13 +1194,13 @@ struct StoreImpl {
       const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 16);
       uint8_t *dst = t.pgrads + size_t(t.pcount) * size_t(dim) * gb;
       if (vec4)
-        k_accumulate<4><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv,
-                                              t.pkeys + t.pcount, dst, status_word);
+        k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys + t.pcount,
+                                              t.prows + t.pcount, dst, status_word);
       else
-        k_accumulate<1><<<grid, 256, 0, st>>>(dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv,
-                                              t.pkeys + t.pcount, dst, status_word);
+        k_accumulate<1><<<grid, 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys + t.pcount,
+                                              t.prows + t.pcount, dst, status_word);
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1171,7 +1238,7 @@ struct StoreImpl {
   void step_table(Table &t, size_t nsteps, cudaStream_t st) {
     const uint32_t P = uint32_t(t.pcount);
     GroupWs w{};
-    w.rows = t.g_rows.get(P);
+    w.rows = t.prows;
     w.row_cnt = t.row_cnt;
     w.row_seg = t.row_seg;
     w.seg_row = t.g_seg_row.get(P);
@@ -1191,6 +1258,7 @@ struct StoreImpl {
     const uint64_t min_parts = (uint64_t(P) + kHotWindowBits - 1) / kHotWindowBits;
     const uint64_t max_items = uint64_t(P) / kPartEntries + 1 + (uint64_t(P) / 5 + 1) * (min_parts + 1);
     w.items = reinterpret_cast<uint4 *>(t.g_items.get(max_items));
+    w.mid = t.g_mid.get(P);
     w.partials = t.g_partials.get(max_items * uint64_t(t.dim));
     w.ctr = t.ctr + kCtrGroup;
     cuda_check(cudaMemsetAsync(w.ctr, 0, 16, st), "memset group counters");
@@ -1232,7 +1300,7 @@ struct StoreImpl {
       constexpr int VC = decltype(vec_tag)::value;
       {
         Prof pr(this, "k_group_apply", st);
-        k_group_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+        k_group_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st>>>(
             t.L, t.slabs, o, gdt, t.pgrads, w, P);
         launched("k_group_apply");
       }
