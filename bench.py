@@ -9,7 +9,8 @@ Workload ("train step", one step per data-parallel batch, per GPU):
   never-seen keys inserted on miss; gradients N(0, sigma=1e-3) fp32 per row;
   step = lookup_or_insert -> accumulate_gradients -> optimizer_step(1) with
   Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1); keys sharded over
-  the GPUs by the hash partitioner (N > 1: all-to-all of keys, rows, grads).
+  the GPUs by the hash partitioner (N > 1: keys, rows and gradients cross
+  NVLink through the library's peer-memory exchange kernels).
   Weak scaling: 65,536 keys per GPU per step.
 
 Also reported (rank 0, 1 GPU): the forward-lookup workload - dim-32 fp32
@@ -57,6 +58,8 @@ def args_parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-forward", action="store_true")
     p.add_argument("--eager", action="store_true", help="time eager API calls instead of CUDA graphs")
+    p.add_argument("--transport", choices=["p2p", "collective"], default="p2p",
+                   help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
     return p.parse_args()
 
 
@@ -231,9 +234,10 @@ def run_ours(args):
     wl = TrainWorkload(num_keys=args.num_keys, batch=BATCH, dim=DIM, rank=rank)
     warm = wl.warm_keys()
     mine = owned_keys(warm, world, rank)
-    # Room for every row the run can create, plus the host-side upper bound
-    # the store reserves per insert call while graphs are captured.
-    cap = int(len(mine) + (W + 4 * K + 8) * BATCH)
+    # Room for every row the run can create (5 % new keys per batch, twice
+    # over), plus the headroom an insert call checks for while it is being
+    # captured: one batch from every rank.
+    cap = int(len(mine) + (W + 4 * K + 8) * BATCH * 0.1 + (world + 1) * BATCH)
     store = se.EmbeddingStore(
         se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap),
         optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
@@ -244,7 +248,8 @@ def run_ours(args):
     if world > 1:
         from sparse_embedding_b200.sharded import ShardedEmbeddingStore
 
-        api = ShardedEmbeddingStore(store, "sparse_embedding.hash")
+        api = ShardedEmbeddingStore(store, "sparse_embedding.hash", transport=args.transport,
+                                    max_keys_per_rank=BATCH)
 
     keys_np, _ = wl.make_batches(W + 2 * K, start_step=0)
     keys_d = torch.from_numpy(keys_np).cuda()
@@ -264,14 +269,15 @@ def run_ours(args):
     barrier(world)
 
     lib = N.lib()
-    # One GPU: every timed step is a CUDA graph captured from the same API
-    # calls (one graph per batch), so the timed region holds the kernels and
-    # not the Python launch path. Several GPUs: eager calls (the exchange
-    # needs host-side splits). Two timed passes over different batches:
+    # Every timed step is a CUDA graph captured from the same API calls (one
+    # graph per batch), so the timed region holds the kernels and not the
+    # Python launch path; on several GPUs the peer-memory exchange kernels
+    # synchronise the ranks inside the graphs. The NCCL transport needs
+    # host-side splits and runs eager. Two timed passes over different batches:
     # pass 1 gives `value` (no instrumentation); pass 2 repeats it with the
     # store's CUDA events around every kernel, on the launching stream, for
     # the per-kernel durations of the roofline.
-    use_graphs = world == 1 and not args.eager
+    use_graphs = not args.eager and (world == 1 or args.transport == "p2p")
 
     def timed_pass(first, profiled):
         store.profile(profiled)
@@ -313,6 +319,8 @@ def run_ours(args):
     # Per-kernel device time inside the timed region.
     names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
              "k_group_place", "k_group_apply", "k_group_hot"]
+    if world > 1 and args.transport == "p2p":
+        names += ["k_ex_scatter", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_grads"]
     times = {}
     for nm in names:
         ms, cnt = store.profile_read(nm)
@@ -330,7 +338,7 @@ def run_ours(args):
     mean_u = sum(uniq) / len(uniq)
     rows_per_owner = BATCH  # weak scaling: each owner receives ~BATCH rows per step
     units = {
-        "k_lookup_or_insert": (["k_lookup_or_insert"],
+        "k_lookup_or_insert": (["k_lookup_or_insert" if "k_ex_owner" not in names else "k_ex_owner"],
                                rows_per_owner * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R),
         "k_accumulate": (["k_accumulate"], rows_per_owner * 2 * (KEY_BYTES + R)),
         "k_group_apply+k_group_hot": (["k_group_apply", "k_group_hot"], mean_u * 4 * R + rows_per_owner * R),
@@ -409,6 +417,7 @@ def run_ours(args):
                                "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
                                "eps 1e-8, init_acc 0.1), hash partitioner",
                    "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
+                   "transport": (args.transport if world > 1 else "none"),
                    "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
         "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
                    else "eager API calls"),
@@ -423,6 +432,7 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
 
+        api.close()
         dist.destroy_process_group()
     return result if rank == 0 else None
 

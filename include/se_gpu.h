@@ -194,6 +194,52 @@ int se_partition_route_noalloc(int32_t kind, uint32_t num_partitions, int32_t ke
 int se_permute_rows(const void *in_rows, void *out_rows, const uint32_t *positions, size_t num_rows,
                     size_t row_bytes, int32_t scatter, int32_t device, void *stream);
 
+/*
+ * Peer-memory exchange of a key-sharded store: one process per GPU, rank r
+ * owns the keys partitioner `kind` maps to r (no reference counterpart: the
+ * reference leaves cross-worker routing to its caller,
+ * sparse_embedding/partitioner.py:84-100). Each rank's batch goes to the
+ * owners and back through CUDA IPC mappings of every rank's exchange arena
+ * (NVLink peer stores, no collective library); the owner applies
+ * lookup_or_insert / forward_lookup / accumulate_gradients to its local store
+ * with the received keys in sender-rank order, so results equal one store fed
+ * the concatenation of the ranks' batches. optimizer_step stays per-rank
+ * (se_optimizer_step on the local store).
+ *
+ * Collective use: every rank makes the same sequence of exchange calls on one
+ * stream each. Waits inside the kernels give up after timeout_ms and mark the
+ * exchange failed; se_exchange_check raises that (SE_ERR_RUNTIME) and the
+ * exchange must then be recreated. Device pointers only; calls are
+ * asynchronous on `stream`.
+ */
+typedef struct se_exchange se_exchange;
+/* This rank's end over `store` (which must outlive it) for rows of length
+ * dim: world_size <= 64 ranks, at most max_keys_per_rank keys per rank per
+ * call. Allocates the arena on the store's device. */
+int se_exchange_create(se_store *store, int32_t partitioner_kind, uint32_t world_size, uint32_t rank,
+                       uint64_t max_keys_per_rank, int64_t dim, uint32_t timeout_ms, se_exchange **out);
+/* Writes this rank's arena handle (a CUDA IPC handle, 64 bytes) to handle_out. */
+int se_exchange_handle(se_exchange *ex, void *handle_out, size_t handle_bytes);
+/* Maps every peer's arena: handles holds world_size handles in rank order
+ * (this rank's entry is ignored). Call once, after every rank created its end. */
+int se_exchange_connect(se_exchange *ex, const void *handles, size_t handles_bytes);
+/* Connects the ends of all ranks when they live in this one process
+ * (exchanges[r] is rank r; count == world_size). */
+int se_exchange_connect_local(se_exchange *const *exchanges, uint32_t count);
+/* Rows (value dtype, n x dim, batch order) of this rank's keys from their
+ * owners: insert != 0 is lookup_or_insert (hogwild_embedding_store.hpp:4925-4980),
+ * insert == 0 is forward_lookup with zero rows for absent keys (4406-4534). */
+int se_exchange_lookup(se_exchange *ex, const void *keys, size_t n, void *out, int32_t insert, void *stream);
+/* accumulate_gradients (hogwild_embedding_store.hpp:4536-4680) at the owners:
+ * grads holds n x dim values of the gradient dtype. Device-side validation
+ * (see se_accumulate_gradients with device inputs). */
+int se_exchange_accumulate(se_exchange *ex, const void *keys, size_t n, const void *grads, void *stream);
+/* Synchronises `stream`; raises a timed-out wait, then the owner table's errors. */
+int se_exchange_check(se_exchange *ex, void *stream);
+/* Frees this rank's end. Call only after every rank finished its last
+ * exchange call (peers store into this arena). */
+int se_exchange_destroy(se_exchange *ex);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -94,6 +94,14 @@ _SIGNATURES = {
     "se_partition_route": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],
     "se_partition_route_noalloc": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],
     "se_permute_rows": [_vp, _vp, _vp, _sz, _sz, _i32, _i32, _vp],
+    "se_exchange_create": [_vp, _i32, _u32, _u32, _u64, _i64, _u32, C.POINTER(_vp)],
+    "se_exchange_handle": [_vp, _vp, _sz],
+    "se_exchange_connect": [_vp, _vp, _sz],
+    "se_exchange_connect_local": [C.POINTER(_vp), _u32],
+    "se_exchange_lookup": [_vp, _vp, _sz, _vp, _i32, _vp],
+    "se_exchange_accumulate": [_vp, _vp, _sz, _vp, _vp],
+    "se_exchange_check": [_vp, _vp],
+    "se_exchange_destroy": [_vp],
 }
 _RESTYPES = {"se_last_error": C.c_char_p, "se_version": C.c_char_p, "se_kernel_launch_count": _u64}
 

@@ -202,11 +202,19 @@ k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_coun
 // scaled value rounded to the gradient dtype.
 template <int VEC>
 __global__ void __launch_bounds__(256)
-k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n, const void *__restrict__ grads,
-             int gdt, uint32_t dim, float scale, float maxv, unsigned long long *__restrict__ pkeys,
-             uint32_t *__restrict__ prows, void *__restrict__ pgrads, uint32_t *status) {
+k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
+             const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
+             unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
+             void *__restrict__ pgrads_base, uint32_t *pending, uint32_t *done, uint32_t *status) {
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  // Rows are appended at the committed pending count; the batch size is the
+  // host's n_max or, for exchanged batches, a count in device memory.
+  const uint32_t base = *pending;
+  const size_t n = n_dev ? min(size_t(*n_dev), n_max) : n_max;
+  unsigned long long *pkeys = pkeys_base + base;
+  uint32_t *prows = prows_base + base;
+  void *pgrads = static_cast<uint8_t *>(pgrads_base) + size_t(base) * dim * (gdt == SE_FLOAT32 ? 4 : 2);
   // Keys and their rows (the directory probe overlaps the gradient copy; a
   // key absent now is probed again by optimizer_step).
   for (size_t i = tid; i < n; i += stride) {
@@ -229,6 +237,15 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n, const void
     stv<VEC>(pgrads, gdt, e, g);
   }
   if (bad) raise_status(status, kStatusBadGradient);
+  // The last block to finish commits the rows (every block has read `base`).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *pending = base + uint32_t(n);
+      *done = 0u;
+    }
+  }
 }
 
 struct OptSpec {
@@ -375,8 +392,9 @@ struct GroupWs {
 // probed again, then dropped and counted, hogwild_embedding_store.hpp:1942-1952);
 // per-row counts; the first entry to count a row registers it as a new segment.
 __global__ void __launch_bounds__(256)
-k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t count, GroupWs w,
+k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t *count_p, GroupWs w,
               unsigned long long *dropped) {
+  const uint32_t count = *count_p;
   __shared__ uint32_t s_rows[256];
   __shared__ uint32_t s_n, s_base;
   if (threadIdx.x == 0) s_n = 0;
@@ -428,7 +446,8 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
 }
 
 // Phase 3: every entry takes a slot of its segment (warp-aggregated).
-__global__ void __launch_bounds__(256) k_group_place(uint32_t count, GroupWs w) {
+__global__ void __launch_bounds__(256) k_group_place(const uint32_t *count_p, GroupWs w) {
+  const uint32_t count = *count_p;
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t row = i < count ? w.rows[i] : kNoRow;
@@ -513,7 +532,8 @@ __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, c
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 4)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
-              GroupWs w, uint32_t count) {
+              GroupWs w, const uint32_t *count_p) {
+  const uint32_t count = *count_p;
   constexpr int GPB = 256 / LANES;
   __shared__ uint32_t s_ord[GPB][LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -560,7 +580,8 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
-            GroupWs w, uint32_t count) {
+            GroupWs w, const uint32_t *count_p) {
+  const uint32_t count = *count_p;
   using Scan = cub::BlockScan<uint32_t, kBlockThreads>;
   constexpr int NG = kBlockThreads / LANES;
   constexpr uint32_t WPT = kHotWindowBits / 32 / kBlockThreads;  // bitmap words per thread
@@ -728,6 +749,12 @@ __global__ void k_find_rows(Dir d, const unsigned long long *keys, uint32_t n, u
   if (i < n) rows[i] = dir_find<true>(d, keys[i]);
 }
 
+}  // namespace se_gpu
+
+#include "se_exchange.cuh"
+
+namespace se_gpu {
+
 // ===========================================================================
 // Host side
 // ===========================================================================
@@ -796,6 +823,9 @@ enum Ctr : int {
   kCtrGradStatus = 13,  // gradient validation of the current accumulate call
   kCtrDropped = 8,      // u64 at words 8-9
   kCtrPoison = 10,      // sticky: a device-input gradient batch failed validation
+  kCtrPending = 11,     // pending gradient rows committed on the device
+  kCtrAccDone = 14,     // blocks of the running k_accumulate that have finished
+  kCtrPendingBackup = 15,
   kCtrWords = 16,
 };
 
@@ -811,6 +841,7 @@ struct Table {
   uint8_t *slabs = nullptr;
   uint64_t capacity = 0;
   uint64_t rows_bound = 0;  // upper bound of rows in use
+  bool bound_stale = false;  // graph-captured inserts may have added rows since
   uint32_t *ctr = nullptr;
   // pending gradients
   unsigned long long *pkeys = nullptr;
@@ -971,8 +1002,34 @@ struct StoreImpl {
     return used;
   }
 
+  static bool capturing(cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return cs == cudaStreamCaptureStatusActive;
+  }
+
   // Guarantees room for `extra` more rows in the arena and the directory.
+  // Under stream capture nothing can grow: the call only checks the room
+  // reserved beforehand. Replays of the captured graph do not come through
+  // here, so the rows they insert are bounded by the arena alone (the insert
+  // kernels report a full arena), and the next call outside capture re-reads
+  // the rows in use.
   void ensure_rows(Table &t, uint64_t extra, cudaStream_t st) {
+    if (capturing(st)) {
+      t.bound_stale = true;
+      const uint64_t need = t.rows_bound + extra;
+      if (need > t.capacity || need > uint64_t(double(t.nbuckets) * kMaxLoadPerBucket))
+        throw Error(SE_ERR_TABLE_FULL, "insert captured in a CUDA graph needs " + std::to_string(extra) +
+                                           " reserved rows; reserve capacity before capturing");
+      return;
+    }
+    if (t.bound_stale) {
+      t.rows_bound = read_rows_used(t, st);
+      t.bound_stale = false;
+    }
     uint64_t need = t.rows_bound + extra;
     const auto dir_limit = [&](uint64_t nb) { return uint64_t(double(nb) * kMaxLoadPerBucket); };
     if (need > t.capacity || need > dir_limit(t.nbuckets)) {
@@ -1168,6 +1225,14 @@ struct StoreImpl {
 
   void accumulate(const void *keys, size_t n, int64_t dim, const void *grads, void *sp) {
     std::lock_guard<std::mutex> lock(mu);
+    accumulate_locked(keys, n, nullptr, dim, grads, sp);
+  }
+
+  // n_dev: optional device count (<= n) of the rows to take, for batches
+  // whose size is only known on the device (exchanged batches); kdt: key
+  // dtype of `keys` when it differs from the store's (exchanged keys are u64).
+  void accumulate_locked(const void *keys, size_t n, const uint32_t *n_dev, int64_t dim, const void *grads,
+                         void *sp, int kdt = -1) {
     DeviceGuard dg(device);
     if (dim <= 0) throw std::invalid_argument("gradient row length must be positive");
     Table &t = table(dim);
@@ -1175,11 +1240,12 @@ struct StoreImpl {
     cudaStream_t st = pick(sp);
     ensure_pending(t, n, st);
     const size_t gb = value_bytes(cfg.gradient_dtype);
-    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    if (kdt < 0) kdt = cfg.key_dtype;
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(kdt), st);
     const void *dgrads = stage_in(stage_vals, grads, n * size_t(dim) * gb, st);
     const float maxv = std::min(host_dtype_max(cfg.gradient_dtype), host_dtype_max(cfg.value_dtype));
-    const bool vec4 = (n * size_t(dim)) % 4 == 0 && uintptr_t(dgrads) % 16 == 0 &&
-                      (size_t(t.pcount) * size_t(dim) * gb) % 16 == 0;
+    // dim % 4 == 0 keeps every appended row 16-byte (fp32) / 8-byte aligned.
+    const bool vec4 = dim % 4 == 0 && uintptr_t(dgrads) % 16 == 0;
     // Host inputs: validate_input semantics of the reference - the call waits
     // for its check and raises before anything is accumulated. Device inputs:
     // the check runs on the device without stalling the stream; a failing
@@ -1187,20 +1253,23 @@ struct StoreImpl {
     // error is raised by the next synchronising call.
     const bool device_inputs = dkeys == keys && dgrads == grads;
     uint32_t *status_word = t.ctr + (device_inputs ? kCtrPoison : kCtrGradStatus);
-    if (!device_inputs) cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+    if (!device_inputs) {
+      cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+      cuda_check(cudaMemcpyAsync(t.ctr + kCtrPendingBackup, t.ctr + kCtrPending, 4, cudaMemcpyDeviceToDevice, st),
+                 "pending backup");
+    }
     {
       Prof pr(this, "k_accumulate", st);
       const size_t chunks = n * size_t(dim) / (vec4 ? 4 : 1);
       const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 16);
-      uint8_t *dst = t.pgrads + size_t(t.pcount) * size_t(dim) * gb;
       if (vec4)
-        k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys + t.pcount,
-                                              t.prows + t.pcount, dst, status_word);
+        k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
+                                              t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word);
       else
-        k_accumulate<1><<<grid, 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys + t.pcount,
-                                              t.prows + t.pcount, dst, status_word);
+        k_accumulate<1><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
+                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
+                                              t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word);
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1209,10 +1278,13 @@ struct StoreImpl {
       cuda_check(cudaStreamSynchronize(st), "sync");
       if (status_host[0] & kStatusBadGradient) {
         cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+        cuda_check(cudaMemcpyAsync(t.ctr + kCtrPending, t.ctr + kCtrPendingBackup, 4, cudaMemcpyDeviceToDevice, st),
+                   "pending rollback");
+        cuda_check(cudaStreamSynchronize(st), "sync");
         throw std::overflow_error("gradient scale storage exceeds configured dtype");
       }
     }
-    t.pcount += n;
+    t.pcount += n;  // upper bound of the rows pending on the device
   }
 
   void optimizer_step(size_t nsteps, void *sp) {
@@ -1226,11 +1298,8 @@ struct StoreImpl {
     for (auto &tp : tables) {
       Table &t = *tp;
       if (t.pcount == 0) continue;
-      if (!apply) {
-        t.pcount = 0;
-        continue;
-      }
-      step_table(t, nsteps, st);
+      if (apply) step_table(t, nsteps, st);
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrPending, 0, 4, st), "pending clear");
       t.pcount = 0;
     }
   }
@@ -1266,7 +1335,7 @@ struct StoreImpl {
     const unsigned g = grid_for(P, 256);
     {
       Prof pr(this, "k_group_count", st);
-      k_group_count<<<g, 256, 0, st>>>(t.dir(), t.pkeys, P, w, dropped);
+      k_group_count<<<g, 256, 0, st>>>(t.dir(), t.pkeys, t.ctr + kCtrPending, w, dropped);
       launched("k_group_count");
     }
     {
@@ -1276,7 +1345,7 @@ struct StoreImpl {
     }
     {
       Prof pr(this, "k_group_place", st);
-      k_group_place<<<g, 256, 0, st>>>(P, w);
+      k_group_place<<<g, 256, 0, st>>>(t.ctr + kCtrPending, w);
       launched("k_group_place");
     }
     OptSpec o{};
@@ -1301,11 +1370,12 @@ struct StoreImpl {
       {
         Prof pr(this, "k_group_apply", st);
         k_group_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st>>>(
-            t.L, t.slabs, o, gdt, t.pgrads, w, P);
+            t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
         launched("k_group_apply");
       }
       Prof pr(this, "k_group_hot", st);
-      k_group_hot<LN, VC><<<148 * 2, kBlockThreads, 0, st>>>(t.L, t.slabs, o, gdt, t.pgrads, w, P);
+      k_group_hot<LN, VC><<<148 * 2, kBlockThreads, 0, st>>>(t.L, t.slabs, o, gdt, t.pgrads, w,
+                                                             t.ctr + kCtrPending);
       launched("k_group_hot");
     };
     auto by_lanes = [&](auto vec_tag) {
@@ -1358,6 +1428,288 @@ struct StoreImpl {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Peer-memory exchange (kernels in se_exchange.cuh)
+// ---------------------------------------------------------------------------
+
+constexpr size_t kIpcHandleBytes = sizeof(cudaIpcMemHandle_t);
+
+struct ExchangeImpl {
+  StoreImpl *store = nullptr;
+  int device = 0;
+  uint32_t W = 1, me = 0;
+  uint64_t M = 0;  // keys per rank per call
+  int64_t dim = 0;
+  PartSpec spec{};
+  uint8_t *arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<uint8_t *> peers;    // arena of every rank in this process's address space
+  std::vector<bool> opened;        // peers[r] came from cudaIpcOpenMemHandle
+  uint8_t **d_peers = nullptr;     // device copy of `peers`
+  ExView view{};
+  bool connected = false;
+  // route scratch of the forward and backward direction
+  uint32_t *route[2] = {nullptr, nullptr};
+  uint32_t tiles_cap = 0;
+  uint32_t *status_host = nullptr;  // pinned
+
+  ~ExchangeImpl() {
+    DeviceGuard dg(device);
+    cudaDeviceSynchronize();
+    for (uint32_t r = 0; r < peers.size(); ++r)
+      if (opened[r]) cudaIpcCloseMemHandle(peers[r]);
+    dfree(d_peers);
+    dfree(arena);
+    dfree(route[0]);
+    dfree(route[1]);
+    if (status_host) cudaFreeHost(status_host);
+  }
+
+  void create(StoreImpl *s, int kind, uint32_t world, uint32_t rank, uint64_t max_keys, int64_t row_dim,
+              uint32_t timeout_ms) {
+    if (world == 0 || world > kExMaxRanks) throw std::invalid_argument("world_size must be in [1, 64]");
+    if (rank >= world) throw std::invalid_argument("rank must be < world_size");
+    if (max_keys == 0 || max_keys > (1ull << 26)) throw std::invalid_argument("max_keys_per_rank must be in [1, 2^26]");
+    if (row_dim <= 0) throw std::invalid_argument("dim must be > 0");
+    if (timeout_ms == 0) throw std::invalid_argument("timeout_ms must be > 0");
+    store = s;
+    device = s->device;
+    s->table(row_dim);  // the dim must have a table
+    W = world;
+    me = rank;
+    M = max_keys;
+    dim = row_dim;
+    spec = make_spec(kind, world);
+    DeviceGuard dg(device);
+    const uint64_t WM = uint64_t(W) * M;
+    const uint32_t row_bytes = uint32_t(dim * int64_t(value_bytes(s->cfg.value_dtype)));
+    const uint32_t grad_bytes = uint32_t(dim * int64_t(value_bytes(s->cfg.gradient_dtype)));
+    auto up = [](uint64_t x) { return (x + 255u) & ~uint64_t(255u); };
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+      const uint64_t at = o;
+      o = up(o + bytes);
+      return at;
+    };
+    view.W = W;
+    view.me = me;
+    view.row_bytes = row_bytes;
+    view.grad_bytes = grad_bytes;
+    view.timeout_ns = uint64_t(timeout_ms) * 1000000ull;
+    view.o_flags = take(4ull * kExKinds * W);
+    view.o_epochs = take(4ull * kExKinds);
+    view.o_words = take(4ull * kExWords);
+    view.o_counts = take(4ull * W * W);
+    view.o_gcounts = take(4ull * W * W);
+    view.o_inkeys = take(8 * WM);
+    view.o_inpos = take(4 * WM);
+    view.o_gkeys = take(8 * WM);
+    view.o_ingrads = take(WM * grad_bytes);
+    view.o_rows = take(M * row_bytes);
+    arena_bytes = o;
+    arena = dalloc<uint8_t>(arena_bytes);
+    cuda_check(cudaMemset(arena, 0, arena_bytes), "memset exchange arena");
+    tiles_cap = uint32_t((M + kRouteTile - 1) / kRouteTile);
+    for (auto &r : route) r = dalloc<uint32_t>(2 * size_t(tiles_cap) * W + W);
+    d_peers = dalloc<uint8_t *>(W);
+    cuda_check(cudaMallocHost(&status_host, 16), "cudaMallocHost");
+    peers.assign(W, nullptr);
+    opened.assign(W, false);
+    peers[me] = arena;
+    cuda_check(cudaDeviceSynchronize(), "sync");
+  }
+
+  void handle(void *out, size_t bytes) const {
+    if (bytes < kIpcHandleBytes) throw std::invalid_argument("handle buffer is smaller than a CUDA IPC handle");
+    DeviceGuard dg(device);
+    cudaIpcMemHandle_t h;
+    cuda_check(cudaIpcGetMemHandle(&h, arena), "cudaIpcGetMemHandle");
+    std::memcpy(out, &h, kIpcHandleBytes);
+  }
+
+  void finish_connect() {
+    cuda_check(cudaMemcpy(d_peers, peers.data(), W * sizeof(uint8_t *), cudaMemcpyHostToDevice), "upload peers");
+    view.peer = d_peers;
+    connected = true;
+  }
+
+  // handles: one CUDA IPC handle per rank, rank order (own entry ignored).
+  void connect(const void *handles, size_t bytes) {
+    if (connected) throw std::invalid_argument("exchange is already connected");
+    if (bytes < kIpcHandleBytes * W) throw std::invalid_argument("need world_size IPC handles");
+    DeviceGuard dg(device);
+    for (uint32_t r = 0; r < W; ++r) {
+      if (r == me) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t *>(handles) + r * kIpcHandleBytes, kIpcHandleBytes);
+      void *p = nullptr;
+      cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+      peers[r] = static_cast<uint8_t *>(p);
+      opened[r] = true;
+    }
+    finish_connect();
+  }
+
+  void require_connected() const {
+    if (!connected) throw std::invalid_argument("exchange is not connected");
+  }
+
+  InitSpec init_spec() const {
+    const se_store_config &c = store->cfg;
+    return InitSpec{c.init_kind, c.init_min, c.init_max - c.init_min,
+                    c.optimizer_kind == SE_OPT_ADAGRAD ? c.initial_accumulator : 0.0f};
+  }
+
+  // Route of this rank's keys: per-tile counts, offsets and per-owner counts.
+  template <class K>
+  const uint32_t *run_route(const K *keys, size_t n, int dir, cudaStream_t st) {
+    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+    uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
+    uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
+    if (tiles) {
+      k_route_count<K><<<tiles, kRouteThreads, W * 4, st>>>(spec, keys, n, tile_counts);
+      launched("k_route_count");
+    }
+    k_route_scan<<<1, 1024, 0, st>>>(tile_counts, tiles, W, tile_offsets, counts);
+    launched("k_route_scan");
+    return counts;
+  }
+
+  void publish(int kind, const uint32_t *counts, cudaStream_t st) {
+    k_ex_publish<<<1, 32, 0, st>>>(view, kind, counts);
+    launched("k_ex_publish");
+  }
+
+  void check_batch(const void *keys, size_t n, const void *rows, const char *rows_name) const {
+    require_connected();
+    if (n > M) throw std::invalid_argument("batch exceeds the exchange's max_keys_per_rank");
+    if (n && (!is_device_ptr(keys) || !is_device_ptr(rows)))
+      throw std::invalid_argument(std::string("exchange takes device keys and ") + rows_name);
+  }
+
+  void forward(const void *keys, size_t n, void *out, bool insert, cudaStream_t st) {
+    check_batch(keys, n, out, "output rows");
+    std::lock_guard<std::mutex> lock(store->mu);
+    DeviceGuard dg(device);
+    Table &t = store->table(dim);
+    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+    dispatch_key(store->cfg.key_dtype, [&](auto tag) {
+      using K = decltype(tag);
+      const K *k = static_cast<const K *>(keys);
+      const uint32_t *counts = run_route<K>(k, n, 0, st);
+      publish(kExCounts, counts, st);
+      StoreImpl::Prof pr(store, "k_ex_scatter", st);
+      k_ex_scatter<K, false, uint4><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
+          spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr);
+      launched("k_ex_scatter");
+    });
+    publish(kExKeys, nullptr, st);
+    // owner side: at most W * M keys arrive
+    const uint64_t WM = uint64_t(W) * M;
+    if (insert) {
+      store->ensure_rows(t, WM, st);
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
+    }
+    uint32_t *def_idx = t.def_pos.get(WM);
+    unsigned long long *def_word = t.def_word.get(WM);
+    const InitSpec init = init_spec();
+    auto go = [&](auto lanes_tag, auto vec_tag) {
+      constexpr int LN = decltype(lanes_tag)::value;
+      constexpr int VC = decltype(vec_tag)::value;
+      const unsigned grid = grid_for(M * LN, 256, 148 * 16);
+      StoreImpl::Prof pr(store, "k_ex_owner", st);
+      if (insert) {
+        k_ex_owner<LN, VC, true><<<grid, 256, 0, st>>>(t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+                                                        init, view, t.ctr + kCtrDeferred, def_idx, def_word,
+                                                        t.ctr + kCtrStatus);
+        launched("k_ex_owner");
+        k_ex_owner_deferred<LN, VC><<<148 * 4, 256, 0, st>>>(t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
+                                                             def_word, t.ctr + kCtrStatus);
+        launched("k_ex_owner_deferred");
+      } else {
+        k_ex_owner<LN, VC, false><<<grid, 256, 0, st>>>(t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+                                                         init, view, nullptr, nullptr, nullptr,
+                                                         t.ctr + kCtrStatus);
+        launched("k_ex_owner");
+      }
+    };
+    auto by_lanes = [&](auto vec_tag) {
+      const uint32_t ln = t.vec == 4 ? t.lanes : pick_lanes(uint64_t(dim));
+      switch (ln) {
+      case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+      case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+      case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+      default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+      }
+    };
+    if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
+    else by_lanes(std::integral_constant<int, 1>{});
+    publish(kExRows, nullptr, st);
+    // requester side: this rank's rows, batch order
+    const size_t bytes = n * size_t(view.row_bytes);
+    const uintptr_t al = uintptr_t(out) | uintptr_t(bytes);
+    auto copy_out = [&](auto utag) {
+      using U = decltype(utag);
+      const size_t units = bytes / sizeof(U);
+      StoreImpl::Prof pr(store, "k_ex_rows_out", st);
+      k_ex_rows_out<U><<<grid_for(units, 256, 148 * 8), 256, 0, st>>>(view, static_cast<U *>(out), units);
+      launched("k_ex_rows_out");
+    };
+    if (al % 16 == 0) copy_out(uint4{});
+    else if (al % 4 == 0) copy_out(uint32_t{});
+    else copy_out(uint16_t{});
+  }
+
+  void backward(const void *keys, size_t n, const void *grads, cudaStream_t st) {
+    check_batch(keys, n, grads, "gradient rows");
+    std::lock_guard<std::mutex> lock(store->mu);
+    DeviceGuard dg(device);
+    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+    const uintptr_t al = uintptr_t(grads) | uintptr_t(view.grad_bytes);
+    dispatch_key(store->cfg.key_dtype, [&](auto tag) {
+      using K = decltype(tag);
+      const K *k = static_cast<const K *>(keys);
+      const uint32_t *counts = run_route<K>(k, n, 1, st);
+      publish(kExGCounts, counts, st);
+      auto scatter = [&](auto utag) {
+        using U = decltype(utag);
+        StoreImpl::Prof pr(store, "k_ex_scatter_grads", st);
+        k_ex_scatter<K, true, U><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
+            spec, view, k, n, route[1] + size_t(tiles_cap) * W, counts, static_cast<const uint8_t *>(grads));
+        launched("k_ex_scatter");
+      };
+      if (al % 16 == 0) scatter(uint4{});
+      else if (al % 4 == 0) scatter(uint32_t{});
+      else scatter(uint16_t{});
+    });
+    publish(kExGrads, nullptr, st);
+    k_ex_grads_total<<<1, 32, 0, st>>>(view);
+    launched("k_ex_grads_total");
+    const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
+    store->accumulate_locked(arena + view.o_gkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
+                             SE_KEY_UINT64);
+  }
+
+  // Waits for the stream; raises a timed-out wait, then the owner's table errors.
+  void check(cudaStream_t st) {
+    require_connected();
+    std::lock_guard<std::mutex> lock(store->mu);
+    DeviceGuard dg(device);
+    cuda_check(cudaMemcpyAsync(status_host, arena + view.o_words + 4 * kExStatus, 4, cudaMemcpyDeviceToHost, st),
+               "exchange status");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    if (status_host[0]) {
+      static const char *names[kExKinds] = {"counts", "keys", "rows", "gradient counts", "gradients"};
+      std::string which;
+      for (int k = 0; k < kExKinds; ++k)
+        if (status_host[0] & (1u << k)) which += std::string(which.empty() ? "" : ", ") + names[k];
+      throw Error(SE_ERR_RUNTIME, "exchange wait timed out (" + which +
+                                      "): a peer rank did not take part; the exchange must be recreated");
+    }
+    store->check_status(store->table(dim), st);
+  }
+};
+
 void set_last_error(const std::string &msg) { t_last_error = msg; }
 void clear_last_error() { t_last_error.clear(); }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
@@ -1366,6 +1718,10 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 struct se_store {
   se_gpu::StoreImpl impl;
+};
+
+struct se_exchange {
+  se_gpu::ExchangeImpl impl;
 };
 
 using namespace se_gpu;
@@ -1620,6 +1976,81 @@ int se_store_profile_read(se_store *store, const char *name, double *out_ms, uin
     *out_ms = ms;
     *out_launches = count;
   });
+}
+
+
+int se_exchange_create(se_store *store, int32_t partitioner_kind, uint32_t world_size, uint32_t rank,
+                       uint64_t max_keys_per_rank, int64_t dim, uint32_t timeout_ms, se_exchange **out) {
+  return guarded([&] {
+    if (!out) throw std::invalid_argument("null output handle");
+    auto ex = std::make_unique<se_exchange>();
+    ex->impl.create(&checked(store)->impl, partitioner_kind, world_size, rank, max_keys_per_rank, dim, timeout_ms);
+    *out = ex.release();
+  });
+}
+
+int se_exchange_handle(se_exchange *ex, void *handle_out, size_t handle_bytes) {
+  return guarded([&] {
+    if (!ex || !handle_out) throw std::invalid_argument("null exchange or handle buffer");
+    ex->impl.handle(handle_out, handle_bytes);
+  });
+}
+
+int se_exchange_connect(se_exchange *ex, const void *handles, size_t handles_bytes) {
+  return guarded([&] {
+    if (!ex || !handles) throw std::invalid_argument("null exchange or handles");
+    ex->impl.connect(handles, handles_bytes);
+  });
+}
+
+int se_exchange_connect_local(se_exchange *const *exchanges, uint32_t count) {
+  return guarded([&] {
+    if (!exchanges || count == 0) throw std::invalid_argument("no exchanges given");
+    for (uint32_t r = 0; r < count; ++r) {
+      ExchangeImpl &e = exchanges[r]->impl;
+      if (e.W != count || e.me != r) throw std::invalid_argument("exchanges[r] must be rank r of world_size == count");
+      if (e.connected) throw std::invalid_argument("exchange is already connected");
+    }
+    for (uint32_t r = 0; r < count; ++r) {
+      ExchangeImpl &e = exchanges[r]->impl;
+      DeviceGuard dg(e.device);
+      for (uint32_t q = 0; q < count; ++q) {
+        const ExchangeImpl &o = exchanges[q]->impl;
+        if (o.device != e.device) {
+          const cudaError_t pe = cudaDeviceEnablePeerAccess(o.device, 0);
+          if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+          else cuda_check(pe, "cudaDeviceEnablePeerAccess");
+        }
+        e.peers[q] = o.arena;
+      }
+      e.finish_connect();
+    }
+  });
+}
+
+int se_exchange_lookup(se_exchange *ex, const void *keys, size_t n, void *out, int32_t insert, void *stream) {
+  return guarded([&] {
+    if (!ex) throw std::invalid_argument("exchange handle is null");
+    ex->impl.forward(keys, n, out, insert != 0, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int se_exchange_accumulate(se_exchange *ex, const void *keys, size_t n, const void *grads, void *stream) {
+  return guarded([&] {
+    if (!ex) throw std::invalid_argument("exchange handle is null");
+    ex->impl.backward(keys, n, grads, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int se_exchange_check(se_exchange *ex, void *stream) {
+  return guarded([&] {
+    if (!ex) throw std::invalid_argument("exchange handle is null");
+    ex->impl.check(static_cast<cudaStream_t>(stream));
+  });
+}
+
+int se_exchange_destroy(se_exchange *ex) {
+  return guarded([&] { delete ex; });
 }
 
 }  // extern "C"

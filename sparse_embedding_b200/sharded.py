@@ -18,13 +18,23 @@ key reaches do not depend on the number of GPUs; received batches are laid
 out rank 0 first, so an owner accumulates a key's gradients in the order of
 the concatenated global batch.
 
-The collectives are torch.distributed all_to_all_single calls (NCCL on GPUs).
-The routing and permutation steps are sm_100a kernels by default
-(GpuRouter); any object with the same three methods can stand in for it.
+Two transports carry the exchange:
+
+  "collective": torch.distributed all_to_all_single calls (NCCL on GPUs, gloo
+                on CPU). The routing and permutation steps are sm_100a kernels
+                by default (GpuRouter); any object with the same three methods
+                can stand in for it.
+  "p2p"       : the library's peer-memory exchange (se_exchange_*): every rank
+                maps every rank's exchange arena through CUDA IPC and the
+                route, scatter, owner lookup / insert and row return are
+                kernels that store straight into the peers' HBM over NVLink,
+                synchronised by flags in device memory - no host round trip,
+                no collective library, and capturable in a CUDA graph.
 """
 
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 from . import _native as N
@@ -71,20 +81,117 @@ class ExchangePlan:
     recv_keys: object
 
 
+class PeerExchange:
+    """One rank's end of the peer-memory exchange for rows of length `dim`.
+
+    Collective: every rank of `group` constructs it with the same arguments
+    and then makes the same sequence of lookup / accumulate calls.
+    """
+
+    HANDLE_BYTES = 64  # a CUDA IPC memory handle
+
+    def __init__(self, store, partitioner_name: str, dim: int, max_keys_per_rank: int, group=None,
+                 timeout_ms: int = 10_000):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.store = store
+        self.dim = int(dim)
+        self.max_keys = int(max_keys_per_rank)
+        self._lib = N.lib()
+        kind = create_partitioner(partitioner_name, self.world)._kind
+        h = C.c_void_p()
+        N.check(self._lib.se_exchange_create(store._h, N.PART_CODES[kind], self.world, self.rank, self.max_keys,
+                                             self.dim, int(timeout_ms), C.byref(h)))
+        self._h = h
+        buf = (C.c_char * self.HANDLE_BYTES)()
+        N.check(self._lib.se_exchange_handle(h, buf, self.HANDLE_BYTES))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(buf), group=group)
+        joined = b"".join(handles)
+        N.check(self._lib.se_exchange_connect(h, joined, len(joined)))
+        dist.barrier(group)  # every arena is mapped before any rank stores into it
+
+    def _stream(self, t):
+        torch = torch_mod()
+        return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+    def lookup(self, keys, insert: bool, out=None):
+        """(n, dim) rows of this rank's keys in batch order, from their owners."""
+        torch = torch_mod()
+        n = keys.numel()
+        if out is None:
+            out = torch.empty((n, self.dim), dtype=getattr(torch, self.store.value_dtype()), device=keys.device)
+        N.check(self._lib.se_exchange_lookup(self._h, keys.data_ptr(), n, out.data_ptr(), int(insert),
+                                             self._stream(keys)))
+        return out
+
+    def accumulate(self, keys, grads) -> None:
+        """Sends grads[i] (gradient dtype, (n, dim)) of keys[i] to the key's owner."""
+        N.check(self._lib.se_exchange_accumulate(self._h, keys.data_ptr(), keys.numel(), grads.data_ptr(),
+                                                 self._stream(keys)))
+
+    def check(self) -> None:
+        """Waits for this rank's stream; raises a timed-out exchange or table errors."""
+        torch = torch_mod()
+        N.check(self._lib.se_exchange_check(self._h, C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+    def close(self) -> None:
+        if self._h is not None:
+            torch = torch_mod()
+            torch.cuda.synchronize()
+            self.dist.barrier(self.group)  # no peer stores into this arena any more
+            N.check(self._lib.se_exchange_destroy(self._h))
+            self._h = None
+
+
 class ShardedEmbeddingStore:
     """Data-parallel batches over key-sharded stores, one per rank."""
 
-    def __init__(self, local_store, partitioner_name: str = "sparse_embedding.hash", group=None, router=None):
+    def __init__(self, local_store, partitioner_name: str = "sparse_embedding.hash", group=None, router=None,
+                 transport: str = "collective", max_keys_per_rank: int | None = None, timeout_ms: int = 10_000):
         import torch.distributed as dist
 
+        if transport not in ("collective", "p2p"):
+            raise ValueError("transport must be 'collective' or 'p2p'")
+        if transport == "p2p" and not max_keys_per_rank:
+            raise ValueError("the p2p transport needs max_keys_per_rank")
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.store = local_store
-        self.router = router if router is not None else GpuRouter(partitioner_name, self.world)
+        self.partitioner_name = partitioner_name
+        self.transport = transport
+        self.max_keys_per_rank = max_keys_per_rank
+        self.timeout_ms = timeout_ms
+        self._exchanges: dict[int, PeerExchange] = {}
+        self.router = router if router is not None else (
+            GpuRouter(partitioner_name, self.world) if transport == "collective" else None)
         self._plan: ExchangePlan | None = None
         self._plan_keys = None
+
+    def exchange(self, dim: int) -> PeerExchange:
+        """The peer-memory exchange for rows of length dim (created on first use; collective)."""
+        ex = self._exchanges.get(dim)
+        if ex is None:
+            ex = PeerExchange(self.store, self.partitioner_name, dim, self.max_keys_per_rank, self.group,
+                              self.timeout_ms)
+            self._exchanges[dim] = ex
+        return ex
+
+    def check(self) -> None:
+        """p2p transport: waits for this rank's stream and raises exchange or table errors."""
+        for ex in self._exchanges.values():
+            ex.check()
+
+    def close(self) -> None:
+        """Releases the peer-memory exchanges (collective)."""
+        for ex in self._exchanges.values():
+            ex.close()
+        self._exchanges.clear()
 
     # ---- exchange ------------------------------------------------------------
 
@@ -110,6 +217,8 @@ class ShardedEmbeddingStore:
     # ---- hot path ------------------------------------------------------------
 
     def _rows(self, keys, dim: int, insert: bool):
+        if self.transport == "p2p":
+            return self.exchange(dim).lookup(keys, insert)
         plan = self.plan(keys)
         fn = self.store.lookup_or_insert if insert else self.store.lookup
         owned, _ = fn(plan.recv_keys, dim)
@@ -127,8 +236,11 @@ class ShardedEmbeddingStore:
 
     def accumulate_gradients(self, keys, grads) -> None:
         """grads[i] is the gradient row of keys[i]; it is sent to the key's owner."""
-        plan = self._plan_for(keys)
         dim = grads.shape[-1]
+        if self.transport == "p2p":
+            self.exchange(dim).accumulate(keys, grads.reshape(-1, dim).contiguous())
+            return
+        plan = self._plan_for(keys)
         routed = self.router.to_routed(grads.reshape(-1, dim), plan.send_positions)
         recv = routed.new_empty((sum(plan.recv_splits), dim))
         self.dist.all_to_all_single(recv, routed, plan.recv_splits, plan.send_splits, group=self.group)

@@ -1,5 +1,6 @@
-"""Key-sharded store on 2 GPUs (NCCL) against one oracle store fed the
-concatenated global batches (GPU, needs 2 devices)."""
+"""Key-sharded store on 2 GPUs against one oracle store fed the concatenated
+global batches (GPU, needs 2 devices), over both transports: NCCL
+all-to-all ("collective") and the library's peer-memory exchange ("p2p")."""
 
 import os
 import socket
@@ -23,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, port, kind, steps, q):
+def _worker(rank, port, kind, transport, steps, q):
     import datetime
 
     import torch.distributed as dist
@@ -38,7 +39,8 @@ def _worker(rank, port, kind, steps, q):
 
         store = se.EmbeddingStore(se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=rank),
                                   optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
-        sharded = ShardedEmbeddingStore(store, f"sparse_embedding.{kind}")
+        sharded = ShardedEmbeddingStore(store, f"sparse_embedding.{kind}", transport=transport,
+                                        max_keys_per_rank=1024, timeout_ms=20_000)
         mine, pool = batches(rank, steps)
         rows_seen = []
         for keys, grads in mine:
@@ -48,14 +50,17 @@ def _worker(rank, port, kind, steps, q):
             sharded.accumulate_gradients(k, torch.from_numpy(grads).cuda())
             sharded.optimizer_step(1)
         final = sharded.lookup(torch.from_numpy(pool).cuda(), DIM).cpu().numpy()
+        sharded.check()
         torch.cuda.synchronize()
+        sharded.close()
         q.put((rank, rows_seen, final))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["collective", "p2p"])
 @pytest.mark.parametrize("kind", ["hash", "fast_range"])
-def test_sharded_two_gpus_match_single_store(kind):
+def test_sharded_two_gpus_match_single_store(kind, transport):
     if torch.cuda.device_count() < WORLD:
         pytest.skip("needs 2 GPUs")
     from oracle import oracle as O
@@ -64,7 +69,7 @@ def test_sharded_two_gpus_match_single_store(kind):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, kind, steps, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, kind, transport, steps, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     results = dict((r, (rows, final)) for r, rows, final in (q.get(timeout=300) for _ in range(WORLD)))
