@@ -320,7 +320,7 @@ def run_ours(args):
     names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
              "k_group_place", "k_group_apply", "k_group_hot"]
     if world > 1 and args.transport == "p2p":
-        names += ["k_ex_scatter", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_grads"]
+        names += ["k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_rows", "k_ex_scatter_grads"]
     times = {}
     for nm in names:
         ms, cnt = store.profile_read(nm)

@@ -234,6 +234,11 @@ int se_exchange_lookup(se_exchange *ex, const void *keys, size_t n, void *out, i
  * grads holds n x dim values of the gradient dtype. Device-side validation
  * (see se_accumulate_gradients with device inputs). */
 int se_exchange_accumulate(se_exchange *ex, const void *keys, size_t n, const void *grads, void *stream);
+/* accumulate_gradients for the keys of this rank's last se_exchange_lookup,
+ * in that batch's order (grads: n x dim, n = that batch's size). The rows
+ * follow the lookup's route and the owners reuse the keys it delivered, so no
+ * keys cross NVLink again. Every rank must make the same choice of call. */
+int se_exchange_accumulate_routed(se_exchange *ex, const void *grads, size_t n, void *stream);
 /* Synchronises `stream`; raises a timed-out wait, then the owner table's errors. */
 int se_exchange_check(se_exchange *ex, void *stream);
 /* Frees this rank's end. Call only after every rank finished its last

@@ -100,6 +100,7 @@ _SIGNATURES = {
     "se_exchange_connect_local": [C.POINTER(_vp), _u32],
     "se_exchange_lookup": [_vp, _vp, _sz, _vp, _i32, _vp],
     "se_exchange_accumulate": [_vp, _vp, _sz, _vp, _vp],
+    "se_exchange_accumulate_routed": [_vp, _vp, _sz, _vp],
     "se_exchange_check": [_vp, _vp],
     "se_exchange_destroy": [_vp],
 }

@@ -77,6 +77,7 @@ enum StatusBits : uint32_t {
   kStatusTableFull = 1u,       // probe sequence or row arena exhausted
   kStatusBadGradient = 2u,     // gradient fails validate_input
   kStatusBadRow = 4u,          // row index outside the arena
+  kStatusPendingOverflow = 8u, // device pending count beyond the host-sized buffers
 };
 
 __device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bits) {

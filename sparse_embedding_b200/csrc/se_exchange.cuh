@@ -18,8 +18,9 @@
 //             key's rows arrive in the order of the concatenated batch).
 //
 // Each phase ends with a flag per (kind, sender) in the receiver's arena,
-// written after a system-scope fence with the sender's epoch for that kind;
-// a receiver waits until every sender's flag reaches its own epoch. Waits are
+// written with the sender's epoch for that kind by the block of the phase's
+// kernel that finishes last (after every block's system-scope fence); a
+// receiver waits until every sender's flag reaches its own epoch. Waits are
 // bounded in time: past the exchange's timeout the kernel records it and returns.
 //
 // One buffer per kind suffices when every rank makes the same sequence of
@@ -33,7 +34,14 @@
 //    precedes p's GCOUNTS flag of call k+1; senders wait for it before
 //    scattering call k+1. The gradient count matrix is read only inside the
 //    scatter kernel (the received total is staged there), which precedes p's
-//    GRADS flag of call k, which senders wait for before publishing call k+1.
+//    GRADS flag of call k, which senders wait for before publishing call k+1;
+//  - a gradient batch routed like the last forward (no keys sent) lands in
+//    the gradient inbox at the forward's slots and is accumulated with the
+//    forward's key inbox: a sender scatters it only after its forward saw
+//    owner p's ROWS flag, which p raises after its previous accumulate, and
+//    p's key inbox is rewritten only after p's next COUNTS flag, which p
+//    raises after this accumulate. The forward's total is staged by the
+//    owner kernel.
 #pragma once
 
 #include "se_partition.cuh"
@@ -47,7 +55,9 @@ constexpr uint64_t kSpinLimit = 1ull << 28;  // hard cap on polls (>= 128 ns eac
 
 struct ExView {
   uint8_t *const *peer;  // [W] arena base of every rank (own included), device array
+  uint32_t *done;        // [kExKinds] finished blocks of the running launch per kind (own memory)
   uint32_t W, me;
+  uint32_t M;            // keys per rank per call: rows of a row buffer; an inbox holds W * M
   uint32_t row_bytes, grad_bytes;
   uint64_t timeout_ns;
   // byte offsets inside every arena
@@ -72,7 +82,12 @@ struct ExView {
   __device__ __forceinline__ uint32_t *words() const { return reinterpret_cast<uint32_t *>(peer[me] + o_words); }
 };
 
-enum ExWord : int { kExTotal = 0, kExTotalStaged = 1, kExStatus = 2, kExWords = 4 };
+// kExFwdTotal: keys received by the last forward (the row count of a
+// gradient batch routed like that forward's keys).
+enum ExWord : int { kExTotal = 0, kExTotalStaged = 1, kExStatus = 2, kExFwdTotal = 3, kExWords = 4 };
+// Status bit (above the per-kind timeout bits) for a slot or position outside
+// the buffers, i.e. ranks created with different sizes; the access is skipped.
+constexpr uint32_t kExBadIndex = 1u << 8;
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   uint32_t v;
@@ -116,11 +131,18 @@ __device__ __forceinline__ bool ex_wait(const ExView &x, int kind) {
   return true;
 }
 
-// One block: bumps this rank's epoch of `kind`, optionally stores this rank's
-// per-owner counts into row `me` of every rank's count matrix, then raises
-// flag (kind, me) on every rank after a system-scope fence.
-__global__ void k_ex_publish(ExView x, int kind, const uint32_t *counts_local) {
+// True once a wait of this rank gave up: the data kernels then do nothing
+// (every block alike), so a failed exchange stops moving data.
+__device__ __forceinline__ bool ex_failed(const ExView &x) {
+  return *reinterpret_cast<volatile uint32_t *>(x.words() + kExStatus) != 0u;
+}
+
+// All threads of one block: bumps this rank's epoch of `kind`, optionally
+// stores this rank's per-owner counts into row `me` of every rank's count
+// matrix, then raises flag (kind, me) on every rank after a system-scope fence.
+__device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local) {
   __shared__ uint32_t e;
+  __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t *ep = x.epochs() + kind;
     e = *ep + 1u;
@@ -130,54 +152,144 @@ __global__ void k_ex_publish(ExView x, int kind, const uint32_t *counts_local) {
   for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) {
     if (counts_local) {
       uint32_t *cm = x.counts(p, kind) + size_t(x.me) * x.W;
-      for (uint32_t d = 0; d < x.W; ++d) cm[d] = counts_local[d];
+      for (uint32_t d = 0; d < x.W; ++d) cm[d] = __ldcg(counts_local + d);
     }
     __threadfence_system();
     st_release_sys(x.flags(p) + size_t(kind) * x.W + x.me, e);
   }
 }
 
+// Every thread of a block calls this at the end of its block's share of a
+// launch; true in the one block that finishes last, which then resets the
+// counter. Each block orders its writes before its count with a GPU-scope
+// fence; the last block, having seen every count, issues one system-scope
+// fence, which (fences being cumulative) orders all of the launch's writes,
+// peer stores included, before the flags it raises next. A system-scope
+// fence in every block costs a stall per block instead.
+__device__ bool ex_last_block(const ExView &x, int kind) {
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(x.done + kind, 1u) == gridDim.x - 1;
+    if (last) {
+      x.done[kind] = 0;
+      __threadfence_system();
+    }
+  }
+  __syncthreads();
+  return last;
+}
+
+// End of a launch that wrote data of `kind` into peers' arenas: the last
+// block raises the flags.
+__device__ void ex_finish(const ExView &x, int kind) {
+  if (ex_last_block(x, kind)) ex_raise(x, kind, nullptr);
+}
+
+// Waits (one thread) until every sender's flag of `kind` reached this rank's
+// epoch; the kernels after it on the stream read what the senders stored.
+// One waiting thread per phase instead of one per block of the next kernel:
+// a system-scope acquire in every block stalls each of them.
+__global__ void k_ex_wait(ExView x, int kind) {
+  if (threadIdx.x == 0) ex_wait(x, kind);
+}
+
+// Route counts of this rank's keys: per-tile histograms, then (in the block
+// that finishes last) the partition-major exclusive offsets of every tile and
+// the per-owner counts, which it publishes as `kind` (COUNTS or GCOUNTS).
+// Launched with max(tiles, 1) blocks of kExTile keys.
+template <class K>
+__global__ void __launch_bounds__(kRouteThreads)
+k_ex_count(PartSpec s, ExView x, int kind, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts,
+           uint32_t *__restrict__ tile_offsets, uint32_t *__restrict__ counts) {
+  extern __shared__ uint32_t hist[];  // [W]
+  if (ex_failed(x)) return;
+  for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) hist[p] = 0;
+  __syncthreads();
+  const size_t i = size_t(blockIdx.x) * kRouteThreads + threadIdx.x;
+  if (i < count) atomicAdd(&hist[partition_of<K>(s, keys[i])], 1u);
+  __syncthreads();
+  for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) tile_counts[size_t(blockIdx.x) * s.n + p] = hist[p];
+  if (!ex_last_block(x, kind)) return;
+  using Scan = cub::BlockScan<uint32_t, kRouteThreads>;
+  __shared__ typename Scan::TempStorage tmp;
+  __shared__ uint32_t carry;
+  const uint32_t tiles = gridDim.x;
+  uint32_t running = 0;  // partition base, valid in thread 0
+  for (uint32_t p = 0; p < s.n; ++p) {
+    if (threadIdx.x == 0) carry = running;
+    __syncthreads();
+    for (uint32_t t0 = 0; t0 < tiles; t0 += kRouteThreads) {
+      const uint32_t t = t0 + threadIdx.x;
+      const uint32_t c = t < tiles ? __ldcg(tile_counts + size_t(t) * s.n + p) : 0u;
+      uint32_t excl, total;
+      Scan(tmp).ExclusiveSum(c, excl, total);
+      const uint32_t base = carry;
+      if (t < tiles) tile_offsets[size_t(t) * s.n + p] = base + excl;
+      __syncthreads();
+      if (threadIdx.x == 0) carry = base + total;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      counts[p] = carry - running;
+      running = carry;
+    }
+    __syncthreads();
+  }
+  ex_raise(x, kind, counts);
+}
+
+// Keys per route tile of the exchange: one per thread of a 256-thread block,
+// so a 65,536-key batch spreads over 256 blocks.
+constexpr int kExTile = kRouteThreads;
+
 // Route scatter into the owners' inboxes (forward: keys and batch positions;
-// backward: keys and gradient rows copied in units U). Same two-pass stable
-// ranking as k_route_scatter; the slot on owner d is sum_{s < me} counts[s][d]
-// plus the key's rank among this rank's keys for d.
+// backward: keys and gradient rows, copied block-wide in units U after the
+// slots are known). Stable: a key's slot on owner d is
+// sum_{s < me} counts[s][d] + (keys of earlier tiles for d) + (keys of
+// earlier warps of this tile for d) + (earlier lanes of its warp for d).
+// The keys are loaded and ranked within their warp before the wait for the
+// peers' counts.
+// Forward also records each key's (owner, slot) in key_pid / key_slot, so a
+// gradient batch for the same keys can follow the same route (k_ex_scatter_rows).
 template <class K, bool kGrads, class U>
 __global__ void __launch_bounds__(kRouteThreads)
 k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, const uint32_t *__restrict__ tile_offsets,
-             const uint32_t *__restrict__ counts_local, const uint8_t *__restrict__ grads) {
+             const uint32_t *__restrict__ counts_local, const uint8_t *__restrict__ grads,
+             uint32_t *__restrict__ key_pid, uint32_t *__restrict__ key_slot) {
   extern __shared__ uint32_t sm[];
   uint32_t *warp_base = sm;                   // [kRouteWarps][W]
   uint32_t *remote = sm + kRouteWarps * s.n;  // [W] slot base on each owner minus the local prefix
-  __shared__ bool ok;
+  __shared__ uint32_t row_pid[kExTile], row_slot[kExTile];
   const int kind = kGrads ? kExGCounts : kExCounts;
-  if (threadIdx.x == 0) ok = ex_wait(x, kind);
+  if (ex_failed(x)) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  const size_t tile_base = size_t(blockIdx.x) * kExTile;
+  const size_t i = tile_base + threadIdx.x;
+  const bool valid = i < count;
+  K key{};
+  uint32_t pid = 0xffffffffu;
+  if (valid) {
+    key = keys[i];
+    pid = partition_of<K>(s, key);
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, pid);
+  for (uint32_t j = threadIdx.x; j < kRouteWarps * s.n; j += blockDim.x) warp_base[j] = 0;
   __syncthreads();
-  if (!ok) return;
+  if (valid && (peers & lt) == 0) warp_base[size_t(warp) * s.n + pid] = __popc(peers);
   const uint32_t *cm = x.counts(x.me, kind);
   if (kGrads && blockIdx.x == 0 && threadIdx.x == 0) {
     uint32_t total = 0;
     for (uint32_t q = 0; q < x.W; ++q) total += __ldcg(cm + size_t(q) * x.W + x.me);
     x.words()[kExTotalStaged] = total;
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const unsigned lt = (1u << lane) - 1u;
-  for (uint32_t j = threadIdx.x; j < kRouteWarps * s.n; j += blockDim.x) warp_base[j] = 0;
   for (uint32_t d = threadIdx.x; d < s.n; d += blockDim.x) {
     uint32_t base = 0, local_prefix = 0;
     for (uint32_t q = 0; q < x.me; ++q) base += __ldcg(cm + size_t(q) * x.W + d);
     for (uint32_t q = 0; q < d; ++q) local_prefix += counts_local[q];
-    remote[d] = base - local_prefix;  // modular: added to the routed index below
-  }
-  __syncthreads();
-  const size_t wbase = size_t(blockIdx.x) * kRouteTile + size_t(warp) * kRouteWarpKeys;
-  uint32_t *mine = warp_base + size_t(warp) * s.n;
-  for (int r = 0; r < kRouteWarpKeys; r += 32) {
-    const size_t i = wbase + r + lane;
-    const bool valid = i < count;
-    const uint32_t pid = valid ? partition_of<K>(s, keys[i]) : 0xffffffffu;
-    const unsigned peers = __match_any_sync(0xffffffffu, pid);
-    if (valid && (peers & lt) == 0) mine[pid] += __popc(peers);
-    __syncwarp();
+    remote[d] = base - local_prefix;  // modular: added to the routed offset below
   }
   __syncthreads();
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) {
@@ -189,45 +301,41 @@ k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, con
     }
   }
   __syncthreads();
-  for (int r = 0; r < kRouteWarpKeys; r += 32) {
-    const size_t i = wbase + r + lane;
-    const bool valid = i < count;
-    K key{};
-    uint32_t pid = 0xffffffffu;
-    if (valid) {
-      key = keys[i];
-      pid = partition_of<K>(s, key);
+  const uint32_t inbox = x.W * x.M;
+  if (valid) {
+    uint32_t slot = warp_base[size_t(warp) * s.n + pid] + __popc(peers & lt) + remote[pid];
+    if (slot >= inbox) {
+      atomicOr(x.words() + kExStatus, kExBadIndex);
+      slot = inbox;  // marks the row as skipped below
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, pid);
-    uint32_t slot = 0;
-    if (valid) slot = mine[pid] + __popc(peers & lt) + remote[pid];
-    __syncwarp();
-    if (valid) {
-      if (kGrads) {
-        x.gkeys(pid)[slot] = key_u64(key);
-      } else {
-        x.inkeys(pid)[slot] = key_u64(key);
-        x.inpos(pid)[slot] = uint32_t(i);
-      }
-      if ((peers & lt) == 0) mine[pid] += __popc(peers);
-    }
-    __syncwarp();
-    if constexpr (kGrads) {
-      // the warp copies its (up to) 32 gradient rows one after another
-      const uint32_t units = x.grad_bytes / uint32_t(sizeof(U));
-      const unsigned any = __ballot_sync(0xffffffffu, valid);
-      for (int k = 0; k < 32; ++k) {
-        if (!((any >> k) & 1u)) continue;
-        const uint32_t kp = __shfl_sync(0xffffffffu, pid, k);
-        const uint32_t ks = __shfl_sync(0xffffffffu, slot, k);
-        const size_t ki = wbase + r + k;
-        const U *src = reinterpret_cast<const U *>(grads + ki * x.grad_bytes);
-        U *dst = reinterpret_cast<U *>(x.ingrads(kp) + size_t(ks) * x.grad_bytes);
-        for (uint32_t u = lane; u < units; u += 32) dst[u] = src[u];
-      }
+    if (slot == inbox) {
+      if constexpr (kGrads) row_slot[threadIdx.x] = inbox;
+      else key_slot[i] = inbox;
+    } else if constexpr (kGrads) {
+      x.gkeys(pid)[slot] = key_u64(key);
+      row_pid[threadIdx.x] = pid;
+      row_slot[threadIdx.x] = slot;
+    } else {
+      x.inkeys(pid)[slot] = key_u64(key);
+      x.inpos(pid)[slot] = uint32_t(i);
+      key_pid[i] = pid;
+      key_slot[i] = slot;
     }
   }
-  __threadfence_system();
+  if constexpr (kGrads) {
+    __syncthreads();
+    const uint32_t units = x.grad_bytes / uint32_t(sizeof(U));
+    const uint32_t rows = uint32_t(min(size_t(kExTile), count - min(count, tile_base)));
+    const U *src = reinterpret_cast<const U *>(grads + tile_base * x.grad_bytes);
+#pragma unroll 4
+    for (uint32_t u = threadIdx.x; u < rows * units; u += blockDim.x) {
+      const uint32_t r = u / units, c = u - r * units;
+      if (row_slot[r] >= inbox) continue;
+      U *dst = reinterpret_cast<U *>(x.ingrads(row_pid[r]) + size_t(row_slot[r]) * x.grad_bytes);
+      dst[c] = src[u];
+    }
+  }
+  ex_finish(x, kGrads ? kExGrads : kExKeys);
 }
 
 // Owner of the keys: after the keys of every sender arrived, finds (and with
@@ -240,20 +348,22 @@ __global__ void __launch_bounds__(256)
 k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uint64_t capacity, InitSpec init,
            ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
   __shared__ uint32_t prefix[kExMaxRanks + 1];
-  __shared__ bool ok;
-  if (threadIdx.x == 0) ok = ex_wait(x, kExKeys);
-  __syncthreads();
-  if (!ok) return;
+  if (ex_failed(x)) return;
   if (threadIdx.x == 0) {
     uint32_t run = 0;
     for (uint32_t s = 0; s < x.W; ++s) {
       prefix[s] = run;
       run += __ldcg(x.counts(x.me, kExCounts) + size_t(s) * x.W + x.me);
     }
+    if (run > x.W * x.M) {
+      atomicOr(x.words() + kExStatus, kExBadIndex);
+      run = x.W * x.M;
+    }
     prefix[x.W] = run;
   }
   __syncthreads();
   const uint32_t total = prefix[x.W];
+  if (blockIdx.x == 0 && threadIdx.x == 0) x.words()[kExFwdTotal] = total;
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -262,9 +372,13 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
   const uint32_t *inpos = x.inpos(x.me);
   for (size_t i = t / LANES; i < total; i += groups) {
     const uint64_t key = __ldcg(inkeys + i);
-    const uint32_t pos = __ldcg(inpos + i);
+    uint32_t pos = __ldcg(inpos + i);
     uint32_t src = 0;
     while (src + 1 < x.W && prefix[src + 1] <= i) ++src;
+    if (pos >= x.M) {
+      atomicOr(x.words() + kExStatus, kExBadIndex);
+      pos = 0;  // inside the buffer; the row there is reported invalid by the status
+    }
     void *out_row = x.rows(src) + size_t(pos) * x.row_bytes;
     int kind = kFound;
     uint32_t row = kNoRow;
@@ -312,7 +426,13 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
     }
   }
-  __threadfence_system();
+  if constexpr (kInsert) {
+    // k_ex_owner_deferred follows; its last block raises the ROWS flags
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence();
+  } else {
+    ex_finish(x, kExRows);
+  }
 }
 
 // Deferred keys of k_ex_owner: their claimant has published the row by now.
@@ -323,6 +443,7 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
+  if (ex_failed(x)) return;
   const uint32_t count = *def_count;
   for (size_t j = t / LANES; j < count; j += groups) {
     const uint32_t i = def_idx[j];
@@ -332,7 +453,8 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
       if (i >= run && i < run + c) src = s;
       run += c;
     }
-    const uint32_t pos = __ldcg(x.inpos(x.me) + i);
+    uint32_t pos = __ldcg(x.inpos(x.me) + i);
+    if (pos >= x.M) pos = 0;  // reported by k_ex_owner
     void *out_row = x.rows(src) + size_t(pos) * x.row_bytes;
     const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
     if (row == kNoRow) {
@@ -343,7 +465,7 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
     const uint8_t *slab = slabs + size_t(row) * L.stride;
     for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
   }
-  __threadfence_system();
+  ex_finish(x, kExRows);
 }
 
 // Requester: waits for the rows of every owner, then copies this rank's row
@@ -351,22 +473,38 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
 template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_rows_out(ExView x, U *__restrict__ out, size_t units) {
-  __shared__ bool ok;
-  if (threadIdx.x == 0) ok = ex_wait(x, kExRows);
-  __syncthreads();
-  if (!ok) return;
+  if (ex_failed(x)) return;
   const U *src = reinterpret_cast<const U *>(x.rows(x.me));
   for (size_t u = size_t(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += size_t(gridDim.x) * blockDim.x)
     out[u] = __ldcg(src + u);
 }
 
+// Gradient rows for the keys of the last forward, in that forward's route:
+// row i goes to slot key_slot[i] of owner key_pid[i]'s gradient inbox, so it
+// lines up with the key the owner holds in its key inbox. No wait: the slots
+// were fixed by the forward.
+template <class U>
+__global__ void __launch_bounds__(256)
+k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot, size_t n,
+                  const U *__restrict__ grads, uint32_t units) {
+  if (ex_failed(x)) return;
+  const size_t total = n * units;
+  for (size_t u = size_t(blockIdx.x) * blockDim.x + threadIdx.x; u < total; u += size_t(gridDim.x) * blockDim.x) {
+    const size_t r = u / units, c = u - r * units;
+    if (key_slot[r] >= x.W * x.M) continue;  // skipped (and reported) by the forward
+    U *dst = reinterpret_cast<U *>(x.ingrads(key_pid[r]) + size_t(key_slot[r]) * x.grad_bytes);
+    dst[c] = grads[u];
+  }
+  ex_finish(x, kExGrads);
+}
+
 // Owner, backward: waits for every sender's gradients and sets the number of
-// received rows (the device count of the accumulate that follows; 0 when the
-// wait gave up).
-__global__ void k_ex_grads_total(ExView x) {
+// received rows from `word` (the device count of the accumulate that
+// follows; 0 when the wait gave up).
+__global__ void k_ex_grads_total(ExView x, int word) {
   if (threadIdx.x != 0) return;
   uint32_t *w = x.words();
-  w[kExTotal] = ex_wait(x, kExGrads) ? w[kExTotalStaged] : 0u;
+  w[kExTotal] = ex_wait(x, kExGrads) ? w[word] : 0u;
 }
 
 }  // namespace se_gpu

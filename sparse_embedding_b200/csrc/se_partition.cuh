@@ -114,14 +114,14 @@ constexpr int kRouteWarpKeys = 256;
 constexpr int kRouteTile = kRouteWarps * kRouteWarpKeys;
 constexpr uint32_t kRouteMaxPartitions = 1024;
 
-template <class K>
+template <class K, int TILE = kRouteTile>
 __global__ void k_route_count(PartSpec s, const K *__restrict__ keys, size_t count,
                               uint32_t *__restrict__ tile_counts) {
   extern __shared__ uint32_t hist[];
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) hist[p] = 0;
   __syncthreads();
-  const size_t base = size_t(blockIdx.x) * kRouteTile;
-  for (int j = threadIdx.x; j < kRouteTile; j += blockDim.x) {
+  const size_t base = size_t(blockIdx.x) * TILE;
+  for (int j = threadIdx.x; j < TILE; j += blockDim.x) {
     const size_t i = base + j;
     if (i < count) atomicAdd(&hist[partition_of<K>(s, keys[i])], 1u);
   }

@@ -205,13 +205,21 @@ __global__ void __launch_bounds__(256)
 k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
-             void *__restrict__ pgrads_base, uint32_t *pending, uint32_t *done, uint32_t *status) {
+             void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
+             uint32_t *err) {
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   // Rows are appended at the committed pending count; the batch size is the
   // host's n_max or, for exchanged batches, a count in device memory.
   const uint32_t base = *pending;
   const size_t n = n_dev ? min(size_t(*n_dev), n_max) : n_max;
+  if (size_t(base) + n > pcap) {
+    // The buffers were sized from the host's count of pending rows; a device
+    // count beyond it means calls of this store were not stream-ordered.
+    // Every block takes this exit, so nothing is appended or committed.
+    if (tid == 0) raise_status(err, kStatusPendingOverflow);
+    return;
+  }
   unsigned long long *pkeys = pkeys_base + base;
   uint32_t *prows = prows_base + base;
   void *pgrads = static_cast<uint8_t *>(pgrads_base) + size_t(base) * dim * (gdt == SE_FLOAT32 ? 4 : 2);
@@ -386,7 +394,15 @@ struct GroupWs {
   uint32_t *mid;       // [P] segments of LANES+1 .. kApplySlots*LANES rows
   float *partials;     // [items][dim] partial sums of multi-part segments
   uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] mid segments
+  uint32_t cap;        // P: entries the [P] buffers hold (the host's pending count)
+  uint32_t *status;    // table status word (kStatusPendingOverflow)
 };
+
+// Pending entries of this step: the device count, bounded by the buffers.
+__device__ __forceinline__ uint32_t step_count(const uint32_t *count_p, const GroupWs &w) {
+  const uint32_t c = *count_p;
+  return c <= w.cap ? c : w.cap;
+}
 
 // Phase 1: row of every entry (probed at accumulate time; absent keys are
 // probed again, then dropped and counted, hogwild_embedding_store.hpp:1942-1952);
@@ -394,7 +410,8 @@ struct GroupWs {
 __global__ void __launch_bounds__(256)
 k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t *count_p, GroupWs w,
               unsigned long long *dropped) {
-  const uint32_t count = *count_p;
+  const uint32_t count = step_count(count_p, w);
+  if (blockIdx.x == 0 && threadIdx.x == 0 && *count_p > w.cap) raise_status(w.status, kStatusPendingOverflow);
   __shared__ uint32_t s_rows[256];
   __shared__ uint32_t s_n, s_base;
   if (threadIdx.x == 0) s_n = 0;
@@ -447,7 +464,7 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
 
 // Phase 3: every entry takes a slot of its segment (warp-aggregated).
 __global__ void __launch_bounds__(256) k_group_place(const uint32_t *count_p, GroupWs w) {
-  const uint32_t count = *count_p;
+  const uint32_t count = step_count(count_p, w);
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t row = i < count ? w.rows[i] : kNoRow;
@@ -533,7 +550,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 4)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
-  const uint32_t count = *count_p;
+  const uint32_t count = step_count(count_p, w);
   constexpr int GPB = 256 / LANES;
   __shared__ uint32_t s_ord[GPB][LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -581,7 +598,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
             GroupWs w, const uint32_t *count_p) {
-  const uint32_t count = *count_p;
+  const uint32_t count = step_count(count_p, w);
   using Scan = cub::BlockScan<uint32_t, kBlockThreads>;
   constexpr int NG = kBlockThreads / LANES;
   constexpr uint32_t WPT = kHotWindowBits / 32 / kBlockThreads;  // bitmap words per thread
@@ -1213,6 +1230,9 @@ struct StoreImpl {
     const uint32_t s = status_host[0];
     if (s & kStatusTableFull) throw Error(SE_ERR_TABLE_FULL, "embedding table is full");
     if (s & kStatusBadRow) throw Error(SE_ERR_RUNTIME, "row index outside the arena");
+    if (s & kStatusPendingOverflow)
+      throw Error(SE_ERR_RUNTIME, "pending gradient rows on the device exceed the host's count: calls on this "
+                                  "store were not ordered on one stream (rows past the buffers were dropped)");
     if (status_host[1] && t.pcount == 0) {
       // the poisoned window has been stepped (and discarded): report it once
       cuda_check(cudaMemsetAsync(t.ctr + kCtrPoison, 0, 4, st), "status clear");
@@ -1265,11 +1285,13 @@ struct StoreImpl {
       if (vec4)
         k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
-                                              t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word);
+                                              size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
+                                              t.ctr + kCtrStatus);
       else
         k_accumulate<1><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
-                                              t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word);
+                                              size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
+                                              t.ctr + kCtrStatus);
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1330,6 +1352,8 @@ struct StoreImpl {
     w.mid = t.g_mid.get(P);
     w.partials = t.g_partials.get(max_items * uint64_t(t.dim));
     w.ctr = t.ctr + kCtrGroup;
+    w.cap = P;
+    w.status = t.ctr + kCtrStatus;
     cuda_check(cudaMemsetAsync(w.ctr, 0, 16, st), "memset group counters");
     auto *dropped = reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped);
     const unsigned g = grid_for(P, 256);
@@ -1446,12 +1470,17 @@ struct ExchangeImpl {
   std::vector<uint8_t *> peers;    // arena of every rank in this process's address space
   std::vector<bool> opened;        // peers[r] came from cudaIpcOpenMemHandle
   uint8_t **d_peers = nullptr;     // device copy of `peers`
+  uint32_t *d_done = nullptr;      // finished-block counters per kind
   ExView view{};
   bool connected = false;
   // route scratch of the forward and backward direction
   uint32_t *route[2] = {nullptr, nullptr};
   uint32_t tiles_cap = 0;
   uint32_t *status_host = nullptr;  // pinned
+  // (owner, slot) of every key of the last forward, and its batch size
+  uint32_t *key_pid = nullptr, *key_slot = nullptr;
+  size_t last_fwd_n = 0;
+  bool have_fwd = false;
 
   ~ExchangeImpl() {
     DeviceGuard dg(device);
@@ -1459,9 +1488,12 @@ struct ExchangeImpl {
     for (uint32_t r = 0; r < peers.size(); ++r)
       if (opened[r]) cudaIpcCloseMemHandle(peers[r]);
     dfree(d_peers);
+    dfree(d_done);
     dfree(arena);
     dfree(route[0]);
     dfree(route[1]);
+    dfree(key_pid);
+    dfree(key_slot);
     if (status_host) cudaFreeHost(status_host);
   }
 
@@ -1470,6 +1502,8 @@ struct ExchangeImpl {
     if (world == 0 || world > kExMaxRanks) throw std::invalid_argument("world_size must be in [1, 64]");
     if (rank >= world) throw std::invalid_argument("rank must be < world_size");
     if (max_keys == 0 || max_keys > (1ull << 26)) throw std::invalid_argument("max_keys_per_rank must be in [1, 2^26]");
+    if (uint64_t(world) * max_keys >= (1ull << 32))
+      throw std::invalid_argument("world_size * max_keys_per_rank must be below 2^32");
     if (row_dim <= 0) throw std::invalid_argument("dim must be > 0");
     if (timeout_ms == 0) throw std::invalid_argument("timeout_ms must be > 0");
     store = s;
@@ -1493,6 +1527,7 @@ struct ExchangeImpl {
     };
     view.W = W;
     view.me = me;
+    view.M = uint32_t(M);
     view.row_bytes = row_bytes;
     view.grad_bytes = grad_bytes;
     view.timeout_ns = uint64_t(timeout_ms) * 1000000ull;
@@ -1509,9 +1544,14 @@ struct ExchangeImpl {
     arena_bytes = o;
     arena = dalloc<uint8_t>(arena_bytes);
     cuda_check(cudaMemset(arena, 0, arena_bytes), "memset exchange arena");
-    tiles_cap = uint32_t((M + kRouteTile - 1) / kRouteTile);
+    tiles_cap = uint32_t((M + kExTile - 1) / kExTile);
     for (auto &r : route) r = dalloc<uint32_t>(2 * size_t(tiles_cap) * W + W);
+    key_pid = dalloc<uint32_t>(M);
+    key_slot = dalloc<uint32_t>(M);
     d_peers = dalloc<uint8_t *>(W);
+    d_done = dalloc<uint32_t>(kExKinds);
+    cuda_check(cudaMemset(d_done, 0, kExKinds * 4), "memset exchange counters");
+    view.done = d_done;
     cuda_check(cudaMallocHost(&status_host, 16), "cudaMallocHost");
     peers.assign(W, nullptr);
     opened.assign(W, false);
@@ -1560,24 +1600,23 @@ struct ExchangeImpl {
                     c.optimizer_kind == SE_OPT_ADAGRAD ? c.initial_accumulator : 0.0f};
   }
 
-  // Route of this rank's keys: per-tile counts, offsets and per-owner counts.
+  // Route of this rank's keys (per-tile counts, offsets, per-owner counts),
+  // published to every rank as `kind` by the launch's last block.
   template <class K>
-  const uint32_t *run_route(const K *keys, size_t n, int dir, cudaStream_t st) {
-    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+  const uint32_t *run_route(const K *keys, size_t n, int dir, int kind, cudaStream_t st) {
+    const uint32_t tiles = std::max(uint32_t((n + kExTile - 1) / kExTile), 1u);
     uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
     uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
-    if (tiles) {
-      k_route_count<K><<<tiles, kRouteThreads, W * 4, st>>>(spec, keys, n, tile_counts);
-      launched("k_route_count");
-    }
-    k_route_scan<<<1, 1024, 0, st>>>(tile_counts, tiles, W, tile_offsets, counts);
-    launched("k_route_scan");
+    k_ex_count<K><<<tiles, kRouteThreads, W * 4, st>>>(spec, view, kind, keys, n, tile_counts, tile_offsets, counts);
+    launched("k_ex_count");
+    wait(kind, st);
     return counts;
   }
 
-  void publish(int kind, const uint32_t *counts, cudaStream_t st) {
-    k_ex_publish<<<1, 32, 0, st>>>(view, kind, counts);
-    launched("k_ex_publish");
+  // Stream-ordered wait for every rank's flag of `kind`.
+  void wait(int kind, cudaStream_t st) {
+    k_ex_wait<<<1, 32, 0, st>>>(view, kind);
+    launched("k_ex_wait");
   }
 
   void check_batch(const void *keys, size_t n, const void *rows, const char *rows_name) const {
@@ -1592,18 +1631,17 @@ struct ExchangeImpl {
     std::lock_guard<std::mutex> lock(store->mu);
     DeviceGuard dg(device);
     Table &t = store->table(dim);
-    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+    const uint32_t tiles = uint32_t((n + kExTile - 1) / kExTile);
     dispatch_key(store->cfg.key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
-      const uint32_t *counts = run_route<K>(k, n, 0, st);
-      publish(kExCounts, counts, st);
-      StoreImpl::Prof pr(store, "k_ex_scatter", st);
+      const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st);
+      StoreImpl::Prof pr(store, "k_ex_scatter_keys", st);
       k_ex_scatter<K, false, uint4><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
-          spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr);
+          spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot);
       launched("k_ex_scatter");
     });
-    publish(kExKeys, nullptr, st);
+    wait(kExKeys, st);
     // owner side: at most W * M keys arrive
     const uint64_t WM = uint64_t(W) * M;
     if (insert) {
@@ -1623,7 +1661,7 @@ struct ExchangeImpl {
                                                         init, view, t.ctr + kCtrDeferred, def_idx, def_word,
                                                         t.ctr + kCtrStatus);
         launched("k_ex_owner");
-        k_ex_owner_deferred<LN, VC><<<148 * 4, 256, 0, st>>>(t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
+        k_ex_owner_deferred<LN, VC><<<148, 256, 0, st>>>(t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
                                                              def_word, t.ctr + kCtrStatus);
         launched("k_ex_owner_deferred");
       } else {
@@ -1644,7 +1682,9 @@ struct ExchangeImpl {
     };
     if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
     else by_lanes(std::integral_constant<int, 1>{});
-    publish(kExRows, nullptr, st);
+    wait(kExRows, st);
+    last_fwd_n = n;
+    have_fwd = true;
     // requester side: this rank's rows, batch order
     const size_t bytes = n * size_t(view.row_bytes);
     const uintptr_t al = uintptr_t(out) | uintptr_t(bytes);
@@ -1664,29 +1704,57 @@ struct ExchangeImpl {
     check_batch(keys, n, grads, "gradient rows");
     std::lock_guard<std::mutex> lock(store->mu);
     DeviceGuard dg(device);
-    const uint32_t tiles = uint32_t((n + kRouteTile - 1) / kRouteTile);
+    const uint32_t tiles = uint32_t((n + kExTile - 1) / kExTile);
     const uintptr_t al = uintptr_t(grads) | uintptr_t(view.grad_bytes);
     dispatch_key(store->cfg.key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
-      const uint32_t *counts = run_route<K>(k, n, 1, st);
-      publish(kExGCounts, counts, st);
+      const uint32_t *counts = run_route<K>(k, n, 1, kExGCounts, st);
       auto scatter = [&](auto utag) {
         using U = decltype(utag);
         StoreImpl::Prof pr(store, "k_ex_scatter_grads", st);
         k_ex_scatter<K, true, U><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
-            spec, view, k, n, route[1] + size_t(tiles_cap) * W, counts, static_cast<const uint8_t *>(grads));
+            spec, view, k, n, route[1] + size_t(tiles_cap) * W, counts, static_cast<const uint8_t *>(grads), nullptr,
+            nullptr);
         launched("k_ex_scatter");
       };
       if (al % 16 == 0) scatter(uint4{});
       else if (al % 4 == 0) scatter(uint32_t{});
       else scatter(uint16_t{});
     });
-    publish(kExGrads, nullptr, st);
-    k_ex_grads_total<<<1, 32, 0, st>>>(view);
+    k_ex_grads_total<<<1, 32, 0, st>>>(view, kExTotalStaged);
     launched("k_ex_grads_total");
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_gkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
+                             SE_KEY_UINT64);
+  }
+
+  // Gradients for the keys of the last forward (lookup) of this exchange, in
+  // that batch's order: rows follow the forward's route, and the owners
+  // accumulate them with the keys already in their key inboxes.
+  void backward_routed(const void *grads, size_t n, cudaStream_t st) {
+    require_connected();
+    if (!have_fwd) throw std::invalid_argument("no lookup on this exchange to route the gradients by");
+    if (n != last_fwd_n) throw std::invalid_argument("gradient rows must match the keys of the last lookup");
+    if (n && !is_device_ptr(grads)) throw std::invalid_argument("exchange takes device gradient rows");
+    std::lock_guard<std::mutex> lock(store->mu);
+    DeviceGuard dg(device);
+    const uintptr_t al = uintptr_t(grads) | uintptr_t(view.grad_bytes);
+    auto scatter = [&](auto utag) {
+      using U = decltype(utag);
+      const uint32_t units = view.grad_bytes / uint32_t(sizeof(U));
+      StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
+      k_ex_scatter_rows<U><<<grid_for(n * units, 256, 148 * 16), 256, 0, st>>>(view, key_pid, key_slot, n,
+                                                                              static_cast<const U *>(grads), units);
+      launched("k_ex_scatter_rows");
+    };
+    if (al % 16 == 0) scatter(uint4{});
+    else if (al % 4 == 0) scatter(uint32_t{});
+    else scatter(uint16_t{});
+    k_ex_grads_total<<<1, 32, 0, st>>>(view, kExFwdTotal);
+    launched("k_ex_grads_total");
+    const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
+    store->accumulate_locked(arena + view.o_inkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
                              SE_KEY_UINT64);
   }
 
@@ -1698,6 +1766,9 @@ struct ExchangeImpl {
     cuda_check(cudaMemcpyAsync(status_host, arena + view.o_words + 4 * kExStatus, 4, cudaMemcpyDeviceToHost, st),
                "exchange status");
     cuda_check(cudaStreamSynchronize(st), "sync");
+    if (status_host[0] & kExBadIndex)
+      throw Error(SE_ERR_RUNTIME, "exchange slot outside its buffers (ranks created with different sizes?); "
+                                  "the exchange must be recreated");
     if (status_host[0]) {
       static const char *names[kExKinds] = {"counts", "keys", "rows", "gradient counts", "gradients"};
       std::string which;
@@ -2039,6 +2110,13 @@ int se_exchange_accumulate(se_exchange *ex, const void *keys, size_t n, const vo
   return guarded([&] {
     if (!ex) throw std::invalid_argument("exchange handle is null");
     ex->impl.backward(keys, n, grads, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int se_exchange_accumulate_routed(se_exchange *ex, const void *grads, size_t n, void *stream) {
+  return guarded([&] {
+    if (!ex) throw std::invalid_argument("exchange handle is null");
+    ex->impl.backward_routed(grads, n, static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -101,6 +101,7 @@ class PeerExchange:
         self.dim = int(dim)
         self.max_keys = int(max_keys_per_rank)
         self._lib = N.lib()
+        self._last_keys = None  # keys tensor of the last lookup
         kind = create_partitioner(partitioner_name, self.world)._kind
         h = C.c_void_p()
         N.check(self._lib.se_exchange_create(store._h, N.PART_CODES[kind], self.world, self.rank, self.max_keys,
@@ -126,10 +127,21 @@ class PeerExchange:
             out = torch.empty((n, self.dim), dtype=getattr(torch, self.store.value_dtype()), device=keys.device)
         N.check(self._lib.se_exchange_lookup(self._h, keys.data_ptr(), n, out.data_ptr(), int(insert),
                                              self._stream(keys)))
+        self._last_keys = keys
         return out
 
     def accumulate(self, keys, grads) -> None:
-        """Sends grads[i] (gradient dtype, (n, dim)) of keys[i] to the key's owner."""
+        """Sends grads[i] (gradient dtype, (n, dim)) of keys[i] to the key's owner.
+
+        When `keys` is the tensor of the last lookup (the usual forward ->
+        backward pair), the rows follow that lookup's route and no keys are
+        sent again; like the collective transport's plan cache, this assumes
+        the tensor was not modified in between.
+        """
+        if keys is self._last_keys:
+            N.check(self._lib.se_exchange_accumulate_routed(self._h, grads.data_ptr(), keys.numel(),
+                                                            self._stream(keys)))
+            return
         N.check(self._lib.se_exchange_accumulate(self._h, keys.data_ptr(), keys.numel(), grads.data_ptr(),
                                                  self._stream(keys)))
 

@@ -65,7 +65,10 @@ def test_single_rank_exchange_matches_oracle(key_dtype):
         want = single.lookup_or_insert(keys, DIM)
         np.testing.assert_array_equal(out.cpu().numpy().ravel().view(np.uint32), want.view(np.uint32))
         g = torch.from_numpy(grads).cuda()
-        N.check(L.se_exchange_accumulate(ex, k.data_ptr(), len(keys), g.data_ptr(), C.c_void_p(st)))
+        if step % 2:
+            N.check(L.se_exchange_accumulate(ex, k.data_ptr(), len(keys), g.data_ptr(), C.c_void_p(st)))
+        else:  # rows routed like the lookup's keys
+            N.check(L.se_exchange_accumulate_routed(ex, g.data_ptr(), len(keys), C.c_void_p(st)))
         single.accumulate_gradients(keys, grads, DIM)
         store.optimizer_step(1)
         single.optimizer_step(1)
@@ -87,9 +90,18 @@ def test_exchange_rejects_batches_above_its_capacity():
     _connect_local([ex])
     k = torch.zeros(129, dtype=torch.int64, device="cuda")
     out = torch.empty((129, DIM), dtype=torch.float32, device="cuda")
+    g = torch.zeros((129, DIM), dtype=torch.float32, device="cuda")
+    rc = L.se_exchange_accumulate_routed(ex, g.data_ptr(), 129, None)
+    assert rc == N.SE_ERR_INVALID_ARGUMENT
+    assert b"no lookup" in L.se_last_error()
     rc = L.se_exchange_lookup(ex, k.data_ptr(), 129, out.data_ptr(), 1, None)
     assert rc == N.SE_ERR_INVALID_ARGUMENT
     assert b"max_keys_per_rank" in L.se_last_error()
+    N.check(L.se_exchange_lookup(ex, k.data_ptr(), 100, out.data_ptr(), 1, None))
+    rc = L.se_exchange_accumulate_routed(ex, g.data_ptr(), 99, None)
+    assert rc == N.SE_ERR_INVALID_ARGUMENT
+    assert b"must match the keys of the last lookup" in L.se_last_error()
+    N.check(L.se_exchange_check(ex, None))
     N.check(L.se_exchange_destroy(ex))
 
 

@@ -43,11 +43,12 @@ def _worker(rank, port, kind, transport, steps, q):
                                         max_keys_per_rank=1024, timeout_ms=20_000)
         mine, pool = batches(rank, steps)
         rows_seen = []
-        for keys, grads in mine:
+        for s, (keys, grads) in enumerate(mine):
             k = torch.from_numpy(keys).cuda()
             rows = sharded.lookup_or_insert(k, DIM)
             rows_seen.append(rows.cpu().numpy().copy())
-            sharded.accumulate_gradients(k, torch.from_numpy(grads).cuda())
+            # odd steps pass a copy of the keys: the gradient batch is routed by its own keys
+            sharded.accumulate_gradients(k if s % 2 == 0 else k.clone(), torch.from_numpy(grads).cuda())
             sharded.optimizer_step(1)
         final = sharded.lookup(torch.from_numpy(pool).cuda(), DIM).cpu().numpy()
         sharded.check()
