@@ -61,7 +61,7 @@ struct ExView {
   uint32_t row_bytes, grad_bytes;
   uint64_t timeout_ns;
   // byte offsets inside every arena
-  uint64_t o_flags, o_epochs, o_counts, o_gcounts, o_inkeys, o_inpos, o_gkeys, o_ingrads, o_rows, o_words;
+  uint64_t o_flags, o_epochs, o_counts, o_gcounts, o_inkeys, o_inpos, o_gkeys, o_ingrads, o_rows, o_words, o_prefix;
 
   __device__ __forceinline__ uint32_t *flags(uint32_t r) const { return reinterpret_cast<uint32_t *>(peer[r] + o_flags); }
   __device__ __forceinline__ uint32_t *epochs() const { return reinterpret_cast<uint32_t *>(peer[me] + o_epochs); }
@@ -80,6 +80,8 @@ struct ExView {
   // own words: [kExTotal] received gradient rows (accumulate count),
   // [kExTotalStaged] its value before the GRADS wait, [kExStatus] timeout bits
   __device__ __forceinline__ uint32_t *words() const { return reinterpret_cast<uint32_t *>(peer[me] + o_words); }
+  // own [W + 1]: first key inbox slot of every sender of the last forward, then the total
+  __device__ __forceinline__ uint32_t *prefix() const { return reinterpret_cast<uint32_t *>(peer[me] + o_prefix); }
 };
 
 // kExFwdTotal: keys received by the last forward (the row count of a
@@ -139,7 +141,11 @@ __device__ __forceinline__ bool ex_failed(const ExView &x) {
 
 // All threads of one block: bumps this rank's epoch of `kind`, optionally
 // stores this rank's per-owner counts into row `me` of every rank's count
-// matrix, then raises flag (kind, me) on every rank after a system-scope fence.
+// matrix, then raises flag (kind, me) on every rank with a system-scope
+// release store. The release orders everything that happens before it - the
+// counts, and (through the finished-block count and the barrier) the stores
+// of every block of the launch - before the flag; it is the one
+// system-scope fence of the phase per destination (each costs microseconds).
 __device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local) {
   __shared__ uint32_t e;
   __syncthreads();
@@ -154,18 +160,17 @@ __device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local
       uint32_t *cm = x.counts(p, kind) + size_t(x.me) * x.W;
       for (uint32_t d = 0; d < x.W; ++d) cm[d] = __ldcg(counts_local + d);
     }
-    __threadfence_system();
     st_release_sys(x.flags(p) + size_t(kind) * x.W + x.me, e);
   }
 }
 
 // Every thread of a block calls this at the end of its block's share of a
 // launch; true in the one block that finishes last, which then resets the
-// counter. Each block orders its writes before its count with a GPU-scope
-// fence; the last block, having seen every count, issues one system-scope
-// fence, which (fences being cumulative) orders all of the launch's writes,
-// peer stores included, before the flags it raises next. A system-scope
-// fence in every block costs a stall per block instead.
+// counter. Each block orders its stores before its count with a GPU-scope
+// fence (release); the last block's fence after the count (acquire) makes
+// every block's stores happen before what it does next, including the
+// system-scope release of the flags. A system-scope fence in every block
+// would stall each of them for microseconds.
 __device__ bool ex_last_block(const ExView &x, int kind) {
   __shared__ bool last;
   __syncthreads();
@@ -174,7 +179,7 @@ __device__ bool ex_last_block(const ExView &x, int kind) {
     last = atomicAdd(x.done + kind, 1u) == gridDim.x - 1;
     if (last) {
       x.done[kind] = 0;
-      __threadfence_system();
+      __threadfence();
     }
   }
   __syncthreads();
@@ -191,8 +196,23 @@ __device__ void ex_finish(const ExView &x, int kind) {
 // epoch; the kernels after it on the stream read what the senders stored.
 // One waiting thread per phase instead of one per block of the next kernel:
 // a system-scope acquire in every block stalls each of them.
+// After the KEYS wait it also lays out the key inbox once for the owner
+// kernels: each sender's first slot, and the total (bounded by the inbox).
 __global__ void k_ex_wait(ExView x, int kind) {
-  if (threadIdx.x == 0) ex_wait(x, kind);
+  if (threadIdx.x != 0) return;
+  if (!ex_wait(x, kind) || kind != kExKeys) return;
+  uint32_t *prefix = x.prefix();
+  uint32_t run = 0;
+  for (uint32_t s = 0; s < x.W; ++s) {
+    prefix[s] = run;
+    run += __ldcg(x.counts(x.me, kExCounts) + size_t(s) * x.W + x.me);
+  }
+  if (run > x.W * x.M) {
+    atomicOr(x.words() + kExStatus, kExBadIndex);
+    run = x.W * x.M;
+  }
+  prefix[x.W] = run;
+  x.words()[kExFwdTotal] = run;
 }
 
 // Route counts of this rank's keys: per-tile histograms, then (in the block
@@ -347,23 +367,9 @@ template <int LANES, int VEC, bool kInsert>
 __global__ void __launch_bounds__(256)
 k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uint64_t capacity, InitSpec init,
            ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
-  __shared__ uint32_t prefix[kExMaxRanks + 1];
   if (ex_failed(x)) return;
-  if (threadIdx.x == 0) {
-    uint32_t run = 0;
-    for (uint32_t s = 0; s < x.W; ++s) {
-      prefix[s] = run;
-      run += __ldcg(x.counts(x.me, kExCounts) + size_t(s) * x.W + x.me);
-    }
-    if (run > x.W * x.M) {
-      atomicOr(x.words() + kExStatus, kExBadIndex);
-      run = x.W * x.M;
-    }
-    prefix[x.W] = run;
-  }
-  __syncthreads();
-  const uint32_t total = prefix[x.W];
-  if (blockIdx.x == 0 && threadIdx.x == 0) x.words()[kExFwdTotal] = total;
+  const uint32_t *prefix = x.prefix();  // written by the KEYS wait
+  const uint32_t total = __ldcg(prefix + x.W);
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -374,7 +380,7 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
     const uint64_t key = __ldcg(inkeys + i);
     uint32_t pos = __ldcg(inpos + i);
     uint32_t src = 0;
-    while (src + 1 < x.W && prefix[src + 1] <= i) ++src;
+    while (src + 1 < x.W && __ldcg(prefix + src + 1) <= i) ++src;
     if (pos >= x.M) {
       atomicOr(x.words() + kExStatus, kExBadIndex);
       pos = 0;  // inside the buffer; the row there is reported invalid by the status
@@ -426,13 +432,9 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
     }
   }
-  if constexpr (kInsert) {
-    // k_ex_owner_deferred follows; its last block raises the ROWS flags
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence();
-  } else {
-    ex_finish(x, kExRows);
-  }
+  // With kInsert, k_ex_owner_deferred follows on the stream and its last
+  // block raises the ROWS flags (after this launch's stores completed).
+  if constexpr (!kInsert) ex_finish(x, kExRows);
 }
 
 // Deferred keys of k_ex_owner: their claimant has published the row by now.
@@ -447,12 +449,8 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
   const uint32_t count = *def_count;
   for (size_t j = t / LANES; j < count; j += groups) {
     const uint32_t i = def_idx[j];
-    uint32_t run = 0, src = 0;
-    for (uint32_t s = 0; s < x.W; ++s) {
-      const uint32_t c = __ldcg(x.counts(x.me, kExCounts) + size_t(s) * x.W + x.me);
-      if (i >= run && i < run + c) src = s;
-      run += c;
-    }
+    uint32_t src = 0;
+    while (src + 1 < x.W && __ldcg(x.prefix() + src + 1) <= i) ++src;
     uint32_t pos = __ldcg(x.inpos(x.me) + i);
     if (pos >= x.M) pos = 0;  // reported by k_ex_owner
     void *out_row = x.rows(src) + size_t(pos) * x.row_bytes;
@@ -475,8 +473,17 @@ __global__ void __launch_bounds__(256)
 k_ex_rows_out(ExView x, U *__restrict__ out, size_t units) {
   if (ex_failed(x)) return;
   const U *src = reinterpret_cast<const U *>(x.rows(x.me));
-  for (size_t u = size_t(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += size_t(gridDim.x) * blockDim.x)
-    out[u] = __ldcg(src + u);
+  const size_t stride = size_t(gridDim.x) * blockDim.x;
+  constexpr int kIlp = 4;  // loads in flight per thread
+  for (size_t u0 = size_t(blockIdx.x) * blockDim.x + threadIdx.x; u0 < units; u0 += stride * kIlp) {
+    U v[kIlp];
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k)
+      if (u0 + k * stride < units) v[k] = __ldcg(src + u0 + k * stride);
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k)
+      if (u0 + k * stride < units) out[u0 + k * stride] = v[k];
+  }
 }
 
 // Gradient rows for the keys of the last forward, in that forward's route:
@@ -486,14 +493,38 @@ k_ex_rows_out(ExView x, U *__restrict__ out, size_t units) {
 template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot, size_t n,
-                  const U *__restrict__ grads, uint32_t units) {
+                  const U *__restrict__ grads, uint32_t units, uint32_t team) {
+  __shared__ uint8_t *inbox_of[kExMaxRanks];
   if (ex_failed(x)) return;
-  const size_t total = n * units;
-  for (size_t u = size_t(blockIdx.x) * blockDim.x + threadIdx.x; u < total; u += size_t(gridDim.x) * blockDim.x) {
-    const size_t r = u / units, c = u - r * units;
-    if (key_slot[r] >= x.W * x.M) continue;  // skipped (and reported) by the forward
-    U *dst = reinterpret_cast<U *>(x.ingrads(key_pid[r]) + size_t(key_slot[r]) * x.grad_bytes);
-    dst[c] = grads[u];
+  for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) inbox_of[p] = x.ingrads(p);
+  __syncthreads();
+  // A team of `team` lanes (a power of two <= 32) copies one row; a warp
+  // moves 32 / team rows per step and each team keeps kIlp rows in flight.
+  constexpr int kIlp = 4;
+  const uint32_t lane = threadIdx.x & 31u, sub = lane & (team - 1u), per = 32u / team;
+  const size_t warp = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const size_t step = ((size_t(gridDim.x) * blockDim.x) >> 5) * per;
+  const uint32_t inbox = x.W * x.M;
+  for (size_t r0 = warp * per + lane / team; r0 < n; r0 += step * kIlp) {
+    const U *src[kIlp];
+    U *dst[kIlp];
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      const size_t r = r0 + k * step;
+      const uint32_t slot = r < n ? key_slot[r] : inbox;
+      // slot == inbox: past the batch, or skipped (and reported) by the forward
+      dst[k] = slot < inbox ? reinterpret_cast<U *>(inbox_of[key_pid[r]] + size_t(slot) * x.grad_bytes) : nullptr;
+      src[k] = grads + r * units;
+    }
+    for (uint32_t c = sub; c < units; c += team) {
+      U v[kIlp];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k)
+        if (dst[k]) v[k] = src[k][c];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k)
+        if (dst[k]) dst[k][c] = v[k];
+    }
   }
   ex_finish(x, kExGrads);
 }

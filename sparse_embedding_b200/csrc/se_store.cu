@@ -1534,6 +1534,7 @@ struct ExchangeImpl {
     view.o_flags = take(4ull * kExKinds * W);
     view.o_epochs = take(4ull * kExKinds);
     view.o_words = take(4ull * kExWords);
+    view.o_prefix = take(4ull * (W + 1));
     view.o_counts = take(4ull * W * W);
     view.o_gcounts = take(4ull * W * W);
     view.o_inkeys = take(8 * WM);
@@ -1743,9 +1744,11 @@ struct ExchangeImpl {
     auto scatter = [&](auto utag) {
       using U = decltype(utag);
       const uint32_t units = view.grad_bytes / uint32_t(sizeof(U));
+      uint32_t team = 1;
+      while (team < 32 && team < units) team <<= 1;
       StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
-      k_ex_scatter_rows<U><<<grid_for(n * units, 256, 148 * 16), 256, 0, st>>>(view, key_pid, key_slot, n,
-                                                                              static_cast<const U *>(grads), units);
+      k_ex_scatter_rows<U><<<grid_for(n * team, 256, 148 * 8), 256, 0, st>>>(
+          view, key_pid, key_slot, n, static_cast<const U *>(grads), units, team);
       launched("k_ex_scatter_rows");
     };
     if (al % 16 == 0) scatter(uint4{});
