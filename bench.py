@@ -60,6 +60,8 @@ def args_parse():
     p.add_argument("--eager", action="store_true", help="time eager API calls instead of CUDA graphs")
     p.add_argument("--transport", choices=["p2p", "collective"], default="p2p",
                    help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
+    p.add_argument("--loopback", action="store_true",
+                   help="N = 1: route the step through a one-rank peer-memory exchange (its kernels on one GPU)")
     return p.parse_args()
 
 
@@ -245,7 +247,7 @@ def run_ours(args):
         store.lookup_or_insert(torch.from_numpy(chunk).cuda(), DIM)
     torch.cuda.synchronize()
     api = store
-    if world > 1:
+    if world > 1 or args.loopback:
         from sparse_embedding_b200.sharded import ShardedEmbeddingStore
 
         api = ShardedEmbeddingStore(store, "sparse_embedding.hash", transport=args.transport,
@@ -319,7 +321,7 @@ def run_ours(args):
     # Per-kernel device time inside the timed region.
     names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
              "k_group_place", "k_group_apply", "k_group_hot"]
-    if world > 1 and args.transport == "p2p":
+    if (world > 1 and args.transport == "p2p") or args.loopback:
         names += ["k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_rows", "k_ex_scatter_grads"]
     times = {}
     for nm in names:
@@ -371,7 +373,7 @@ def run_ours(args):
     kh = [torch.from_numpy(keys_e[s]).pin_memory() for s in range(K + 1)]
     gh = [torch.from_numpy(grads_e[s]).pin_memory() for s in range(K + 1)]
     e2e_value = None
-    if world == 1:
+    if api is store:
         def host_step(s):
             vals, _ = store.lookup_or_insert(kh[s], DIM)  # host in, host out
             store.accumulate_gradients(kh[s], gh[s])
@@ -417,7 +419,7 @@ def run_ours(args):
                                "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
                                "eps 1e-8, init_acc 0.1), hash partitioner",
                    "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
-                   "transport": (args.transport if world > 1 else "none"),
+                   "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none")),
                    "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
         "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
                    else "eager API calls"),
@@ -429,10 +431,11 @@ def run_ours(args):
         result["forward_lookup"] = fwd
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
+    if api is not store:
+        api.close()
     if world > 1:
         import torch.distributed as dist
 
-        api.close()
         dist.destroy_process_group()
     return result if rank == 0 else None
 

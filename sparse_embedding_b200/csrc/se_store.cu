@@ -1281,7 +1281,9 @@ struct StoreImpl {
     {
       Prof pr(this, "k_accumulate", st);
       const size_t chunks = n * size_t(dim) / (vec4 ? 4 : 1);
-      const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 16);
+      // 4 blocks per SM: enough 16-byte loads in flight to stream the rows,
+      // and few blocks to count in for the commit
+      const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 4);
       if (vec4)
         k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,

@@ -85,7 +85,9 @@ class PeerExchange:
     """One rank's end of the peer-memory exchange for rows of length `dim`.
 
     Collective: every rank of `group` constructs it with the same arguments
-    and then makes the same sequence of lookup / accumulate calls.
+    and then makes the same sequence of lookup / accumulate calls. Without an
+    initialised process group it is a one-rank exchange (every key owned
+    locally), which runs the same kernels on one GPU.
     """
 
     HANDLE_BYTES = 64  # a CUDA IPC memory handle
@@ -95,8 +97,9 @@ class PeerExchange:
         import torch.distributed as dist
 
         self.dist, self.group = dist, group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.distributed = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if self.distributed else 1
+        self.rank = dist.get_rank(group) if self.distributed else 0
         self.store = store
         self.dim = int(dim)
         self.max_keys = int(max_keys_per_rank)
@@ -107,6 +110,9 @@ class PeerExchange:
         N.check(self._lib.se_exchange_create(store._h, N.PART_CODES[kind], self.world, self.rank, self.max_keys,
                                              self.dim, int(timeout_ms), C.byref(h)))
         self._h = h
+        if not self.distributed:
+            N.check(self._lib.se_exchange_connect_local((C.c_void_p * 1)(h.value), 1))
+            return
         buf = (C.c_char * self.HANDLE_BYTES)()
         N.check(self._lib.se_exchange_handle(h, buf, self.HANDLE_BYTES))
         handles = [None] * self.world
@@ -154,7 +160,8 @@ class PeerExchange:
         if self._h is not None:
             torch = torch_mod()
             torch.cuda.synchronize()
-            self.dist.barrier(self.group)  # no peer stores into this arena any more
+            if self.distributed:
+                self.dist.barrier(self.group)  # no peer stores into this arena any more
             N.check(self._lib.se_exchange_destroy(self._h))
             self._h = None
 
@@ -172,8 +179,11 @@ class ShardedEmbeddingStore:
             raise ValueError("the p2p transport needs max_keys_per_rank")
         self.dist = dist
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        distributed = dist.is_available() and dist.is_initialized()
+        if transport == "collective" and not distributed:
+            raise ValueError("the collective transport needs an initialised process group")
+        self.world = dist.get_world_size(group) if distributed else 1
+        self.rank = dist.get_rank(group) if distributed else 0
         self.store = local_store
         self.partitioner_name = partitioner_name
         self.transport = transport
