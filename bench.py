@@ -319,7 +319,7 @@ def run_ours(args):
     elapsed_prof, _, _ = timed_pass(W + K, True)
 
     # Per-kernel device time inside the timed region.
-    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_count", "k_group_alloc",
+    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc",
              "k_group_place", "k_group_apply", "k_group_hot"]
     if (world > 1 and args.transport == "p2p") or args.loopback:
         names += ["k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_rows", "k_ex_scatter_grads"]

@@ -80,6 +80,13 @@ enum StatusBits : uint32_t {
   kStatusPendingOverflow = 8u, // device pending count beyond the host-sized buffers
 };
 
+// Programmatic dependent launch: wait for the previous kernel on the stream
+// (its completion and memory); a no-op when launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel's blocks be scheduled as soon as this grid's blocks
+// have all started (they still wait in pdl_wait for this grid's results).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bits) {
   atomicOr(status, bits);
 }

@@ -199,6 +199,7 @@ __device__ void ex_finish(const ExView &x, int kind) {
 // After the KEYS wait it also lays out the key inbox once for the owner
 // kernels: each sender's first slot, and the total (bounded by the inbox).
 __global__ void k_ex_wait(ExView x, int kind) {
+  pdl_wait();
   if (threadIdx.x != 0) return;
   if (!ex_wait(x, kind) || kind != kExKeys) return;
   uint32_t *prefix = x.prefix();
@@ -223,6 +224,7 @@ template <class K>
 __global__ void __launch_bounds__(kRouteThreads)
 k_ex_count(PartSpec s, ExView x, int kind, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts,
            uint32_t *__restrict__ tile_offsets, uint32_t *__restrict__ counts) {
+  pdl_wait();
   extern __shared__ uint32_t hist[];  // [W]
   if (ex_failed(x)) return;
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) hist[p] = 0;
@@ -278,6 +280,7 @@ __global__ void __launch_bounds__(kRouteThreads)
 k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, const uint32_t *__restrict__ tile_offsets,
              const uint32_t *__restrict__ counts_local, const uint8_t *__restrict__ grads,
              uint32_t *__restrict__ key_pid, uint32_t *__restrict__ key_slot) {
+  pdl_wait();
   extern __shared__ uint32_t sm[];
   uint32_t *warp_base = sm;                   // [kRouteWarps][W]
   uint32_t *remote = sm + kRouteWarps * s.n;  // [W] slot base on each owner minus the local prefix
@@ -367,6 +370,7 @@ template <int LANES, int VEC, bool kInsert>
 __global__ void __launch_bounds__(256)
 k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uint64_t capacity, InitSpec init,
            ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
+  pdl_wait();
   if (ex_failed(x)) return;
   const uint32_t *prefix = x.prefix();  // written by the KEYS wait
   const uint32_t total = __ldcg(prefix + x.W);
@@ -415,7 +419,7 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
     }
     if (kind == kFound) {
       const uint8_t *slab = slabs + size_t(row) * L.stride;
-      for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+      copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
     } else if (kind == kInserted) {
       uint8_t *slab = slabs + size_t(row) * L.stride;
       init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
@@ -442,6 +446,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(256)
 k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const uint32_t *def_count,
                     const uint32_t *def_idx, const unsigned long long *def_word, uint32_t *status) {
+  pdl_wait();
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -461,7 +466,7 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
       continue;
     }
     const uint8_t *slab = slabs + size_t(row) * L.stride;
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+    copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
   }
   ex_finish(x, kExRows);
 }
@@ -471,6 +476,7 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
 template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_rows_out(ExView x, U *__restrict__ out, size_t units) {
+  pdl_wait();
   if (ex_failed(x)) return;
   const U *src = reinterpret_cast<const U *>(x.rows(x.me));
   const size_t stride = size_t(gridDim.x) * blockDim.x;
@@ -494,6 +500,7 @@ template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot, size_t n,
                   const U *__restrict__ grads, uint32_t units, uint32_t team) {
+  pdl_wait();
   __shared__ uint8_t *inbox_of[kExMaxRanks];
   if (ex_failed(x)) return;
   for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) inbox_of[p] = x.ingrads(p);
@@ -533,6 +540,7 @@ k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t
 // received rows from `word` (the device count of the accumulate that
 // follows; 0 when the wait gave up).
 __global__ void k_ex_grads_total(ExView x, int word) {
+  pdl_wait();
   if (threadIdx.x != 0) return;
   uint32_t *w = x.words();
   w[kExTotal] = ex_wait(x, kExGrads) ? w[word] : 0u;

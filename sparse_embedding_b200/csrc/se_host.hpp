@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "../../include/se_gpu.h"
 
@@ -86,6 +87,29 @@ template <class F> int guarded(F &&f) {
 
 inline size_t key_bytes(int key_dtype) { return key_dtype <= SE_KEY_UINT32 ? 4 : 8; }
 inline size_t value_bytes(int value_dtype) { return value_dtype == SE_FLOAT32 ? 4 : 2; }
+
+// Launches a kernel that may start while the previous kernel on the stream
+// finishes (programmatic dependent launch): its blocks are scheduled as the
+// previous grid's blocks retire and wait in pdl_wait() (griddepcontrol.wait)
+// for that grid's completion and memory, so the launch latency of a chain of
+// short kernels overlaps their tails. Captured into graphs as programmatic
+// edges. Every kernel launched this way calls pdl_wait() before it touches
+// memory the previous kernels write or read.
+template <class... KArgs, class... Args>
+inline void pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                Args &&...args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "cudaLaunchKernelEx");
+}
 
 inline unsigned grid_for(size_t work_items, unsigned per_block, unsigned cap = 1u << 20) {
   size_t b = (work_items + per_block - 1) / per_block;

@@ -41,6 +41,7 @@ template <int LANES, class V>
 __global__ void __launch_bounds__(256)
 k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row_units,
          const void *__restrict__ keys, int kdt, size_t n, V *__restrict__ out) {
+  pdl_wait();
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -49,29 +50,18 @@ k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row
   V *dst = out + i * row_units;
   if (row != kNoRow) {
     const V *src = reinterpret_cast<const V *>(slabs + size_t(row) * stride);
-    for (uint32_t u = lane; u < row_units; u += LANES) dst[u] = src[u];
+    constexpr int kIlp = 4;  // loads in flight per lane
+    for (uint32_t u = lane; u < row_units; u += LANES * kIlp) {
+      V v[kIlp];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k)
+        if (u + k * LANES < row_units) v[k] = src[u + k * LANES];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k)
+        if (u + k * LANES < row_units) dst[u + k * LANES] = v[k];
+    }
   } else {
     for (uint32_t u = lane; u < row_units; u += LANES) dst[u] = zero_unit<V>();
-  }
-}
-
-// Copies VEC elements (raw bits) of dtype dt. Source loads go to L2 (ld.cg):
-// in the insert kernel a row may have been initialised by another SM during
-// the same launch, so no L1 line may be trusted.
-template <int VEC>
-__device__ __forceinline__ void copy_elems(void *dst, const void *src, int dt, size_t e) {
-  if (dt == SE_FLOAT32) {
-    if constexpr (VEC == 4)
-      reinterpret_cast<uint4 *>(static_cast<float *>(dst) + e)[0] =
-          __ldcg(reinterpret_cast<const uint4 *>(static_cast<const float *>(src) + e));
-    else
-      static_cast<uint32_t *>(dst)[e] = __ldcg(static_cast<const uint32_t *>(src) + e);
-  } else {
-    if constexpr (VEC == 4)
-      reinterpret_cast<uint2 *>(static_cast<uint16_t *>(dst) + e)[0] =
-          __ldcg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(src) + e));
-    else
-      static_cast<uint16_t *>(dst)[e] = __ldcg(static_cast<const unsigned short *>(src) + e);
   }
 }
 
@@ -81,6 +71,38 @@ __device__ __forceinline__ void zero_elems(void *dst, int dt, size_t e) {
 #pragma unroll
   for (int j = 0; j < VEC; ++j) z[j] = 0.0f;
   stv<VEC>(dst, dt, e, z);
+}
+
+// Copies elements e0, e0 + step, ... (< dim) of a row in VEC-element units,
+// raw bits. Loads go to L2 (ld.cg): in the insert kernels a row may have been
+// initialised by another SM during the same launch, so no L1 line may be
+// trusted. ILP loads are in flight before their stores: a few lanes per key then
+// keep a whole row's loads outstanding, and more keys fit in flight per SM.
+template <class U, int VEC, int ILP>
+__device__ __forceinline__ void copy_units(void *dst, const void *src, uint32_t dim, uint32_t e0, uint32_t step) {
+  const U *s = static_cast<const U *>(src);
+  U *d = static_cast<U *>(dst);
+  for (uint32_t e = e0; e < dim; e += step * ILP) {
+    U v[ILP];
+#pragma unroll
+    for (int k = 0; k < ILP; ++k)
+      if (e + k * step < dim) v[k] = __ldcg(s + (e + k * step) / VEC);
+#pragma unroll
+    for (int k = 0; k < ILP; ++k)
+      if (e + k * step < dim) d[(e + k * step) / VEC] = v[k];
+  }
+}
+
+template <int VEC, int ILP = 4>
+__device__ __forceinline__ void copy_row(void *dst, const void *src, int dt, uint32_t dim, uint32_t e0,
+                                         uint32_t step) {
+  if (dt == SE_FLOAT32) {
+    if constexpr (VEC == 4) copy_units<uint4, 4, ILP>(dst, src, dim, e0, step);
+    else copy_units<unsigned int, 1, ILP>(dst, src, dim, e0, step);
+  } else {
+    if constexpr (VEC == 4) copy_units<uint2, 4, ILP>(dst, src, dim, e0, step);
+    else copy_units<unsigned short, 1, ILP>(dst, src, dim, e0, step);
+  }
 }
 
 // Initialises a freshly claimed slab: param from the initializer (also written
@@ -122,6 +144,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_
                    uint64_t capacity, InitSpec init, const void *__restrict__ keys, int kdt,
                    size_t n, void *__restrict__ out, uint32_t *def_count, uint32_t *def_pos,
                    unsigned long long *def_word, uint32_t *status) {
+  pdl_wait();
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -153,7 +176,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_
   void *out_row = static_cast<uint8_t *>(out) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
   if (kind == kFound) {
     const uint8_t *slab = slabs + size_t(row) * L.stride;
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+    copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
   } else if (kind == kInserted) {
     uint8_t *slab = slabs + size_t(row) * L.stride;
     init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
@@ -177,6 +200,7 @@ __global__ void __launch_bounds__(256)
 k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_count,
            const uint32_t *def_pos, const unsigned long long *def_word, void *__restrict__ out,
            uint32_t *status) {
+  pdl_wait();
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -191,7 +215,51 @@ k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_coun
       continue;
     }
     const uint8_t *slab = slabs + size_t(row) * L.stride;
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) copy_elems<VEC>(out_row, slab, L.pdt, e);
+    copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
+  }
+}
+
+// Per-row counting of the pending entries for optimizer_step's grouping,
+// done where the entries are appended: each row present gets a segment the
+// first time one of its entries is counted; entries whose key is absent when
+// appended are listed and probed again at step time (k_group_fix).
+struct CountWs {
+  uint32_t *row_cnt;    // [capacity] entries of a row in this window (zero between steps)
+  uint32_t *row_seg;    // [capacity] segment of a row in this window
+  uint32_t *seg_row;    // [pending capacity] row of each segment
+  uint32_t *seg_ctr;    // segments registered in this window
+  uint32_t *unres;      // [pending capacity] entries whose key was absent when appended
+  uint32_t *unres_ctr;  // their count
+};
+
+// Whole warp, one entry per lane (valid lanes only): counts the entries'
+// rows (one atomic per distinct row of the warp) and registers new segments
+// (one atomic per warp).
+__device__ __forceinline__ void count_entries(const CountWs &c, bool valid, uint32_t row, uint32_t entry) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const unsigned lt = (1u << lane) - 1u;
+  const bool absent = valid && row == kNoRow;
+  const unsigned abs_mask = __ballot_sync(0xffffffffu, absent);
+  if (abs_mask) {
+    uint32_t base = 0;
+    if (lane == __ffs(abs_mask) - 1) base = atomicAdd(c.unres_ctr, uint32_t(__popc(abs_mask)));
+    base = __shfl_sync(0xffffffffu, base, __ffs(abs_mask) - 1);
+    if (absent) c.unres[base + __popc(abs_mask & lt)] = entry;
+  }
+  const uint32_t key = valid && row != kNoRow ? row : kNoRow;
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  bool fresh = false;
+  if (key != kNoRow && (peers & lt) == 0) fresh = atomicAdd(&c.row_cnt[key], uint32_t(__popc(peers))) == 0u;
+  const unsigned fresh_mask = __ballot_sync(0xffffffffu, fresh);
+  if (fresh_mask) {
+    uint32_t base = 0;
+    if (lane == __ffs(fresh_mask) - 1) base = atomicAdd(c.seg_ctr, uint32_t(__popc(fresh_mask)));
+    base = __shfl_sync(0xffffffffu, base, __ffs(fresh_mask) - 1);
+    if (fresh) {
+      const uint32_t sid = base + __popc(fresh_mask & lt);
+      c.seg_row[sid] = key;
+      c.row_seg[key] = sid;
+    }
   }
 }
 
@@ -206,7 +274,8 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
              const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
              void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
-             uint32_t *err) {
+             uint32_t *err, CountWs cw, int count_rows) {
+  pdl_wait();
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   // Rows are appended at the committed pending count; the batch size is the
@@ -224,11 +293,19 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
   uint32_t *prows = prows_base + base;
   void *pgrads = static_cast<uint8_t *>(pgrads_base) + size_t(base) * dim * (gdt == SE_FLOAT32 ? 4 : 2);
   // Keys and their rows (the directory probe overlaps the gradient copy; a
-  // key absent now is probed again by optimizer_step).
-  for (size_t i = tid; i < n; i += stride) {
-    const uint64_t key = load_key(keys, kdt, i);
-    pkeys[i] = key;
-    prows[i] = dir_find<false>(d, key);
+  // key absent now is probed again by optimizer_step). With count_rows the
+  // rows are counted for the step's grouping here (warp-uniform loop).
+  for (size_t i0 = tid - (tid & 31u); i0 < n; i0 += stride) {
+    const size_t i = i0 + (tid & 31u);
+    const bool valid = i < n;
+    uint32_t row = kNoRow;
+    if (valid) {
+      const uint64_t key = load_key(keys, kdt, i);
+      pkeys[i] = key;
+      row = dir_find<false>(d, key);
+      prows[i] = row;
+    }
+    if (count_rows) count_entries(cw, valid, row, base + uint32_t(i));
   }
   const size_t chunks = n * dim / VEC;
   bool bad = false;
@@ -396,6 +473,9 @@ struct GroupWs {
   uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] mid segments
   uint32_t cap;        // P: entries the [P] buffers hold (the host's pending count)
   uint32_t *status;    // table status word (kStatusPendingOverflow)
+  // cleared by the last block of k_group_hot, the step's last kernel, for
+  // the next window: ctr[0..3], the unresolved count, the pending count
+  uint32_t *done, *unres_ctr, *pending;
 };
 
 // Pending entries of this step: the device count, bounded by the buffers.
@@ -404,47 +484,53 @@ __device__ __forceinline__ uint32_t step_count(const uint32_t *count_p, const Gr
   return c <= w.cap ? c : w.cap;
 }
 
-// Phase 1: row of every entry (probed at accumulate time; absent keys are
-// probed again, then dropped and counted, hogwild_embedding_store.hpp:1942-1952);
-// per-row counts; the first entry to count a row registers it as a new segment.
+// Phase 1 (the counting itself ran when the entries were appended): entries
+// whose key was absent then are probed again; still absent, their gradients
+// are dropped and counted (hogwild_embedding_store.hpp:1942-1952), else they
+// are counted now.
 __global__ void __launch_bounds__(256)
-k_group_count(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t *count_p, GroupWs w,
-              unsigned long long *dropped) {
-  const uint32_t count = step_count(count_p, w);
+k_group_fix(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t *count_p, GroupWs w, CountWs c,
+            unsigned long long *dropped) {
+  pdl_wait();
   if (blockIdx.x == 0 && threadIdx.x == 0 && *count_p > w.cap) raise_status(w.status, kStatusPendingOverflow);
-  __shared__ uint32_t s_rows[256];
-  __shared__ uint32_t s_n, s_base;
-  if (threadIdx.x == 0) s_n = 0;
-  __syncthreads();
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t lane = threadIdx.x & 31u;
-  uint32_t row = kNoRow;
-  if (i < count) {
-    row = w.rows[i];  // probed by accumulate_gradients
+  const uint32_t nunres = min(*c.unres_ctr, w.cap);
+  const uint32_t count = step_count(count_p, w);
+  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < nunres; j += gridDim.x * blockDim.x) {
+    const uint32_t i = c.unres[j];
+    if (i >= count) continue;
+    const uint32_t row = dir_find<false>(d, pkeys[i]);
     if (row == kNoRow) {
-      row = dir_find<false>(d, pkeys[i]);  // inserted since?
-      if (row != kNoRow) w.rows[i] = row;
+      atomicAdd(dropped, 1ull);
+      continue;
+    }
+    w.rows[i] = row;
+    if (atomicAdd(&c.row_cnt[row], 1u) == 0u) {
+      const uint32_t sid = atomicAdd(c.seg_ctr, 1u);
+      c.seg_row[sid] = row;
+      c.row_seg[row] = sid;
     }
   }
-  const unsigned absent = __ballot_sync(0xffffffffu, i < count && row == kNoRow);
-  if (lane == 0 && absent) atomicAdd(dropped, (unsigned long long)__popc(absent));
-  const unsigned peers = __match_any_sync(0xffffffffu, row);
-  if (row != kNoRow && (peers & ((1u << lane) - 1u)) == 0) {
-    const uint32_t old = atomicAdd(&w.row_cnt[row], uint32_t(__popc(peers)));
-    if (old == 0) s_rows[atomicAdd(&s_n, 1u)] = row;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && s_n) s_base = atomicAdd(&w.ctr[0], s_n);
-  __syncthreads();
-  if (threadIdx.x < s_n) {
-    const uint32_t sid = s_base + threadIdx.x, r = s_rows[threadIdx.x];
-    w.seg_row[sid] = r;
-    w.row_seg[r] = sid;
+}
+
+// Counting of host-input batches, which are only kept once their validation
+// passed: entries [*base_p, *base_p + n) of the pending rows.
+__global__ void __launch_bounds__(256)
+k_count_range(const uint32_t *__restrict__ prows, const uint32_t *base_p, uint32_t n, uint32_t pcap, CountWs c) {
+  pdl_wait();
+  const uint32_t base = *base_p;
+  if (uint64_t(base) + n > pcap) return;  // refused by k_accumulate (reported there)
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  for (uint32_t i0 = tid - (tid & 31u); i0 < n; i0 += stride) {
+    const uint32_t i = i0 + (tid & 31u);
+    const bool valid = i < n;
+    count_entries(c, valid, valid ? prows[base + i] : kNoRow, base + i);
   }
 }
 
 // Phase 2: a contiguous slot range per segment (block-aggregated allocation).
 __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
+  pdl_wait();
   using Scan = cub::BlockScan<uint32_t, 256>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ uint32_t s_base;
@@ -464,6 +550,7 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
 
 // Phase 3: every entry takes a slot of its segment (warp-aggregated).
 __global__ void __launch_bounds__(256) k_group_place(const uint32_t *count_p, GroupWs w) {
+  pdl_wait();
   const uint32_t count = step_count(count_p, w);
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
@@ -550,6 +637,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 4)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
+  pdl_wait();
   const uint32_t count = step_count(count_p, w);
   constexpr int GPB = 256 / LANES;
   __shared__ uint32_t s_ord[GPB][LANES];
@@ -598,6 +686,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
             GroupWs w, const uint32_t *count_p) {
+  pdl_wait();
   const uint32_t count = step_count(count_p, w);
   using Scan = cub::BlockScan<uint32_t, kBlockThreads>;
   constexpr int NG = kBlockThreads / LANES;
@@ -747,6 +836,14 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
       w.seg_fill[s] = 0u;
     }
   }
+  // The last block clears the window's counters (every block has read them).
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(w.done, 1u) == gridDim.x - 1) {
+    w.ctr[0] = w.ctr[1] = w.ctr[2] = w.ctr[3] = 0u;
+    *w.unres_ctr = 0u;
+    *w.pending = 0u;
+    *w.done = 0u;
+  }
 }
 
 // Rebuild into a larger directory.
@@ -788,6 +885,15 @@ uint64_t next_pow2(uint64_t x) {
   uint64_t p = 1;
   while (p < x) p <<= 1;
   return p;
+}
+
+// Lanes per key of the gathers: as few as keep each lane's share of the row
+// at <= 8 units, so a warp probes 8 keys at once and each lane keeps its
+// loads of the row in flight together.
+uint32_t gather_lanes(uint64_t units) {
+  uint32_t l = 4;
+  while (l < 32 && uint64_t(l) * 8 < units) l <<= 1;
+  return l;
 }
 
 uint32_t pick_lanes(uint64_t units) {
@@ -835,7 +941,7 @@ enum Ctr : int {
   kCtrSpecialClaim = 1,
   kCtrSpecialRow = 2,
   kCtrDeferred = 3,
-  kCtrGroup = 4,       // words 4-5-6 (+7 spare): GroupWs counters, cleared each step
+  kCtrGroup = 4,       // words 4-7: GroupWs counters ([0] segments of the window), cleared after each step
   kCtrStatus = 12,      // insert / directory errors
   kCtrGradStatus = 13,  // gradient validation of the current accumulate call
   kCtrDropped = 8,      // u64 at words 8-9
@@ -843,7 +949,9 @@ enum Ctr : int {
   kCtrPending = 11,     // pending gradient rows committed on the device
   kCtrAccDone = 14,     // blocks of the running k_accumulate that have finished
   kCtrPendingBackup = 15,
-  kCtrWords = 16,
+  kCtrUnres = 16,      // pending entries whose key was absent when appended (cleared after each step)
+  kCtrStepDone = 17,   // blocks of the running k_group_hot that have finished
+  kCtrWords = 20,
 };
 
 struct Table {
@@ -864,11 +972,14 @@ struct Table {
   unsigned long long *pkeys = nullptr;
   uint32_t *prows = nullptr;  // row of each pending key at accumulate time
   uint8_t *pgrads = nullptr;
+  // counted with the pending entries (pcap entries each): row of each
+  // segment, entries whose key was absent when appended
+  uint32_t *seg_row = nullptr, *unres = nullptr;
   uint64_t pcap = 0, pcount = 0;
   // per-row grouping counters of optimizer_step (capacity entries each)
   uint32_t *row_cnt = nullptr, *row_seg = nullptr;
   // step and insert work buffers
-  Scratch<uint32_t> g_seg_row, g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_mid, def_pos;
+  Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_mid, def_pos;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -884,6 +995,11 @@ struct Table {
     dfree(pgrads);
     dfree(row_cnt);
     dfree(row_seg);
+    dfree(seg_row);
+    dfree(unres);
+  }
+  CountWs count_ws() const {
+    return CountWs{row_cnt, row_seg, seg_row, ctr + kCtrGroup, unres, ctr + kCtrUnres};
   }
 };
 
@@ -1003,12 +1119,20 @@ struct StoreImpl {
   }
 
   // Per-row grouping counters, zero between steps.
-  void alloc_row_arrays(Table &t, uint64_t cap) {
+  // Rows counted since the last step keep their counts and segments when
+  // the arena grows (the first `keep` rows are copied).
+  void alloc_row_arrays(Table &t, uint64_t cap, uint64_t keep = 0, cudaStream_t st = nullptr) {
+    uint32_t *nc = dalloc<uint32_t>(cap), *ns = dalloc<uint32_t>(cap);
+    cuda_check(cudaMemsetAsync(nc, 0, cap * 4, st), "memset row counters");
+    if (keep) {
+      cuda_check(cudaMemcpyAsync(nc, t.row_cnt, keep * 4, cudaMemcpyDeviceToDevice, st), "grow row counters");
+      cuda_check(cudaMemcpyAsync(ns, t.row_seg, keep * 4, cudaMemcpyDeviceToDevice, st), "grow row counters");
+    }
+    cuda_check(cudaStreamSynchronize(st), "sync");
     dfree(t.row_cnt);
     dfree(t.row_seg);
-    t.row_cnt = dalloc<uint32_t>(cap);
-    t.row_seg = dalloc<uint32_t>(cap);
-    cuda_check(cudaMemset(t.row_cnt, 0, cap * 4), "memset row counters");
+    t.row_cnt = nc;
+    t.row_seg = ns;
   }
 
   uint64_t read_rows_used(Table &t, cudaStream_t st) {
@@ -1061,8 +1185,9 @@ struct StoreImpl {
         cuda_check(cudaStreamSynchronize(st), "sync");
         dfree(t.slabs);
         t.slabs = ns;
+        const uint64_t old_cap = t.capacity;
         t.capacity = ncap;
-        alloc_row_arrays(t, ncap);
+        alloc_row_arrays(t, ncap, old_cap, st);
       }
       if (need > dir_limit(t.nbuckets)) {
         uint64_t nb = t.nbuckets;
@@ -1092,19 +1217,27 @@ struct StoreImpl {
     auto *nk = dalloc<unsigned long long>(ncap);
     auto *nr = dalloc<uint32_t>(ncap);
     auto *ng = dalloc<uint8_t>(size_t(ncap) * gb);
+    auto *nsr = dalloc<uint32_t>(ncap);
+    auto *nu = dalloc<uint32_t>(ncap);
     if (t.pcount) {
       cuda_check(cudaMemcpyAsync(nk, t.pkeys, t.pcount * 8, cudaMemcpyDeviceToDevice, st), "grow pending");
       cuda_check(cudaMemcpyAsync(nr, t.prows, t.pcount * 4, cudaMemcpyDeviceToDevice, st), "grow pending");
       cuda_check(cudaMemcpyAsync(ng, t.pgrads, size_t(t.pcount) * gb, cudaMemcpyDeviceToDevice, st),
                  "grow pending");
+      cuda_check(cudaMemcpyAsync(nsr, t.seg_row, t.pcount * 4, cudaMemcpyDeviceToDevice, st), "grow pending");
+      cuda_check(cudaMemcpyAsync(nu, t.unres, t.pcount * 4, cudaMemcpyDeviceToDevice, st), "grow pending");
     }
     cuda_check(cudaStreamSynchronize(st), "sync");
     dfree(t.pkeys);
     dfree(t.prows);
     dfree(t.pgrads);
+    dfree(t.seg_row);
+    dfree(t.unres);
     t.pkeys = nk;
     t.prows = nr;
     t.pgrads = ng;
+    t.seg_row = nsr;
+    t.unres = nu;
     t.pcap = ncap;
   }
 
@@ -1160,13 +1293,13 @@ struct StoreImpl {
         using V = decltype(vtag);
         const uint32_t units = uint32_t(row_bytes / sizeof(V));
         Prof pr(this, "k_lookup", st);
-        k_lookup<LN, V><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+        pdl(k_lookup<LN, V>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
             d, t.slabs, t.L.stride, units, dkeys, cfg.key_dtype, n, static_cast<V *>(dout));
         launched("k_lookup");
       };
       auto by_lanes = [&](auto vtag) {
         using V = decltype(vtag);
-        const uint32_t ln = pick_lanes(row_bytes / sizeof(V));
+        const uint32_t ln = gather_lanes(row_bytes / sizeof(V));
         switch (ln) {
         case 4: go(std::integral_constant<int, 4>{}, vtag); break;
         case 8: go(std::integral_constant<int, 8>{}, vtag); break;
@@ -1190,18 +1323,18 @@ struct StoreImpl {
         constexpr int VC = decltype(vec_tag)::value;
         {
           Prof pr(this, "k_lookup_or_insert", st);
-          k_lookup_or_insert<LN, VC><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+          pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
               t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity, init, dkeys, cfg.key_dtype, n,
               dout, t.ctr + kCtrDeferred, dpos, dword, t.ctr + kCtrStatus);
           launched("k_lookup_or_insert");
         }
         Prof pr(this, "k_deferred", st);
-        k_deferred<LN, VC><<<grid_for(n * LN, 256, 148 * 4), 256, 0, st>>>(
+        pdl(k_deferred<LN, VC>, grid_for(n * LN, 256, 148 * 4), 256, 0, st,
             t.L, t.slabs, t.ctr + kCtrDeferred, dpos, dword, dout, t.ctr + kCtrStatus);
         launched("k_deferred");
       };
       auto by_lanes = [&](auto vec_tag) {
-        const uint32_t ln = vec4 ? t.lanes : pick_lanes(uint64_t(dim));
+        const uint32_t ln = gather_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim));
         switch (ln) {
         case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
         case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
@@ -1278,6 +1411,7 @@ struct StoreImpl {
       cuda_check(cudaMemcpyAsync(t.ctr + kCtrPendingBackup, t.ctr + kCtrPending, 4, cudaMemcpyDeviceToDevice, st),
                  "pending backup");
     }
+    const CountWs cw = t.count_ws();
     {
       Prof pr(this, "k_accumulate", st);
       const size_t chunks = n * size_t(dim) / (vec4 ? 4 : 1);
@@ -1285,15 +1419,15 @@ struct StoreImpl {
       // and few blocks to count in for the commit
       const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 4);
       if (vec4)
-        k_accumulate<4><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
+        pdl(k_accumulate<4>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
                                               size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus);
+                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0);
       else
-        k_accumulate<1><<<grid, 256, 0, st>>>(t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
+        pdl(k_accumulate<1>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
                                               size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus);
+                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0);
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1307,6 +1441,10 @@ struct StoreImpl {
         cuda_check(cudaStreamSynchronize(st), "sync");
         throw std::overflow_error("gradient scale storage exceeds configured dtype");
       }
+      // the batch is kept: count its rows for the step's grouping
+      pdl(k_count_range, grid_for(n, 256, 148 * 4), 256, 0, st, t.prows, t.ctr + kCtrPendingBackup, uint32_t(n),
+                                                               uint32_t(t.pcap), cw);
+      launched("k_count_range");
     }
     t.pcount += n;  // upper bound of the rows pending on the device
   }
@@ -1322,8 +1460,13 @@ struct StoreImpl {
     for (auto &tp : tables) {
       Table &t = *tp;
       if (t.pcount == 0) continue;
-      if (apply) step_table(t, nsteps, st);
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrPending, 0, 4, st), "pending clear");
+      if (apply) {
+        step_table(t, nsteps, st);  // its last kernel clears the window's counters
+      } else {
+        cuda_check(cudaMemsetAsync(t.ctr + kCtrGroup, 0, 16, st), "memset group counters");
+        cuda_check(cudaMemsetAsync(t.ctr + kCtrUnres, 0, 4, st), "memset unresolved counter");
+        cuda_check(cudaMemsetAsync(t.ctr + kCtrPending, 0, 4, st), "pending clear");
+      }
       t.pcount = 0;
     }
   }
@@ -1334,7 +1477,7 @@ struct StoreImpl {
     w.rows = t.prows;
     w.row_cnt = t.row_cnt;
     w.row_seg = t.row_seg;
-    w.seg_row = t.g_seg_row.get(P);
+    w.seg_row = t.seg_row;  // filled as the entries were counted
     w.seg_cnt = t.g_seg_cnt.get(P);
     w.seg_off = t.g_seg_off.get(P);
     const size_t fill_cap_before = t.g_seg_fill.cap;
@@ -1356,22 +1499,26 @@ struct StoreImpl {
     w.ctr = t.ctr + kCtrGroup;
     w.cap = P;
     w.status = t.ctr + kCtrStatus;
-    cuda_check(cudaMemsetAsync(w.ctr, 0, 16, st), "memset group counters");
+    // ctr[0] (segments) was counted with the entries; ctr[1..3] are zero
+    // (cleared with the window's other counters by the previous step)
+    w.done = t.ctr + kCtrStepDone;
+    w.unres_ctr = t.ctr + kCtrUnres;
+    w.pending = t.ctr + kCtrPending;
     auto *dropped = reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped);
     const unsigned g = grid_for(P, 256);
     {
-      Prof pr(this, "k_group_count", st);
-      k_group_count<<<g, 256, 0, st>>>(t.dir(), t.pkeys, t.ctr + kCtrPending, w, dropped);
-      launched("k_group_count");
+      Prof pr(this, "k_group_fix", st);
+      pdl(k_group_fix, 148, 256, 0, st, t.dir(), t.pkeys, t.ctr + kCtrPending, w, t.count_ws(), dropped);
+      launched("k_group_fix");
     }
     {
       Prof pr(this, "k_group_alloc", st);
-      k_group_alloc<<<g, 256, 0, st>>>(w);
+      pdl(k_group_alloc, g, 256, 0, st, w);
       launched("k_group_alloc");
     }
     {
       Prof pr(this, "k_group_place", st);
-      k_group_place<<<g, 256, 0, st>>>(t.ctr + kCtrPending, w);
+      pdl(k_group_place, g, 256, 0, st, t.ctr + kCtrPending, w);
       launched("k_group_place");
     }
     OptSpec o{};
@@ -1395,12 +1542,12 @@ struct StoreImpl {
       constexpr int VC = decltype(vec_tag)::value;
       {
         Prof pr(this, "k_group_apply", st);
-        k_group_apply<LN, VC><<<grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st>>>(
+        pdl(k_group_apply<LN, VC>, grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st,
             t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
         launched("k_group_apply");
       }
       Prof pr(this, "k_group_hot", st);
-      k_group_hot<LN, VC><<<148 * 2, kBlockThreads, 0, st>>>(t.L, t.slabs, o, gdt, t.pgrads, w,
+      pdl(k_group_hot<LN, VC>, 148 * 2, kBlockThreads, 0, st, t.L, t.slabs, o, gdt, t.pgrads, w,
                                                              t.ctr + kCtrPending);
       launched("k_group_hot");
     };
@@ -1610,7 +1757,7 @@ struct ExchangeImpl {
     const uint32_t tiles = std::max(uint32_t((n + kExTile - 1) / kExTile), 1u);
     uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
     uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
-    k_ex_count<K><<<tiles, kRouteThreads, W * 4, st>>>(spec, view, kind, keys, n, tile_counts, tile_offsets, counts);
+    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, kind, keys, n, tile_counts, tile_offsets, counts);
     launched("k_ex_count");
     wait(kind, st);
     return counts;
@@ -1618,7 +1765,7 @@ struct ExchangeImpl {
 
   // Stream-ordered wait for every rank's flag of `kind`.
   void wait(int kind, cudaStream_t st) {
-    k_ex_wait<<<1, 32, 0, st>>>(view, kind);
+    pdl(k_ex_wait, 1, 32, 0, st, view, kind);
     launched("k_ex_wait");
   }
 
@@ -1640,7 +1787,7 @@ struct ExchangeImpl {
       const K *k = static_cast<const K *>(keys);
       const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st);
       StoreImpl::Prof pr(store, "k_ex_scatter_keys", st);
-      k_ex_scatter<K, false, uint4><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
+      pdl(k_ex_scatter<K, false, uint4>, std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st,
           spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot);
       launched("k_ex_scatter");
     });
@@ -1660,22 +1807,22 @@ struct ExchangeImpl {
       const unsigned grid = grid_for(M * LN, 256, 148 * 16);
       StoreImpl::Prof pr(store, "k_ex_owner", st);
       if (insert) {
-        k_ex_owner<LN, VC, true><<<grid, 256, 0, st>>>(t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+        pdl(k_ex_owner<LN, VC, true>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
                                                         init, view, t.ctr + kCtrDeferred, def_idx, def_word,
                                                         t.ctr + kCtrStatus);
         launched("k_ex_owner");
-        k_ex_owner_deferred<LN, VC><<<148, 256, 0, st>>>(t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
+        pdl(k_ex_owner_deferred<LN, VC>, 148, 256, 0, st, t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
                                                              def_word, t.ctr + kCtrStatus);
         launched("k_ex_owner_deferred");
       } else {
-        k_ex_owner<LN, VC, false><<<grid, 256, 0, st>>>(t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+        pdl(k_ex_owner<LN, VC, false>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
                                                          init, view, nullptr, nullptr, nullptr,
                                                          t.ctr + kCtrStatus);
         launched("k_ex_owner");
       }
     };
     auto by_lanes = [&](auto vec_tag) {
-      const uint32_t ln = t.vec == 4 ? t.lanes : pick_lanes(uint64_t(dim));
+      const uint32_t ln = gather_lanes(t.vec == 4 ? uint64_t(dim) / 4 : uint64_t(dim));
       switch (ln) {
       case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
       case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
@@ -1695,7 +1842,7 @@ struct ExchangeImpl {
       using U = decltype(utag);
       const size_t units = bytes / sizeof(U);
       StoreImpl::Prof pr(store, "k_ex_rows_out", st);
-      k_ex_rows_out<U><<<grid_for(units, 256, 148 * 8), 256, 0, st>>>(view, static_cast<U *>(out), units);
+      pdl(k_ex_rows_out<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), units);
       launched("k_ex_rows_out");
     };
     if (al % 16 == 0) copy_out(uint4{});
@@ -1716,7 +1863,7 @@ struct ExchangeImpl {
       auto scatter = [&](auto utag) {
         using U = decltype(utag);
         StoreImpl::Prof pr(store, "k_ex_scatter_grads", st);
-        k_ex_scatter<K, true, U><<<std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st>>>(
+        pdl(k_ex_scatter<K, true, U>, std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st,
             spec, view, k, n, route[1] + size_t(tiles_cap) * W, counts, static_cast<const uint8_t *>(grads), nullptr,
             nullptr);
         launched("k_ex_scatter");
@@ -1725,7 +1872,7 @@ struct ExchangeImpl {
       else if (al % 4 == 0) scatter(uint32_t{});
       else scatter(uint16_t{});
     });
-    k_ex_grads_total<<<1, 32, 0, st>>>(view, kExTotalStaged);
+    pdl(k_ex_grads_total, 1, 32, 0, st, view, kExTotalStaged);
     launched("k_ex_grads_total");
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_gkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
@@ -1749,14 +1896,14 @@ struct ExchangeImpl {
       uint32_t team = 1;
       while (team < 32 && team < units) team <<= 1;
       StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
-      k_ex_scatter_rows<U><<<grid_for(n * team, 256, 148 * 8), 256, 0, st>>>(
+      pdl(k_ex_scatter_rows<U>, grid_for(n * team, 256, 148 * 8), 256, 0, st,
           view, key_pid, key_slot, n, static_cast<const U *>(grads), units, team);
       launched("k_ex_scatter_rows");
     };
     if (al % 16 == 0) scatter(uint4{});
     else if (al % 4 == 0) scatter(uint32_t{});
     else scatter(uint16_t{});
-    k_ex_grads_total<<<1, 32, 0, st>>>(view, kExFwdTotal);
+    pdl(k_ex_grads_total, 1, 32, 0, st, view, kExFwdTotal);
     launched("k_ex_grads_total");
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_inkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
