@@ -42,6 +42,7 @@ DIM = 64
 BATCH = 65_536
 NUM_KEYS = 10_000_000
 FWD_KEYS, FWD_DIM, FWD_BATCH, FWD_BATCHES = 1_000_000, 32, 4096, 400
+WIDE_KEYS, WIDE_DIM, WIDE_BATCH, WIDE_BATCHES = 200_000_000, 256, 262_144, 40
 KEY_BYTES, M_BYTES = 8, 16
 FALLBACK_HBM_GBS = 6650.0
 # value = train-step keys/s; the forward-lookup figure rides in "forward_lookup".
@@ -57,6 +58,8 @@ def args_parse():
     p.add_argument("--num-keys", type=int, default=NUM_KEYS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-forward", action="store_true")
+    p.add_argument("--wide-keys", type=int, default=WIDE_KEYS,
+                   help="keys of the wide-row forward store (weight-only, dim 256 bf16); 0 skips it")
     p.add_argument("--eager", action="store_true", help="time eager API calls instead of CUDA graphs")
     p.add_argument("--transport", choices=["p2p", "collective"], default="p2p",
                    help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
@@ -406,9 +409,11 @@ def run_ours(args):
     e2e = {"value": e2e_value, "unit": "keys/s", "h2d_bytes_per_step": BATCH * (2 * KEY_BYTES + R) * world,
            "d2h_bytes_per_step": BATCH * R * world}
 
-    fwd = None
+    fwd = wide = None
     if world == 1 and not args.no_forward:
         fwd = forward_bench(se, torch, N)
+        if args.wide_keys > 0:
+            wide = forward_wide_bench(se, torch, N, args.wide_keys)
 
     result = {
         "metric": METRIC,
@@ -429,6 +434,8 @@ def run_ours(args):
     }
     if fwd:
         result["forward_lookup"] = fwd
+    if wide:
+        result["forward_wide"] = wide
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
     if api is not store:
@@ -478,6 +485,54 @@ def forward_bench(se, torch, N):
             "us_per_call": el / FWD_BATCHES * 1e6, "kernel_us": kms / kcnt * 1e3,
             "kernel_achieved_gbs": round(kern_gbs, 1), "kernel_frac": round(kern_gbs / peak, 4),
             "note": "4,096-key batches are launch-latency bound; the tables fit in L2 partly"}
+
+
+def forward_wide_bench(se, torch, N, num_keys):
+    """Weight-only inference store: int32 keys 0..num_keys-1, dim 256 bf16
+    rows from the initializer; forward_lookup of 262,144-key batches uniform
+    over the keys (the table is far larger than L2, so every row comes from
+    HBM). Algorithmic bytes per key: key 4 + directory 16 + row read 512 +
+    row write 512."""
+    import ctypes
+
+    from sparse_embedding_b200.workloads import InferenceWorkload
+
+    wl = InferenceWorkload(num_keys=num_keys, dim=WIDE_DIM, batch=WIDE_BATCH)
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[WIDE_DIM], key_dtype="int32", value_dtype="bfloat16",
+                                                 enable_optimizer=False, initial_capacity=num_keys))
+    chunk = 1 << 22
+    for s0 in range(0, num_keys, chunk):
+        keys = torch.arange(s0, min(s0 + chunk, num_keys), dtype=torch.int32, device="cuda")
+        store.lookup_or_insert(keys, WIDE_DIM)
+    torch.cuda.synchronize()
+    batches = torch.from_numpy(wl.batches(WIDE_BATCHES)).cuda()
+    out = torch.empty(WIDE_BATCH * WIDE_DIM, dtype=torch.bfloat16, device="cuda")
+    lib = N.lib()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run(i):
+        N.check(lib.se_forward_lookup_dim(store._h, batches[i].data_ptr(), WIDE_BATCH, WIDE_DIM, out.data_ptr(),
+                                          ctypes.c_void_p(st)))
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(WIDE_BATCHES):
+        run(i)
+    b.record()
+    torch.cuda.synchronize()
+    el = a.elapsed_time(b) / 1e3
+    peak, _ = measured_hbm()
+    per_key = 4 + M_BYTES + 2 * WIDE_DIM * 2
+    gbs = per_key * WIDE_BATCH * WIDE_BATCHES / el / 1e9
+    del store
+    torch.cuda.empty_cache()
+    return {"workload": f"weight-only dim 256 bf16, {num_keys:,} int32 keys, {WIDE_BATCHES} batches x "
+                        f"262,144 keys uniform (table {num_keys * 512 / 1e9:.0f} GB >> L2)",
+            "value": WIDE_BATCH * WIDE_BATCHES / el / 1e6, "unit": "Mkeys/s",
+            "us_per_call": el / WIDE_BATCHES * 1e6, "algorithmic_bytes_per_key": per_key,
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_gbs": peak}
 
 
 # ---------------------------------------------------------------------------

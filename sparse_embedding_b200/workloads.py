@@ -107,3 +107,99 @@ class TrainWorkload:
             keys[s] = k.view(np.int64)
         grads = (rng.standard_normal((count, self.batch, self.dim), dtype=np.float32) * np.float32(self.sigma))
         return keys, grads
+
+
+@dataclass
+class DlrmWorkload:
+    """DLRM-style multi-table step: `tables` tables with row counts
+    log-uniform in [min_rows, max_rows] (seeded), dim 128; per sample and
+    table max(1, Poisson(mean_ids)) ids drawn Zipf(alpha) over the table's
+    rows. A key is fmix64((table << 40) | id): a pre-mixed u64, so every
+    partitioner spreads the tables over the GPUs. The harness sum-pools the
+    rows of each (sample, table) and broadcasts a N(0, sigma) pooled
+    gradient back to each of its ids."""
+
+    tables: int = 26
+    min_rows: int = 1_000
+    max_rows: int = 40_000_000
+    dim: int = 128
+    batch: int = 8192
+    mean_ids: float = 20.0
+    alpha: float = 1.2
+    sigma: float = 1e-3
+    seed: int = 0xD1A
+    rank: int = 0
+
+    def table_rows(self) -> np.ndarray:
+        rng = np.random.default_rng(self.seed)
+        lo, hi = np.log(self.min_rows), np.log(self.max_rows)
+        return np.round(np.exp(rng.uniform(lo, hi, size=self.tables))).astype(np.int64)
+
+    def make_batch(self, step: int):
+        """(keys u64 [n], bag [n] int64 = sample * tables + table, pooled grads
+        [batch * tables, dim] float32) for one step."""
+        rows = self.table_rows()
+        rng = np.random.default_rng([self.seed, self.rank, step])
+        keys, bags = [], []
+        for t in range(self.tables):
+            z = Zipf(int(rows[t]), self.alpha, self.seed + t)
+            counts = np.maximum(1, rng.poisson(self.mean_ids, size=self.batch))
+            ids = z.sample(rng, int(counts.sum())).astype(np.uint64)
+            keys.append(fmix64((np.uint64(t) << np.uint64(40)) | ids))
+            bags.append(np.repeat(np.arange(self.batch, dtype=np.int64) * self.tables + t, counts))
+        pooled = rng.standard_normal((self.batch * self.tables, self.dim), dtype=np.float32) * np.float32(self.sigma)
+        return np.concatenate(keys), np.concatenate(bags), pooled
+
+
+@dataclass
+class CapacityWorkload:
+    """Capacity run: `num_keys` u64 keys splitmix64(i), dim 64 fp32 with Adam
+    state; batches of `batch` keys, (1 - new_fraction) Zipf(alpha) over the
+    keys and new_fraction never-seen keys; gradients N(0, sigma). On g GPUs,
+    rank r warms the keys the partitioner maps to r."""
+
+    num_keys: int = 1_500_000_000
+    dim: int = 64
+    batch: int = 262_144
+    alpha: float = 1.05
+    new_fraction: float = 0.01
+    sigma: float = 1e-3
+    seed: int = 0xCA9
+    rank: int = 0
+
+    def warm_keys(self) -> np.ndarray:
+        return splitmix64_sequence(np.arange(self.num_keys))
+
+    def make_batches(self, count: int, start_step: int = 0):
+        z = Zipf(self.num_keys, self.alpha, self.seed)
+        rng = np.random.default_rng([self.seed, self.rank, start_step])
+        n_new = int(round(self.batch * self.new_fraction))
+        keys = np.empty((count, self.batch), dtype=np.uint64)
+        for s in range(count):
+            old = splitmix64_sequence(z.sample(rng, self.batch - n_new))
+            base = self.num_keys + ((start_step + s) * 1024 + self.rank) * n_new
+            new = splitmix64_sequence(np.arange(base, base + n_new, dtype=np.uint64))
+            k = np.concatenate([old, new])
+            rng.shuffle(k)
+            keys[s] = k
+        grads = rng.standard_normal((count, self.batch, self.dim), dtype=np.float32) * np.float32(self.sigma)
+        return keys, grads
+
+
+@dataclass
+class InferenceWorkload:
+    """Weight-only inference store: int32 keys 0 .. num_keys-1, dim 256
+    bf16 values from the Uniform(-0.05, 0.05) initializer, no optimizer;
+    forward_lookup batches of `batch` keys uniform over the key set."""
+
+    num_keys: int = 200_000_000
+    dim: int = 256
+    batch: int = 262_144
+    seed: int = 0x1BF
+
+    def warm_keys(self) -> np.ndarray:
+        return np.arange(self.num_keys, dtype=np.int32)
+
+    def batches(self, count: int, start: int = 0) -> np.ndarray:
+        rng = np.random.default_rng([self.seed, start])
+        return rng.integers(0, self.num_keys, size=(count, self.batch), dtype=np.int32)
