@@ -18,10 +18,10 @@
 //             key's rows arrive in the order of the concatenated batch).
 //
 // Each phase ends with a flag per (kind, sender) in the receiver's arena,
-// written with the sender's epoch for that kind by the block of the phase's
-// kernel that finishes last (after every block's system-scope fence); a
-// receiver waits until every sender's flag reaches its own epoch. Waits are
-// bounded in time: past the exchange's timeout the kernel records it and returns.
+// written with the sender's epoch for that kind by a one-block sync kernel
+// that runs after the phase's data kernel completed; the same kernel then
+// waits until every sender's flag reaches its own epoch. Waits are bounded in
+// time: past the exchange's timeout the kernel records it and returns.
 //
 // One buffer per kind suffices when every rank makes the same sequence of
 // calls:
@@ -55,13 +55,13 @@ constexpr uint64_t kSpinLimit = 1ull << 28;  // hard cap on polls (>= 128 ns eac
 
 struct ExView {
   uint8_t *const *peer;  // [W] arena base of every rank (own included), device array
-  uint32_t *done;        // [kExKinds] finished blocks of the running launch per kind (own memory)
   uint32_t W, me;
   uint32_t M;            // keys per rank per call: rows of a row buffer; an inbox holds W * M
   uint32_t row_bytes, grad_bytes;
   uint64_t timeout_ns;
   // byte offsets inside every arena
-  uint64_t o_flags, o_epochs, o_counts, o_gcounts, o_inkeys, o_inpos, o_gkeys, o_ingrads, o_rows, o_words, o_prefix;
+  uint64_t o_flags, o_epochs, o_counts, o_gcounts, o_inkeys, o_inpos, o_inrow, o_gkeys, o_ingrads, o_rows, o_words,
+      o_prefix;
 
   __device__ __forceinline__ uint32_t *flags(uint32_t r) const { return reinterpret_cast<uint32_t *>(peer[r] + o_flags); }
   __device__ __forceinline__ uint32_t *epochs() const { return reinterpret_cast<uint32_t *>(peer[me] + o_epochs); }
@@ -72,6 +72,8 @@ struct ExView {
     return reinterpret_cast<unsigned long long *>(peer[r] + o_inkeys);
   }
   __device__ __forceinline__ uint32_t *inpos(uint32_t r) const { return reinterpret_cast<uint32_t *>(peer[r] + o_inpos); }
+  // own [W * M]: row of each key inbox entry after the forward (kNoRow: none)
+  __device__ __forceinline__ uint32_t *inrow() const { return reinterpret_cast<uint32_t *>(peer[me] + o_inrow); }
   __device__ __forceinline__ unsigned long long *gkeys(uint32_t r) const {
     return reinterpret_cast<unsigned long long *>(peer[r] + o_gkeys);
   }
@@ -142,10 +144,7 @@ __device__ __forceinline__ bool ex_failed(const ExView &x) {
 // All threads of one block: bumps this rank's epoch of `kind`, optionally
 // stores this rank's per-owner counts into row `me` of every rank's count
 // matrix, then raises flag (kind, me) on every rank with a system-scope
-// release store. The release orders everything that happens before it - the
-// counts, and (through the finished-block count and the barrier) the stores
-// of every block of the launch - before the flag; it is the one
-// system-scope fence of the phase per destination (each costs microseconds).
+// release store.
 __device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local) {
   __shared__ uint32_t e;
   __syncthreads();
@@ -158,50 +157,40 @@ __device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local
   for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) {
     if (counts_local) {
       uint32_t *cm = x.counts(p, kind) + size_t(x.me) * x.W;
-      for (uint32_t d = 0; d < x.W; ++d) cm[d] = __ldcg(counts_local + d);
+      for (uint32_t d = 0; d < x.W; ++d) cm[d] = counts_local[d];
     }
     st_release_sys(x.flags(p) + size_t(kind) * x.W + x.me, e);
   }
-}
-
-// Every thread of a block calls this at the end of its block's share of a
-// launch; true in the one block that finishes last, which then resets the
-// counter. Each block orders its stores before its count with a GPU-scope
-// fence (release); the last block's fence after the count (acquire) makes
-// every block's stores happen before what it does next, including the
-// system-scope release of the flags. A system-scope fence in every block
-// would stall each of them for microseconds.
-__device__ bool ex_last_block(const ExView &x, int kind) {
-  __shared__ bool last;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last = atomicAdd(x.done + kind, 1u) == gridDim.x - 1;
-    if (last) {
-      x.done[kind] = 0;
-      __threadfence();
-    }
-  }
-  __syncthreads();
-  return last;
 }
 
-// End of a launch that wrote data of `kind` into peers' arenas: the last
-// block raises the flags.
-__device__ void ex_finish(const ExView &x, int kind) {
-  if (ex_last_block(x, kind)) ex_raise(x, kind, nullptr);
-}
-
-// Waits (one thread) until every sender's flag of `kind` reached this rank's
-// epoch; the kernels after it on the stream read what the senders stored.
-// One waiting thread per phase instead of one per block of the next kernel:
-// a system-scope acquire in every block stalls each of them.
-// After the KEYS wait it also lays out the key inbox once for the owner
-// kernels: each sender's first slot, and the total (bounded by the inbox).
-__global__ void k_ex_wait(ExView x, int kind) {
+// One small block between a phase's data kernel and the kernels that read
+// what the peers stored: raises this rank's flags of `kind` (the data kernel
+// before it on the stream has completed, with all its stores, peer stores
+// included, when pdl_wait returns), then waits until every sender's flag of
+// `kind` reached this rank's epoch. A separate kernel per phase instead of a
+// last-block tail in the data kernel (a GPU-scope fence and a counter atomic
+// in every block, then the system-scope release: ~3 us per phase) and
+// instead of a wait in every block of the next kernel.
+// After KEYS it also lays out the key inbox once for the owner kernels (each
+// sender's first slot and the total, bounded by the inbox); after GRADS it
+// sets the row count of the accumulate that follows from `total_word` (0
+// when the wait gave up).
+__global__ void k_ex_sync(ExView x, int kind, int total_word) {
   pdl_wait();
+  if (ex_failed(x)) {  // a failed exchange raises nothing more
+    if (threadIdx.x == 0 && kind == kExGrads) x.words()[kExTotal] = 0u;
+    return;
+  }
+  ex_raise(x, kind, nullptr);
   if (threadIdx.x != 0) return;
-  if (!ex_wait(x, kind) || kind != kExKeys) return;
+  const bool ok = ex_wait(x, kind);
+  if (kind == kExGrads) {
+    uint32_t *w = x.words();
+    w[kExTotal] = ok ? w[total_word] : 0u;
+    return;
+  }
+  if (!ok || kind != kExKeys) return;
   uint32_t *prefix = x.prefix();
   uint32_t run = 0;
   for (uint32_t s = 0; s < x.W; ++s) {
@@ -216,14 +205,11 @@ __global__ void k_ex_wait(ExView x, int kind) {
   x.words()[kExFwdTotal] = run;
 }
 
-// Route counts of this rank's keys: per-tile histograms, then (in the block
-// that finishes last) the partition-major exclusive offsets of every tile and
-// the per-owner counts, which it publishes as `kind` (COUNTS or GCOUNTS).
-// Launched with max(tiles, 1) blocks of kExTile keys.
+// Route counts of this rank's keys: per-tile histograms by owner. Launched
+// with max(tiles, 1) blocks of kExTile keys.
 template <class K>
 __global__ void __launch_bounds__(kRouteThreads)
-k_ex_count(PartSpec s, ExView x, int kind, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts,
-           uint32_t *__restrict__ tile_offsets, uint32_t *__restrict__ counts) {
+k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts) {
   pdl_wait();
   extern __shared__ uint32_t hist[];  // [W]
   if (ex_failed(x)) return;
@@ -233,22 +219,31 @@ k_ex_count(PartSpec s, ExView x, int kind, const K *__restrict__ keys, size_t co
   if (i < count) atomicAdd(&hist[partition_of<K>(s, keys[i])], 1u);
   __syncthreads();
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) tile_counts[size_t(blockIdx.x) * s.n + p] = hist[p];
-  if (!ex_last_block(x, kind)) return;
+}
+
+// One block: the partition-major exclusive offsets of every tile and the
+// per-owner counts, which it stores into every owner's count matrix and
+// publishes as `kind` (COUNTS or GCOUNTS); then waits for every sender's.
+__global__ void __launch_bounds__(kRouteThreads)
+k_ex_sync_counts(ExView x, int kind, uint32_t tiles, const uint32_t *__restrict__ tile_counts,
+                 uint32_t *__restrict__ tile_offsets, uint32_t *__restrict__ counts) {
+  pdl_wait();
   using Scan = cub::BlockScan<uint32_t, kRouteThreads>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ uint32_t carry;
-  const uint32_t tiles = gridDim.x;
+  const uint32_t n = x.W;
+  if (ex_failed(x)) return;  // a failed exchange raises nothing more
   uint32_t running = 0;  // partition base, valid in thread 0
-  for (uint32_t p = 0; p < s.n; ++p) {
+  for (uint32_t p = 0; p < n; ++p) {
     if (threadIdx.x == 0) carry = running;
     __syncthreads();
     for (uint32_t t0 = 0; t0 < tiles; t0 += kRouteThreads) {
       const uint32_t t = t0 + threadIdx.x;
-      const uint32_t c = t < tiles ? __ldcg(tile_counts + size_t(t) * s.n + p) : 0u;
+      const uint32_t c = t < tiles ? tile_counts[size_t(t) * n + p] : 0u;
       uint32_t excl, total;
       Scan(tmp).ExclusiveSum(c, excl, total);
       const uint32_t base = carry;
-      if (t < tiles) tile_offsets[size_t(t) * s.n + p] = base + excl;
+      if (t < tiles) tile_offsets[size_t(t) * n + p] = base + excl;
       __syncthreads();
       if (threadIdx.x == 0) carry = base + total;
       __syncthreads();
@@ -260,6 +255,7 @@ k_ex_count(PartSpec s, ExView x, int kind, const K *__restrict__ keys, size_t co
     __syncthreads();
   }
   ex_raise(x, kind, counts);
+  if (threadIdx.x == 0) ex_wait(x, kind);
 }
 
 // Keys per route tile of the exchange: one per thread of a 256-thread block,
@@ -358,7 +354,6 @@ k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, con
       dst[c] = src[u];
     }
   }
-  ex_finish(x, kGrads ? kExGrads : kExKeys);
 }
 
 // Owner of the keys: after the keys of every sender arrived, finds (and with
@@ -417,6 +412,8 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
       row = dir_find<false>(d, key);
       if (row == kNoRow) kind = kFull;
     }
+    // the row for a gradient batch routed like this forward (deferred keys: below)
+    if (lane == 0 && kind != 3) x.inrow()[i] = (kind == kFound || kind == kInserted) ? row : kNoRow;
     if (kind == kFound) {
       const uint8_t *slab = slabs + size_t(row) * L.stride;
       copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
@@ -436,9 +433,6 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
     }
   }
-  // With kInsert, k_ex_owner_deferred follows on the stream and its last
-  // block raises the ROWS flags (after this launch's stores completed).
-  if constexpr (!kInsert) ex_finish(x, kExRows);
 }
 
 // Deferred keys of k_ex_owner: their claimant has published the row by now.
@@ -460,6 +454,7 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
     if (pos >= x.M) pos = 0;  // reported by k_ex_owner
     void *out_row = x.rows(src) + size_t(pos) * x.row_bytes;
     const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
+    if (lane == 0) x.inrow()[i] = row;
     if (row == kNoRow) {
       if (lane == 0) raise_status(status, kStatusTableFull);
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
@@ -468,7 +463,6 @@ k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const
     const uint8_t *slab = slabs + size_t(row) * L.stride;
     copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
   }
-  ex_finish(x, kExRows);
 }
 
 // Requester: waits for the rows of every owner, then copies this rank's row
@@ -533,17 +527,6 @@ k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t
         if (dst[k]) dst[k][c] = v[k];
     }
   }
-  ex_finish(x, kExGrads);
-}
-
-// Owner, backward: waits for every sender's gradients and sets the number of
-// received rows from `word` (the device count of the accumulate that
-// follows; 0 when the wait gave up).
-__global__ void k_ex_grads_total(ExView x, int word) {
-  pdl_wait();
-  if (threadIdx.x != 0) return;
-  uint32_t *w = x.words();
-  w[kExTotal] = ex_wait(x, kExGrads) ? w[word] : 0u;
 }
 
 }  // namespace se_gpu

@@ -274,7 +274,7 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
              const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
              void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
-             uint32_t *err, CountWs cw, int count_rows) {
+             uint32_t *err, CountWs cw, int count_rows, const uint32_t *__restrict__ known_rows) {
   pdl_wait();
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -302,7 +302,8 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
     if (valid) {
       const uint64_t key = load_key(keys, kdt, i);
       pkeys[i] = key;
-      row = dir_find<false>(d, key);
+      // rows an exchange's owner kernel already resolved for these keys
+      row = known_rows ? known_rows[i] : dir_find<false>(d, key);
       prows[i] = row;
     }
     if (count_rows) count_entries(cw, valid, row, base + uint32_t(i));
@@ -322,10 +323,10 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
     stv<VEC>(pgrads, gdt, e, g);
   }
   if (bad) raise_status(status, kStatusBadGradient);
-  // The last block to finish commits the rows (every block has read `base`).
+  // The last block to finish commits the rows (every block has read `base`;
+  // the rows themselves are read by later kernels only, so no fence).
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     if (atomicAdd(done, 1u) == gridDim.x - 1) {
       *pending = base + uint32_t(n);
       *done = 0u;
@@ -1384,8 +1385,9 @@ struct StoreImpl {
   // n_dev: optional device count (<= n) of the rows to take, for batches
   // whose size is only known on the device (exchanged batches); kdt: key
   // dtype of `keys` when it differs from the store's (exchanged keys are u64).
+  // known_rows: the rows of `keys` when the caller resolved them already.
   void accumulate_locked(const void *keys, size_t n, const uint32_t *n_dev, int64_t dim, const void *grads,
-                         void *sp, int kdt = -1) {
+                         void *sp, int kdt = -1, const uint32_t *known_rows = nullptr) {
     DeviceGuard dg(device);
     if (dim <= 0) throw std::invalid_argument("gradient row length must be positive");
     Table &t = table(dim);
@@ -1422,12 +1424,12 @@ struct StoreImpl {
         pdl(k_accumulate<4>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
                                               size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0);
+                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows);
       else
         pdl(k_accumulate<1>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
                                               uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
                                               size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0);
+                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows);
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1619,7 +1621,6 @@ struct ExchangeImpl {
   std::vector<uint8_t *> peers;    // arena of every rank in this process's address space
   std::vector<bool> opened;        // peers[r] came from cudaIpcOpenMemHandle
   uint8_t **d_peers = nullptr;     // device copy of `peers`
-  uint32_t *d_done = nullptr;      // finished-block counters per kind
   ExView view{};
   bool connected = false;
   // route scratch of the forward and backward direction
@@ -1637,7 +1638,6 @@ struct ExchangeImpl {
     for (uint32_t r = 0; r < peers.size(); ++r)
       if (opened[r]) cudaIpcCloseMemHandle(peers[r]);
     dfree(d_peers);
-    dfree(d_done);
     dfree(arena);
     dfree(route[0]);
     dfree(route[1]);
@@ -1688,6 +1688,7 @@ struct ExchangeImpl {
     view.o_gcounts = take(4ull * W * W);
     view.o_inkeys = take(8 * WM);
     view.o_inpos = take(4 * WM);
+    view.o_inrow = take(4 * WM);
     view.o_gkeys = take(8 * WM);
     view.o_ingrads = take(WM * grad_bytes);
     view.o_rows = take(M * row_bytes);
@@ -1699,9 +1700,6 @@ struct ExchangeImpl {
     key_pid = dalloc<uint32_t>(M);
     key_slot = dalloc<uint32_t>(M);
     d_peers = dalloc<uint8_t *>(W);
-    d_done = dalloc<uint32_t>(kExKinds);
-    cuda_check(cudaMemset(d_done, 0, kExKinds * 4), "memset exchange counters");
-    view.done = d_done;
     cuda_check(cudaMallocHost(&status_host, 16), "cudaMallocHost");
     peers.assign(W, nullptr);
     opened.assign(W, false);
@@ -1751,22 +1749,25 @@ struct ExchangeImpl {
   }
 
   // Route of this rank's keys (per-tile counts, offsets, per-owner counts),
-  // published to every rank as `kind` by the launch's last block.
+  // published to every rank as `kind`; returns after every rank's counts
+  // arrived (stream order).
   template <class K>
   const uint32_t *run_route(const K *keys, size_t n, int dir, int kind, cudaStream_t st) {
     const uint32_t tiles = std::max(uint32_t((n + kExTile - 1) / kExTile), 1u);
     uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
     uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
-    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, kind, keys, n, tile_counts, tile_offsets, counts);
+    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, keys, n, tile_counts);
     launched("k_ex_count");
-    wait(kind, st);
+    pdl(k_ex_sync_counts, 1, kRouteThreads, 0, st, view, kind, tiles, tile_counts, tile_offsets, counts);
+    launched("k_ex_sync_counts");
     return counts;
   }
 
-  // Stream-ordered wait for every rank's flag of `kind`.
-  void wait(int kind, cudaStream_t st) {
-    pdl(k_ex_wait, 1, 32, 0, st, view, kind);
-    launched("k_ex_wait");
+  // Stream-ordered end of a phase: raises this rank's flags of `kind` and
+  // waits for every rank's (total_word: see k_ex_sync).
+  void sync(int kind, cudaStream_t st, int total_word = kExTotal) {
+    pdl(k_ex_sync, 1, 32, 0, st, view, kind, total_word);
+    launched("k_ex_sync");
   }
 
   void check_batch(const void *keys, size_t n, const void *rows, const char *rows_name) const {
@@ -1791,7 +1792,7 @@ struct ExchangeImpl {
           spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot);
       launched("k_ex_scatter");
     });
-    wait(kExKeys, st);
+    sync(kExKeys, st);
     // owner side: at most W * M keys arrive
     const uint64_t WM = uint64_t(W) * M;
     if (insert) {
@@ -1832,7 +1833,7 @@ struct ExchangeImpl {
     };
     if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
     else by_lanes(std::integral_constant<int, 1>{});
-    wait(kExRows, st);
+    sync(kExRows, st);
     last_fwd_n = n;
     have_fwd = true;
     // requester side: this rank's rows, batch order
@@ -1872,8 +1873,7 @@ struct ExchangeImpl {
       else if (al % 4 == 0) scatter(uint32_t{});
       else scatter(uint16_t{});
     });
-    pdl(k_ex_grads_total, 1, 32, 0, st, view, kExTotalStaged);
-    launched("k_ex_grads_total");
+    sync(kExGrads, st, kExTotalStaged);
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_gkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
                              SE_KEY_UINT64);
@@ -1903,11 +1903,10 @@ struct ExchangeImpl {
     if (al % 16 == 0) scatter(uint4{});
     else if (al % 4 == 0) scatter(uint32_t{});
     else scatter(uint16_t{});
-    pdl(k_ex_grads_total, 1, 32, 0, st, view, kExFwdTotal);
-    launched("k_ex_grads_total");
+    sync(kExGrads, st, kExFwdTotal);
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_inkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
-                             SE_KEY_UINT64);
+                             SE_KEY_UINT64, reinterpret_cast<const uint32_t *>(arena + view.o_inrow));
   }
 
   // Waits for the stream; raises a timed-out wait, then the owner's table errors.
