@@ -469,9 +469,8 @@ struct GroupWs {
   uint32_t *seg_fill;  // [P] placement counters (all zero between steps)
   uint32_t *pos;       // [P] entry positions grouped by segment
   uint4 *items;        // work items of k_group_hot: (segment, part, parts, first item)
-  uint32_t *mid;       // [P] segments of LANES+1 .. kApplySlots*LANES rows
   float *partials;     // [items][dim] partial sums of multi-part segments
-  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] mid segments
+  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] unused
   uint32_t cap;        // P: entries the [P] buffers hold (the host's pending count)
   uint32_t *status;    // table status word (kStatusPendingOverflow)
   // cleared by the last block of k_group_hot, the step's last kernel, for
@@ -631,17 +630,17 @@ __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, c
   __syncwarp(mask);
 }
 
-// Phase 4: one group per segment of at most LANES rows (the bulk of the
-// keys). Segments of up to kApplySlots * LANES rows are listed for the
-// group pass of k_group_hot, larger ones become its block work items.
+// Phase 4: one group per segment of at most kApplySlots * LANES rows (the
+// bulk of the keys), summed serially in arrival order; larger segments
+// become the block work items of k_group_hot.
 template <int LANES, int VEC>
-__global__ void __launch_bounds__(256, 4)
+__global__ void __launch_bounds__(256, 3)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
   pdl_wait();
   const uint32_t count = step_count(count_p, w);
   constexpr int GPB = 256 / LANES;
-  __shared__ uint32_t s_ord[GPB][LANES];
+  __shared__ uint32_t s_ord[GPB][kApplySlots * LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -660,13 +659,14 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
       }
       continue;
     }
-    if (cnt > uint32_t(LANES)) {
-      if (lane == 0) w.mid[atomicAdd(&w.ctr[3], 1u)] = uint32_t(s);
-      continue;
+    if (cnt > 0 && !poisoned) {
+      if (cnt <= uint32_t(LANES))
+        group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
+                                        s_ord[gib]);
+      else
+        group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane,
+                                                  mask, s_ord[gib]);
     }
-    if (cnt > 0 && !poisoned)
-      group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
-                                      s_ord[gib]);
     if (lane == 0) {
       w.row_cnt[row] = 0u;
       w.seg_fill[s] = 0u;
@@ -823,20 +823,6 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
     }
     __syncthreads();
   }
-  // Group pass: segments of LANES+1 .. kApplySlots*LANES rows, one group each.
-  const uint32_t nmid = w.ctr[3];
-  const unsigned mask = group_mask<LANES>();
-  uint32_t *ord = reinterpret_cast<uint32_t *>(bitmap) + grp * (kApplySlots * LANES);
-  for (uint32_t m = blockIdx.x * NG + grp; m < nmid; m += gridDim.x * NG) {
-    const uint32_t s = w.mid[m];
-    const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
-    if (!poisoned)
-      group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, s, cnt, off, row, lane, mask, ord);
-    if (lane == 0) {
-      w.row_cnt[row] = 0u;
-      w.seg_fill[s] = 0u;
-    }
-  }
   // The last block clears the window's counters (every block has read them).
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(w.done, 1u) == gridDim.x - 1) {
@@ -980,7 +966,7 @@ struct Table {
   // per-row grouping counters of optimizer_step (capacity entries each)
   uint32_t *row_cnt = nullptr, *row_seg = nullptr;
   // step and insert work buffers
-  Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_mid, def_pos;
+  Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, def_pos;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -1496,7 +1482,6 @@ struct StoreImpl {
     const uint64_t min_parts = (uint64_t(P) + kHotWindowBits - 1) / kHotWindowBits;
     const uint64_t max_items = uint64_t(P) / kPartEntries + 1 + (uint64_t(P) / 5 + 1) * (min_parts + 1);
     w.items = reinterpret_cast<uint4 *>(t.g_items.get(max_items));
-    w.mid = t.g_mid.get(P);
     w.partials = t.g_partials.get(max_items * uint64_t(t.dim));
     w.ctr = t.ctr + kCtrGroup;
     w.cap = P;
