@@ -310,17 +310,23 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
   }
   const size_t chunks = n * dim / VEC;
   bool bad = false;
-  for (size_t c = tid; c < chunks; c += stride) {
-    const size_t e = c * VEC;
-    float g[VEC];
-    ldv<VEC>(grads, gdt, e, g);
+  constexpr int kIlp = 4;  // chunks loaded before any is stored: more bytes in flight per thread
+  for (size_t c0 = tid; c0 < chunks; c0 += stride * kIlp) {
+    float g[kIlp][VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const float s = __fdiv_rn(g[j], scale);
-      bad |= !(fabsf(s) <= maxv);
-      if (scale != 1.0f) g[j] = s;
+    for (int k = 0; k < kIlp; ++k)
+      if (c0 + k * stride < chunks) ldv<VEC>(grads, gdt, (c0 + k * stride) * VEC, g[k]);
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      if (c0 + k * stride >= chunks) continue;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float s = __fdiv_rn(g[k][j], scale);
+        bad |= !(fabsf(s) <= maxv);
+        if (scale != 1.0f) g[k][j] = s;
+      }
+      stv<VEC>(pgrads, gdt, (c0 + k * stride) * VEC, g[k]);
     }
-    stv<VEC>(pgrads, gdt, e, g);
   }
   if (bad) raise_status(status, kStatusBadGradient);
   // The last block to finish commits the rows (every block has read `base`;
