@@ -371,43 +371,59 @@ def run_ours(args):
                  "achieved_gbs_per_gpu": round(step_bytes * K / (elapsed) / 1e9, 1)}
     step_roof["frac_of_peak"] = round(step_roof["achieved_gbs_per_gpu"] / peak, 4)
 
-    # e2e through the public API with host (pinned) buffers.
+    # e2e through the public API from pinned host memory: every step copies
+    # its keys and gradients host -> device and reads its rows back device ->
+    # host, inside the timed region. The copies run on their own streams
+    # (copy engines, both PCIe directions at once), so step s+1's inputs and
+    # step s-1's rows move while step s computes; the device buffers and the
+    # pinned output buffers are double-buffered.
     keys_e, grads_e = wl.make_batches(K + 1, start_step=10_000)
     kh = [torch.from_numpy(keys_e[s]).pin_memory() for s in range(K + 1)]
     gh = [torch.from_numpy(grads_e[s]).pin_memory() for s in range(K + 1)]
-    e2e_value = None
-    if api is store:
-        def host_step(s):
-            vals, _ = store.lookup_or_insert(kh[s], DIM)  # host in, host out
-            store.accumulate_gradients(kh[s], gh[s])
-            store.optimizer_step(1)
-            return vals
-        host_step(0)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for s in range(1, K + 1):
-            host_step(s)
-        torch.cuda.synchronize()
-        e2e_value = BATCH * K / (time.perf_counter() - t0)
-    else:
-        def host_step(s):
-            k = kh[s].cuda(non_blocking=True)
-            g = gh[s].cuda(non_blocking=True)
-            vals = api.lookup_or_insert(k, DIM)
-            api.accumulate_gradients(k, g)
-            api.optimizer_step(1)
-            return vals.cpu()
-        host_step(0)
-        torch.cuda.synchronize()
-        barrier(world)
-        t0 = time.perf_counter()
-        for s in range(1, K + 1):
-            host_step(s)
-        torch.cuda.synchronize()
-        e2e_el = max_over_ranks(time.perf_counter() - t0, world)
-        e2e_value = world * BATCH * K / e2e_el
-    e2e = {"value": e2e_value, "unit": "keys/s", "h2d_bytes_per_step": BATCH * (2 * KEY_BYTES + R) * world,
-           "d2h_bytes_per_step": BATCH * R * world}
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    kd = [torch.empty(BATCH, dtype=torch.int64, device="cuda") for _ in range(2)]
+    gd = [torch.empty((BATCH, DIM), dtype=torch.float32, device="cuda") for _ in range(2)]
+    out_h = [torch.empty((BATCH, DIM), dtype=torch.float32).pin_memory() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(K + 1)]
+    ev_comp = [torch.cuda.Event() for _ in range(K + 1)]
+
+    def e2e_step(s):
+        b = s % 2
+        with torch.cuda.stream(s_in):
+            if s >= 2:
+                s_in.wait_event(ev_comp[s - 2])  # step s-2 is done with buffers b
+            kd[b].copy_(kh[s], non_blocking=True)
+            gd[b].copy_(gh[s], non_blocking=True)
+            ev_in[s].record(s_in)
+        comp.wait_event(ev_in[s])
+        rows = api.lookup_or_insert(kd[b], DIM)
+        if isinstance(rows, tuple):
+            rows = rows[0]
+        api.accumulate_gradients(kd[b], gd[b])
+        api.optimizer_step(1)
+        ev_comp[s].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[s])
+            out_h[b].copy_(rows.view(BATCH, DIM), non_blocking=True)
+            rows.record_stream(s_out)
+
+    e2e_step(0)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for s in range(1, K + 1):
+        e2e_step(s)
+    torch.cuda.synchronize()
+    e2e_el = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_value = world * BATCH * K / e2e_el
+    e2e = {"value": e2e_value, "unit": "keys/s", "h2d_bytes_per_step": BATCH * (KEY_BYTES + R) * world,
+           "d2h_bytes_per_step": BATCH * R * world,
+           "pipeline": "H2D, compute and D2H on separate streams, double-buffered"}
+
+    large = None
+    if world == 1 and not args.no_forward:
+        large = large_batch_bench(store, torch, args.num_keys, peak)
 
     fwd = wide = None
     if world == 1 and not args.no_forward:
@@ -436,6 +452,8 @@ def run_ours(args):
         result["forward_lookup"] = fwd
     if wide:
         result["forward_wide"] = wide
+    if large:
+        result["train_step_large_batch"] = large
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
     if api is not store:
@@ -485,6 +503,47 @@ def forward_bench(se, torch, N):
             "us_per_call": el / FWD_BATCHES * 1e6, "kernel_us": kms / kcnt * 1e3,
             "kernel_achieved_gbs": round(kern_gbs, 1), "kernel_frac": round(kern_gbs / peak, 4),
             "note": "4,096-key batches are launch-latency bound; the tables fit in L2 partly"}
+
+
+def large_batch_bench(store, torch, num_keys, peak):
+    """The same train step on the same table with 8x larger batches
+    (524,288 keys, same key and gradient distributions): how the step's
+    kernels use HBM once the batch is large enough to leave the latency
+    floor. Eager API calls (each step is several hundred microseconds)."""
+    from sparse_embedding_b200.workloads import TrainWorkload
+
+    big = 8 * BATCH
+    wl = TrainWorkload(num_keys=num_keys, batch=big, dim=DIM, rank=0)
+    steps = 12
+    keys_np, grads_np = wl.make_batches(steps + 2, start_step=50_000)
+    keys = torch.from_numpy(keys_np).cuda()
+    grads = torch.from_numpy(grads_np).cuda()
+    del grads_np
+    uniq = [int(np.unique(keys_np[2 + s]).size) for s in range(steps)]
+
+    def step(s):
+        store.lookup_or_insert(keys[s], DIM)
+        store.accumulate_gradients(keys[s], grads[s])
+        store.optimizer_step(1)
+    for s in range(2):
+        step(s)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(2, steps + 2):
+        step(s)
+    b.record()
+    torch.cuda.synchronize()
+    el = a.elapsed_time(b) / 1e3
+    R = DIM * 4
+    n_new = int(round(big * wl.new_fraction))
+    step_bytes = big * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R + big * (KEY_BYTES + R) \
+        + sum(uniq) / len(uniq) * 4 * R
+    gbs = step_bytes * steps / el / 1e9
+    return {"workload": "train step as above with 524,288-key batches (8x), same table", "batch": big,
+            "value": big * steps / el, "unit": "keys/s", "us_per_step": el / steps * 1e6,
+            "algorithmic_bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "timing": "eager API calls, CUDA events"}
 
 
 def forward_wide_bench(se, torch, N, num_keys):
