@@ -535,6 +535,18 @@ def large_batch_bench(store, torch, num_keys, peak):
     b.record()
     torch.cuda.synchronize()
     el = a.elapsed_time(b) / 1e3
+    # per-kernel times from a second, instrumented pass over the same batches
+    store.profile(True)
+    for s in range(2, steps + 2):
+        step(s)
+    torch.cuda.synchronize()
+    per_kernel = {}
+    for nm in ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc", "k_group_place",
+               "k_group_apply", "k_group_hot"]:
+        ms, cnt = store.profile_read(nm)
+        if cnt:
+            per_kernel[nm] = round(ms / cnt * 1e3, 1)
+    store.profile(False)
     R = DIM * 4
     n_new = int(round(big * wl.new_fraction))
     step_bytes = big * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R + big * (KEY_BYTES + R) \
@@ -543,7 +555,8 @@ def large_batch_bench(store, torch, num_keys, peak):
     return {"workload": "train step as above with 524,288-key batches (8x), same table", "batch": big,
             "value": big * steps / el, "unit": "keys/s", "us_per_step": el / steps * 1e6,
             "algorithmic_bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
-            "frac": round(gbs / peak, 4), "timing": "eager API calls, CUDA events"}
+            "frac": round(gbs / peak, 4), "timing": "eager API calls, CUDA events",
+            "kernel_us": per_kernel}
 
 
 def forward_wide_bench(se, torch, N, num_keys):
