@@ -405,3 +405,33 @@ def test_train_workload_small_scale_parity():
     got, _ = gpu.lookup(touched, 64)
     np.testing.assert_allclose(got, orc.lookup(touched, 64), rtol=RTOL_FP32, atol=ATOL_FP32)
     assert gpu.total_size() == orc.size()
+
+
+def test_growth_between_accumulate_and_step():
+    """Rows are counted for the step when gradients are appended; an arena
+    and pending-buffer growth before the step must keep those counts."""
+    gpu, orc = pair([16], key_dtype="int64", opt="adagrad", lr=0.01, eps=1e-8, initial_accumulator_value=0.1,
+                    capacity=64)
+    rng = np.random.default_rng(11)
+    a = rng.integers(-2**62, 2**62, size=200, dtype=np.int64)
+    hot = np.repeat(a[:5], 40)  # a few keys with many rows
+    keys = np.concatenate([a, hot])
+    gpu.lookup_or_insert(keys, 16)
+    orc.lookup_or_insert(keys, 16)
+    g = (rng.standard_normal((len(keys), 16)) * 1e-2).astype(np.float32)
+    gpu.accumulate_gradients(keys, g)
+    orc.accumulate_gradients(keys, g, 16)
+    # grow the arena (and the directory) before the step
+    b = rng.integers(-2**62, 2**62, size=20_000, dtype=np.int64)
+    gpu.lookup_or_insert(b, 16)
+    orc.lookup_or_insert(b, 16)
+    # and the pending buffers
+    g2 = (rng.standard_normal((len(b), 16)) * 1e-2).astype(np.float32)
+    gpu.accumulate_gradients(b, g2)
+    orc.accumulate_gradients(b, g2, 16)
+    gpu.optimizer_step(1)
+    orc.optimizer_step(1)
+    probe = np.concatenate([a, b])
+    got, _ = gpu.lookup(probe, 16)
+    np.testing.assert_allclose(np.asarray(got), orc.lookup(probe, 16).reshape(np.asarray(got).shape),
+                               rtol=RTOL_FP32, atol=ATOL_FP32)
