@@ -476,7 +476,9 @@ struct GroupWs {
   uint32_t *pos;       // [P] entry positions grouped by segment
   uint4 *items;        // work items of k_group_hot: (segment, part, parts, first item)
   float *partials;     // [items][dim] partial sums of multi-part segments
-  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] unused
+  uint32_t *ctr;       // [0] segments, [1] slots allocated, [2] work items, [3] long segments
+  uint32_t *long_list;  // [P] segments of short_max+1 .. long_max rows (listed by k_group_alloc)
+  uint32_t short_max, long_max;  // row bounds of the apply kernel's short and long segments
   uint32_t cap;        // P: entries the [P] buffers hold (the host's pending count)
   uint32_t *status;    // table status word (kStatusPendingOverflow)
   // cleared by the last block of k_group_hot, the step's last kernel, for
@@ -551,6 +553,7 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
   if (sid < nseg) {
     w.seg_off[sid] = s_base + excl;
     w.seg_cnt[sid] = cnt;
+    if (cnt > w.short_max && cnt <= w.long_max) w.long_list[atomicAdd(&w.ctr[3], 1u)] = sid;
   }
 }
 
@@ -638,7 +641,9 @@ __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, c
 
 // Phase 4: one group per segment of at most kApplySlots * LANES rows (the
 // bulk of the keys), summed serially in arrival order; larger segments
-// become the block work items of k_group_hot.
+// become the block work items of k_group_hot. (Tried and slower: the long
+// segments in a concurrent kernel of their own, and half the lanes per
+// segment.)
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 3)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
@@ -654,9 +659,30 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
   const unsigned mask = group_mask<LANES>();
   const uint32_t nseg = w.ctr[0];
   const bool poisoned = *o.poison != 0u;
-  for (size_t s = t / LANES; s < nseg; s += groups) {
+  // The long segments (serial chains of up to long_max rows) get groups of
+  // their own, so no group runs a long chain after its share of short ones.
+  const uint32_t nlong = w.ctr[3];
+  const size_t long_groups = min(size_t(nlong), groups / 4);
+  const size_t g = t / LANES;
+  if (g < long_groups) {
+    for (size_t j = g; j < nlong; j += long_groups) {
+      const uint32_t s = w.long_list[j];
+      const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
+      if (!poisoned)
+        group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, s, cnt, off, row, lane, mask,
+                                                  s_ord[gib]);
+      if (lane == 0) {
+        w.row_cnt[row] = 0u;
+        w.seg_fill[s] = 0u;
+      }
+    }
+    return;
+  }
+  // Every other group: the short segments (and the hot ones' work items).
+  const size_t short_groups = groups - long_groups;
+  for (size_t s = g - long_groups; s < nseg; s += short_groups) {
     const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
-    if (cnt > uint32_t(kApplySlots * LANES)) {
+    if (cnt > w.long_max) {
       if (lane == 0) {
         // Work items of k_group_hot: windows of the batch's positions.
         const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
@@ -665,14 +691,10 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
       }
       continue;
     }
-    if (cnt > 0 && !poisoned) {
-      if (cnt <= uint32_t(LANES))
-        group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
-                                        s_ord[gib]);
-      else
-        group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane,
-                                                  mask, s_ord[gib]);
-    }
+    if (cnt > w.short_max) continue;  // a long segment
+    if (cnt > 0 && !poisoned)
+      group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
+                                      s_ord[gib]);
     if (lane == 0) {
       w.row_cnt[row] = 0u;
       w.seg_fill[s] = 0u;
@@ -972,7 +994,7 @@ struct Table {
   // per-row grouping counters of optimizer_step (capacity entries each)
   uint32_t *row_cnt = nullptr, *row_seg = nullptr;
   // step and insert work buffers
-  Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, def_pos;
+  Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_long, def_pos;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -1483,6 +1505,12 @@ struct StoreImpl {
       t.seg_fill_zeroed = t.g_seg_fill.cap;
     }
     w.pos = t.g_pos.get(P);
+    {
+      const uint32_t lna = t.vec == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
+      w.short_max = lna;                            // one slot per lane
+      w.long_max = uint32_t(kApplySlots) * lna;     // larger: k_group_hot
+      w.long_list = t.g_long.get(P);
+    }
     // Upper bound on k_group_hot work items: segments of more than `lanes`
     // rows, each cut into max(ceil(rows / kPartEntries), ceil(P / window)) parts.
     const uint64_t min_parts = (uint64_t(P) + kHotWindowBits - 1) / kHotWindowBits;
