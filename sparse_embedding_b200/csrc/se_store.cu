@@ -723,7 +723,7 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
   __shared__ uint32_t bitmap[kHotWindowBits / 32];
   __shared__ typename Scan::TempStorage scan_tmp;
   __shared__ uint32_t s_pos[kRoundEntries];
-  __shared__ float part[NG][LANES][VEC];
+  __shared__ float part[kBlockThreads / 32][LANES][VEC];  // one run sum per warp
   __shared__ uint32_t s_last, s_step;
   const uint32_t lane = threadIdx.x % LANES;
   const uint32_t grp = threadIdx.x / LANES;
@@ -793,20 +793,22 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
 #pragma unroll
           for (int j = 0; j < VEC; ++j) a[j] = 0.0f;
           if (e < L.dim) sum_rows<VEC, 4>(pgrads, gdt, L.dim, s_pos, k0, k1, e, a);
+          // Fixed reduction order over the runs: a butterfly across the
+          // groups of a warp (shuffles), then the warps' sums added in warp
+          // order by group 0 - two block barriers instead of one per level.
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) part[grp][lane][j] = a[j];
+          for (int off = LANES; off < 32; off <<= 1)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) a[j] = round_to(gdt, __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], off)));
+          const uint32_t warp = threadIdx.x >> 5;
+          if ((threadIdx.x & 31u) < uint32_t(LANES))
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) part[warp][lane][j] = a[j];
           __syncthreads();
-          // fixed pairwise tree over the runs, then into the window's sum
-          for (int half = NG / 2; half > 0; half >>= 1) {
-            if (int(grp) < half)
-#pragma unroll
-              for (int j = 0; j < VEC; ++j)
-                part[grp][lane][j] = round_to(gdt, __fadd_rn(part[grp][lane][j], part[grp + half][lane][j]));
-            __syncthreads();
-          }
           if (grp == 0)
+            for (uint32_t wi = 0; wi < kBlockThreads / 32; ++wi)
 #pragma unroll
-            for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], part[0][lane][j]));
+              for (int j = 0; j < VEC; ++j) acc[j] = round_to(gdt, __fadd_rn(acc[j], part[wi][lane][j]));
           __syncthreads();
         }
       }
