@@ -363,8 +363,19 @@ def run_ours(args):
         rooflines.append({"kernel": label, "ms_total": ms, "algorithmic_bytes_per_launch": int(nbytes),
                           "achieved_gbs": round(nbytes / per / 1e9, 1)})
     dom = max(rooflines, key=lambda k: k["ms_total"])
+    # DRAM bytes (read + write) per launch from one ncu --set full capture of
+    # the same kernels on the same 65,536-key batch shape with a 2M-key table
+    # (profiles/train_step_2M_dim64_full.md; the 10M-key table is too large
+    # to capture under the capture-size rule). Below the algorithmic bytes:
+    # every hot key's row is read once and served from L2 after that.
+    dram = {"k_group_apply+k_group_hot": 23.887e6 + 6.707e6, "k_lookup_or_insert": 9.457e6,
+            "k_accumulate": 22.181e6 + 0.030e6}
+    local = world == 1 and not args.loopback  # the captured kernels are the local store's
+    traffic = dram.get(dom["kernel"]) if local else None
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": dom["achieved_gbs"], "peak": peak,
-                "unit": "GB/s", "frac": round(dom["achieved_gbs"] / peak, 4), "traffic": None,
+                "unit": "GB/s", "frac": round(dom["achieved_gbs"] / peak, 4), "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, 2M-key table, "
+                                  "same batch shape" if traffic else None,
                 "peak_source": peak_kind, "per_kernel": rooflines}
     step_bytes = units["k_lookup_or_insert"][1] + BATCH * (KEY_BYTES + R) + mean_u * 4 * R
     step_roof = {"algorithmic_bytes_per_step_per_gpu": int(step_bytes),
