@@ -536,8 +536,14 @@ k_count_range(const uint32_t *__restrict__ prows, const uint32_t *base_p, uint32
   }
 }
 
+constexpr int kBlockThreads = 1024;
+constexpr uint32_t kSerialMax = 64;          // rows summed serially (bit-exact order)
+constexpr uint32_t kPartEntries = 512;       // target rows per k_group_hot work item
+constexpr uint32_t kHotWindowBits = 1u << 17;  // positions per bitmap window
+constexpr uint32_t kRoundEntries = 2048;     // rows compacted per round
+
 // Phase 2: a contiguous slot range per segment (block-aggregated allocation).
-__global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
+__global__ void __launch_bounds__(256) k_group_alloc(GroupWs w, const uint32_t *count_p) {
   pdl_wait();
   using Scan = cub::BlockScan<uint32_t, 256>;
   __shared__ typename Scan::TempStorage tmp;
@@ -554,6 +560,13 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w) {
     w.seg_off[sid] = s_base + excl;
     w.seg_cnt[sid] = cnt;
     if (cnt > w.short_max && cnt <= w.long_max) w.long_list[atomicAdd(&w.ctr[3], 1u)] = sid;
+    if (cnt > w.long_max) {
+      // work items of k_group_hot: windows of the batch's positions
+      const uint32_t count = step_count(count_p, w);
+      const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
+      const uint32_t base = atomicAdd(&w.ctr[2], nparts);
+      for (uint32_t q = 0; q < nparts; ++q) w.items[base + q] = make_uint4(sid, q, nparts, base);
+    }
   }
 }
 
@@ -580,11 +593,6 @@ __device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
   return t;
 }
 
-constexpr int kBlockThreads = 1024;
-constexpr uint32_t kSerialMax = 64;          // rows summed serially (bit-exact order)
-constexpr uint32_t kPartEntries = 512;       // target rows per k_group_hot work item
-constexpr uint32_t kHotWindowBits = 1u << 17;  // positions per bitmap window
-constexpr uint32_t kRoundEntries = 2048;     // rows compacted per round
 
 // Sums a segment of at most kApplySlots * LANES rows in the reference's
 // order and applies the optimizer, by one group of LANES lanes: the group
@@ -648,8 +656,6 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 3)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
-  pdl_wait();
-  const uint32_t count = step_count(count_p, w);
   constexpr int GPB = 256 / LANES;
   __shared__ uint32_t s_ord[GPB][kApplySlots * LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -676,22 +682,12 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
         w.seg_fill[s] = 0u;
       }
     }
-    return;
   }
-  // Every other group: the short segments (and the hot ones' work items).
+  // Every other group: the short segments.
   const size_t short_groups = groups - long_groups;
-  for (size_t s = g - long_groups; s < nseg; s += short_groups) {
+  for (size_t s = g - long_groups; g >= long_groups && s < nseg; s += short_groups) {
     const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
-    if (cnt > w.long_max) {
-      if (lane == 0) {
-        // Work items of k_group_hot: windows of the batch's positions.
-        const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
-        const uint32_t base = atomicAdd(&w.ctr[2], nparts);
-        for (uint32_t q = 0; q < nparts; ++q) w.items[base + q] = make_uint4(uint32_t(s), q, nparts, base);
-      }
-      continue;
-    }
-    if (cnt > w.short_max) continue;  // a long segment
+    if (cnt > w.short_max) continue;  // a long segment or one of k_group_hot's
     if (cnt > 0 && !poisoned)
       group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
                                       s_ord[gib]);
@@ -699,6 +695,17 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
       w.row_cnt[row] = 0u;
       w.seg_fill[s] = 0u;
     }
+  }
+  // k_group_hot (launched first, running beside this kernel) has completed
+  // once pdl_wait returns; then the last block clears the window's counters
+  // (every block of both kernels has read them).
+  pdl_wait();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(w.done, 1u) == gridDim.x - 1) {
+    w.ctr[0] = w.ctr[1] = w.ctr[2] = w.ctr[3] = 0u;
+    *w.unres_ctr = 0u;
+    *w.pending = 0u;
+    *w.done = 0u;
   }
 }
 
@@ -716,6 +723,7 @@ __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
             GroupWs w, const uint32_t *count_p) {
   pdl_wait();
+  pdl_trigger();  // k_group_apply runs beside this kernel (disjoint segments)
   const uint32_t count = step_count(count_p, w);
   using Scan = cub::BlockScan<uint32_t, kBlockThreads>;
   constexpr int NG = kBlockThreads / LANES;
@@ -852,14 +860,6 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
       w.seg_fill[s] = 0u;
     }
     __syncthreads();
-  }
-  // The last block clears the window's counters (every block has read them).
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(w.done, 1u) == gridDim.x - 1) {
-    w.ctr[0] = w.ctr[1] = w.ctr[2] = w.ctr[3] = 0u;
-    *w.unres_ctr = 0u;
-    *w.pending = 0u;
-    *w.done = 0u;
   }
 }
 
@@ -1536,7 +1536,7 @@ struct StoreImpl {
     }
     {
       Prof pr(this, "k_group_alloc", st);
-      pdl(k_group_alloc, g, 256, 0, st, w);
+      pdl(k_group_alloc, g, 256, 0, st, w, t.ctr + kCtrPending);
       launched("k_group_alloc");
     }
     {
@@ -1563,16 +1563,16 @@ struct StoreImpl {
     auto go = [&](auto lanes_tag, auto vec_tag) {
       constexpr int LN = decltype(lanes_tag)::value;
       constexpr int VC = decltype(vec_tag)::value;
+      // k_group_hot first (its blocks take whole SMs), k_group_apply beside it
       {
-        Prof pr(this, "k_group_apply", st);
-        pdl(k_group_apply<LN, VC>, grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st,
-            t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
-        launched("k_group_apply");
+        Prof pr(this, "k_group_hot", st);
+        pdl(k_group_hot<LN, VC>, 128, kBlockThreads, 0, st, t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
+        launched("k_group_hot");
       }
-      Prof pr(this, "k_group_hot", st);
-      pdl(k_group_hot<LN, VC>, 148 * 2, kBlockThreads, 0, st, t.L, t.slabs, o, gdt, t.pgrads, w,
-                                                             t.ctr + kCtrPending);
-      launched("k_group_hot");
+      Prof pr(this, "k_group_apply", st);
+      pdl(k_group_apply<LN, VC>, grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st,
+          t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
+      launched("k_group_apply");
     };
     auto by_lanes = [&](auto vec_tag) {
       const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
