@@ -178,6 +178,7 @@ __device__ void ex_raise(const ExView &x, int kind, const uint32_t *counts_local
 // when the wait gave up).
 __global__ void k_ex_sync(ExView x, int kind, int total_word) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   if (ex_failed(x)) {  // a failed exchange raises nothing more
     if (threadIdx.x == 0 && kind == kExGrads) x.words()[kExTotal] = 0u;
     return;
@@ -211,6 +212,7 @@ template <class K>
 __global__ void __launch_bounds__(kRouteThreads)
 k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   extern __shared__ uint32_t hist[];  // [W]
   if (ex_failed(x)) return;
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) hist[p] = 0;
@@ -228,6 +230,7 @@ __global__ void __launch_bounds__(kRouteThreads)
 k_ex_sync_counts(ExView x, int kind, uint32_t tiles, const uint32_t *__restrict__ tile_counts,
                  uint32_t *__restrict__ tile_offsets, uint32_t *__restrict__ counts) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   using Scan = cub::BlockScan<uint32_t, kRouteThreads>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ uint32_t carry;
@@ -277,6 +280,7 @@ k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, con
              const uint32_t *__restrict__ counts_local, const uint8_t *__restrict__ grads,
              uint32_t *__restrict__ key_pid, uint32_t *__restrict__ key_slot) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   extern __shared__ uint32_t sm[];
   uint32_t *warp_base = sm;                   // [kRouteWarps][W]
   uint32_t *remote = sm + kRouteWarps * s.n;  // [W] slot base on each owner minus the local prefix
@@ -366,6 +370,7 @@ __global__ void __launch_bounds__(256)
 k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uint64_t capacity, InitSpec init,
            ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   if (ex_failed(x)) return;
   const uint32_t *prefix = x.prefix();  // written by the KEYS wait
   const uint32_t total = __ldcg(prefix + x.W);
@@ -441,6 +446,7 @@ __global__ void __launch_bounds__(256)
 k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const uint32_t *def_count,
                     const uint32_t *def_idx, const unsigned long long *def_word, uint32_t *status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -471,6 +477,7 @@ template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_rows_out(ExView x, U *__restrict__ out, size_t units) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   if (ex_failed(x)) return;
   const U *src = reinterpret_cast<const U *>(x.rows(x.me));
   const size_t stride = size_t(gridDim.x) * blockDim.x;
@@ -495,6 +502,7 @@ __global__ void __launch_bounds__(256)
 k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot, size_t n,
                   const U *__restrict__ grads, uint32_t units, uint32_t team) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   __shared__ uint8_t *inbox_of[kExMaxRanks];
   if (ex_failed(x)) return;
   for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) inbox_of[p] = x.ingrads(p);

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(256)
 k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row_units,
          const void *__restrict__ keys, int kdt, size_t n, V *__restrict__ out) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -145,6 +146,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_
                    size_t n, void *__restrict__ out, uint32_t *def_count, uint32_t *def_pos,
                    unsigned long long *def_word, uint32_t *status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -201,6 +203,7 @@ k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_coun
            const uint32_t *def_pos, const unsigned long long *def_word, void *__restrict__ out,
            uint32_t *status) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
@@ -276,6 +279,7 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
              void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
              uint32_t *err, CountWs cw, int count_rows, const uint32_t *__restrict__ known_rows) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   // Rows are appended at the committed pending count; the batch size is the
@@ -500,6 +504,7 @@ __global__ void __launch_bounds__(256)
 k_group_fix(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t *count_p, GroupWs w, CountWs c,
             unsigned long long *dropped) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   if (blockIdx.x == 0 && threadIdx.x == 0 && *count_p > w.cap) raise_status(w.status, kStatusPendingOverflow);
   const uint32_t nunres = min(*c.unres_ctr, w.cap);
   const uint32_t count = step_count(count_p, w);
@@ -525,6 +530,7 @@ k_group_fix(Dir d, const unsigned long long *__restrict__ pkeys, const uint32_t 
 __global__ void __launch_bounds__(256)
 k_count_range(const uint32_t *__restrict__ prows, const uint32_t *base_p, uint32_t n, uint32_t pcap, CountWs c) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const uint32_t base = *base_p;
   if (uint64_t(base) + n > pcap) return;  // refused by k_accumulate (reported there)
   const uint32_t stride = gridDim.x * blockDim.x;
@@ -545,6 +551,7 @@ constexpr uint32_t kRoundEntries = 2048;     // rows compacted per round
 // Phase 2: a contiguous slot range per segment (block-aggregated allocation).
 __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w, const uint32_t *count_p) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   using Scan = cub::BlockScan<uint32_t, 256>;
   __shared__ typename Scan::TempStorage tmp;
   __shared__ uint32_t s_base;
@@ -573,6 +580,7 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w, const uint32_t *
 // Phase 3: every entry takes a slot of its segment (warp-aggregated).
 __global__ void __launch_bounds__(256) k_group_place(const uint32_t *count_p, GroupWs w) {
   pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const uint32_t count = step_count(count_p, w);
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
@@ -656,6 +664,7 @@ template <int LANES, int VEC>
 __global__ void __launch_bounds__(256, 3)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   constexpr int GPB = 256 / LANES;
   __shared__ uint32_t s_ord[GPB][kApplySlots * LANES];
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
