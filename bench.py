@@ -432,9 +432,10 @@ def run_ours(args):
            "d2h_bytes_per_step": BATCH * R * world,
            "pipeline": "H2D, compute and D2H on separate streams, double-buffered"}
 
-    large = None
+    large = mut = None
     if world == 1 and not args.no_forward:
         large = large_batch_bench(store, torch, args.num_keys, peak)
+        mut = mutation_bench(store, torch, args.num_keys, peak)
 
     fwd = wide = None
     if world == 1 and not args.no_forward:
@@ -465,6 +466,8 @@ def run_ours(args):
         result["forward_wide"] = wide
     if large:
         result["train_step_large_batch"] = large
+    if mut:
+        result["mutation"] = mut
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
     if api is not store:
@@ -568,6 +571,61 @@ def large_batch_bench(store, torch, num_keys, peak):
             "algorithmic_bytes_per_step": int(step_bytes), "achieved_gbs": round(gbs, 1),
             "frac": round(gbs / peak, 4), "timing": "eager API calls, CUDA events",
             "kernel_us": per_kernel}
+
+
+def mutation_bench(store, torch, num_keys, peak):
+    """Mutation API on the bench's table (dim 64 fp32 Adagrad, num_keys warmed
+    keys): contains, assign and erase of 65,536 distinct present keys per
+    call, then the erased keys inserted again (their rows come back from the
+    free stack). Device-resident keys and values; call times from CUDA events
+    around the calls, kernel times from the store's per-kernel events."""
+    from sparse_embedding_b200.workloads import splitmix64_sequence
+
+    rng = np.random.default_rng(7)
+    calls = 8
+    idx = rng.choice(num_keys, size=(calls + 1) * BATCH, replace=False)
+    keys = torch.from_numpy(splitmix64_sequence(idx).view(np.int64).reshape(calls + 1, BATCH)).cuda()
+    vals = torch.randn((BATCH, DIM), device="cuda") * 0.01
+    R = DIM * 4
+    ops = [  # (name, call, kernel, algorithmic bytes per key)
+        ("contains", lambda i: store.contains(keys[i]), "k_contains", KEY_BYTES + M_BYTES + 1),
+        ("assign", lambda i: store.assign(keys[i], vals), "k_assign", KEY_BYTES + M_BYTES + 2 * R),
+        ("erase", lambda i: store.erase(keys[i]), "k_erase", KEY_BYTES + M_BYTES + 4 + 4),
+        # insert again: probe, claim, param + Adagrad state init, row out
+        ("reinsert", lambda i: store.lookup_or_insert(keys[i], DIM), "k_lookup_or_insert",
+         KEY_BYTES + M_BYTES + 3 * R),
+    ]
+    for _, fn, _, _ in ops:  # warm-up on the extra batch (erase then insert again)
+        fn(calls)
+    torch.cuda.synchronize()
+    out = {}
+    for profiled in (False, True):
+        store.profile(profiled)
+        for name, fn, kname, per_key in ops:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for i in range(calls):
+                fn(i)
+            b.record()
+            torch.cuda.synchronize()
+            if not profiled:
+                out[name] = {"us_per_call": round(a.elapsed_time(b) / calls * 1e3, 1),
+                             "keys_per_s": BATCH * calls / (a.elapsed_time(b) / 1e3)}
+            else:
+                ms, cnt = store.profile_read(kname)
+                if cnt == 0:
+                    continue
+                kus = ms / cnt * 1e3
+                gbs = per_key * BATCH / (kus / 1e6) / 1e9
+                out[name].update({"kernel": kname, "kernel_us": round(kus, 1),
+                                  "algorithmic_bytes_per_key": per_key,
+                                  "kernel_achieved_gbs": round(gbs, 1), "kernel_frac": round(gbs / peak, 4)})
+    store.profile(False)
+    assert store.total_size() >= num_keys
+    return {"workload": "65,536 distinct present keys per call on the train-step table, 8 calls each",
+            "ops": out,
+            "note": "assign checks the batch for repeated keys on the host (copy + hash set), as the "
+                    "reference's validate_unique_mutation_batch does; the call time includes it"}
 
 
 def forward_wide_bench(se, torch, N, num_keys):

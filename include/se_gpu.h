@@ -128,6 +128,29 @@ int se_accumulate_gradients_dim(se_store *store, const void *keys, size_t num_ke
  * key present in the store. */
 int se_optimizer_step(se_store *store, size_t normalization_steps, void *stream);
 
+/* EmbeddingTableFacade::contains (hogwild_embedding_store.hpp:4983-5009):
+ * out_exists[i] = 1 when any table of the store holds keys[i], else 0.
+ * out_exists is host or device memory (num_keys bytes). */
+int se_contains(se_store *store, const void *keys, size_t num_keys, uint8_t *out_exists, void *stream);
+
+/* EmbeddingTableFacade::assign (hogwild_embedding_store.hpp:4838-4923): each
+ * key's parameters are set to its row of values (ParamT, row_lengths[i]
+ * each); a present key keeps its optimizer state, an absent key is inserted
+ * with fresh optimizer state. Keys must be distinct
+ * (validate_unique_mutation_batch, 5278-5305). */
+int se_assign(se_store *store, const void *keys, size_t num_keys, const void *values,
+              size_t num_values, const int64_t *row_lengths, size_t num_row_lengths, void *stream);
+int se_assign_dim(se_store *store, const void *keys, size_t num_keys, int64_t dim, const void *values,
+                  void *stream);
+
+/* EmbeddingTableFacade::erase (hogwild_embedding_store.hpp:5011-5062): removes
+ * the keys from every table; absent keys are ignored. Gradients accumulated
+ * for an erased key are dropped at the next optimizer_step unless the key is
+ * inserted again before it. erase_dimension (5064-5106) removes them from the
+ * table of one dim only. */
+int se_erase(se_store *store, const void *keys, size_t num_keys, void *stream);
+int se_erase_dimension(se_store *store, int64_t dim, const void *keys, size_t num_keys, void *stream);
+
 /* Metadata conventions (embedding_table_interface.hpp:317-396). */
 int se_store_size(se_store *store, uint64_t *out_size);
 int se_store_dim_size(se_store *store, int64_t dim, uint64_t *out_size);

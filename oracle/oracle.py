@@ -78,6 +78,9 @@ def lib():
         L.or_store_dropped.restype = _c.c_uint64
         L.or_store_dropped.argtypes = [_vp]
         L.or_read_row.argtypes = [_vp, _c.c_int64, _c.c_uint64, _vp, _vp, _vp]
+        L.or_contains.argtypes = [_vp, _vp, _c.c_size_t, _vp]
+        L.or_assign.argtypes = [_vp, _vp, _c.c_size_t, _c.c_int64, _vp]
+        L.or_erase.argtypes = [_vp, _vp, _c.c_size_t, _c.c_int64]
         _lib = L
     return _lib
 
@@ -253,6 +256,21 @@ class OracleStore:
 
     def optimizer_step(self, normalization_steps=1):
         _check(lib().or_optimizer_step(self._h, normalization_steps))
+
+    def contains(self, keys):
+        keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
+        out = np.zeros(len(keys), dtype=np.uint8)
+        lib().or_contains(self._h, _ptr(keys), len(keys), _ptr(out))
+        return out
+
+    def assign(self, keys, values, dim):
+        keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
+        values = np.ascontiguousarray(values)
+        _check(lib().or_assign(self._h, _ptr(keys), len(keys), dim, _ptr(values)))
+
+    def erase(self, keys, dim=0):
+        keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
+        _check(lib().or_erase(self._h, _ptr(keys), len(keys), dim))
 
     def size(self, dim=0) -> int:
         return int(lib().or_store_size(self._h, dim))

@@ -263,16 +263,17 @@ void adagrad_row(P *param, const P *grad, O *acc, float lr, float eps, float wd,
 }
 
 // ---------------------------------------------------------------------------
-// Key -> slot map (sentinel-free linear probing). Stands in for the
-// FlatKeyDirectory + SegmentedLocatorTable pair; only its find/insert
-// semantics matter to the results.
+// Key -> slot map (sentinel-free linear probing, erase by tombstone). Stands
+// in for the FlatKeyDirectory + SegmentedLocatorTable pair; only its
+// find/insert/erase semantics matter to the results.
 // ---------------------------------------------------------------------------
 
 struct KeyMap {
   std::vector<uint64_t> keys;
   std::vector<uint32_t> vals;
-  std::vector<uint8_t> used;
-  size_t count = 0;
+  std::vector<uint8_t> used;  // 0 empty, 1 live, 2 erased
+  size_t count = 0;           // occupied slots (live + erased)
+  size_t live = 0;
   size_t mask = 0;
 
   KeyMap() { rehash(64); }
@@ -289,8 +290,9 @@ struct KeyMap {
     used.assign(cap, 0);
     mask = cap - 1;
     count = 0;
+    live = 0;
     for (size_t i = 0; i < ou.size(); ++i)
-      if (ou[i]) insert_new(ok[i], ov[i]);
+      if (ou[i] == 1) insert_new(ok[i], ov[i]);
   }
   void insert_new(uint64_t k, uint32_t v) {
     size_t pos = splitmix64(k) & mask;
@@ -299,11 +301,24 @@ struct KeyMap {
     keys[pos] = k;
     vals[pos] = v;
     ++count;
+    ++live;
   }
   bool find(uint64_t k, uint32_t *v) const {
     size_t pos = splitmix64(k) & mask;
     while (used[pos]) {
-      if (keys[pos] == k) { *v = vals[pos]; return true; }
+      if (used[pos] == 1 && keys[pos] == k) { *v = vals[pos]; return true; }
+      pos = (pos + 1) & mask;
+    }
+    return false;
+  }
+  bool erase(uint64_t k) {
+    size_t pos = splitmix64(k) & mask;
+    while (used[pos]) {
+      if (used[pos] == 1 && keys[pos] == k) {
+        used[pos] = 2;
+        --live;
+        return true;
+      }
       pos = (pos + 1) & mask;
     }
     return false;
@@ -314,12 +329,13 @@ struct KeyMap {
     if (cap != keys.size()) rehash(cap);
   }
   void insert(uint64_t k, uint32_t v) {
-    if (2 * (count + 1) > keys.size()) rehash(keys.size() * 2);
+    if (2 * (count + 1) > keys.size()) rehash(4 * (live + 1) > keys.size() ? keys.size() * 2 : keys.size());
     insert_new(k, v);
   }
   void clear() {
     std::fill(used.begin(), used.end(), 0);
     count = 0;
+    live = 0;
   }
 };
 
@@ -349,6 +365,9 @@ struct TableBase {
   virtual int accumulate(const void *keys, size_t n, const void *grads) = 0;
   virtual void optimizer_step(size_t normalization_steps, uint64_t *dropped, int threads) = 0;
   virtual int read_row(uint64_t key, void *param, void *state, uint32_t *step) const = 0;
+  virtual void contains(const void *keys, size_t n, uint8_t *out) const = 0;
+  virtual void assign(const void *keys, size_t n, const void *values) = 0;
+  virtual void erase(const void *keys, size_t n) = 0;
 };
 
 template <class F> void parallel_for(size_t n, int threads, F &&f) {
@@ -366,6 +385,7 @@ template <class P, class O, class G> struct Table final : TableBase {
   int64_t dim_;
   size_t simd_cut;
   KeyMap map;
+  uint32_t nrows = 0;  // rows ever created (an erased key's row is not reused)
   std::vector<P> params;
   std::vector<O> s0, s1;    // Adam m, v  |  Adagrad acc (s0)
   std::vector<uint32_t> steps;
@@ -385,7 +405,7 @@ template <class P, class O, class G> struct Table final : TableBase {
     simd_cut = (size_t(d) / w) * w;
   }
   int64_t dim() const override { return dim_; }
-  size_t size() const override { return map.count; }
+  size_t size() const override { return map.live; }
   void reserve(size_t n) override { map.reserve(n); }
 
   size_t nstate() const {
@@ -396,7 +416,7 @@ template <class P, class O, class G> struct Table final : TableBase {
   }
 
   uint32_t insert_row(uint64_t key) {
-    const uint32_t row = uint32_t(map.count);
+    const uint32_t row = nrows++;
     map.insert(key, row);
     const size_t d = size_t(dim_);
     params.resize(params.size() + d);
@@ -568,6 +588,35 @@ template <class P, class O, class G> struct Table final : TableBase {
     }
   }
 
+  // contains: hogwild_embedding_store.hpp:4983-5009 (a key is present when
+  // any table holds it: the caller ORs the tables).
+  void contains(const void *keys, size_t n, uint8_t *out) const override {
+    for (size_t i = 0; i < n; ++i) {
+      uint32_t row;
+      if (map.find(key_at(cfg.key_dtype, keys, i), &row)) out[i] = 1;
+    }
+  }
+
+  // assign: hogwild_embedding_store.hpp:4838-4923. A present key's
+  // parameters are overwritten (optimizer state kept); an absent key is
+  // inserted (fresh optimizer state) with the given parameters.
+  void assign(const void *keys, size_t n, const void *values) override {
+    const P *v = static_cast<const P *>(values);
+    const size_t d = size_t(dim_);
+    for (size_t i = 0; i < n; ++i) {
+      const uint64_t key = key_at(cfg.key_dtype, keys, i);
+      uint32_t row;
+      if (!map.find(key, &row)) row = insert_row(key);
+      std::memcpy(params.data() + size_t(row) * d, v + i * d, d * sizeof(P));
+    }
+  }
+
+  // erase: hogwild_embedding_store.hpp:5011-5062 (absent keys are ignored).
+  // Pending gradients stay keyed; optimizer_step resolves them then.
+  void erase(const void *keys, size_t n) override {
+    for (size_t i = 0; i < n; ++i) map.erase(key_at(cfg.key_dtype, keys, i));
+  }
+
   int read_row(uint64_t key, void *param, void *state, uint32_t *step) const override {
     uint32_t row;
     if (!map.find(key, &row)) return 0;
@@ -737,6 +786,27 @@ uint64_t or_store_size(void *h, int64_t dim) {
 }
 
 uint64_t or_store_dropped(void *h) { return static_cast<Store *>(h)->dropped; }
+
+void or_contains(void *h, const void *keys, size_t n, uint8_t *out) {
+  Store *s = static_cast<Store *>(h);
+  std::memset(out, 0, n);
+  for (auto *t : s->tables) t->contains(keys, n, out);
+}
+
+int or_assign(void *h, const void *keys, size_t n, int64_t dim, const void *values) {
+  auto *t = static_cast<Store *>(h)->table(dim);
+  if (!t) return -2;
+  t->assign(keys, n, values);
+  return 0;
+}
+
+// dim 0: every table (erase); else the table of dim (erase_dimension).
+int or_erase(void *h, const void *keys, size_t n, int64_t dim) {
+  Store *s = static_cast<Store *>(h);
+  if (dim != 0 && !s->table(dim)) { g_last_error = "erase dimension is not configured"; return -1; }
+  for (auto *t : s->tables) if (dim == 0 || t->dim() == dim) t->erase(keys, n);
+  return 0;
+}
 
 int or_read_row(void *h, int64_t dim, uint64_t key, void *param, void *state, uint32_t *step) {
   auto *t = static_cast<Store *>(h)->table(dim);

@@ -79,6 +79,11 @@ _SIGNATURES = {
     "se_accumulate_gradients": [_vp, _vp, _sz, _vp, _sz, C.POINTER(_i64), _sz, _vp],
     "se_accumulate_gradients_dim": [_vp, _vp, _sz, _i64, _vp, _vp],
     "se_optimizer_step": [_vp, _sz, _vp],
+    "se_contains": [_vp, _vp, _sz, _vp, _vp],
+    "se_assign": [_vp, _vp, _sz, _vp, _sz, C.POINTER(_i64), _sz, _vp],
+    "se_assign_dim": [_vp, _vp, _sz, _i64, _vp, _vp],
+    "se_erase": [_vp, _vp, _sz, _vp],
+    "se_erase_dimension": [_vp, _i64, _vp, _sz, _vp],
     "se_store_size": [_vp, C.POINTER(_u64)],
     "se_store_dim_size": [_vp, _i64, C.POINTER(_u64)],
     "se_store_reserve": [_vp, _sz, _i64],

@@ -367,7 +367,7 @@ k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, con
 // a zero row.
 template <int LANES, int VEC, bool kInsert>
 __global__ void __launch_bounds__(256)
-k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uint64_t capacity, InitSpec init,
+k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init,
            ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
@@ -398,16 +398,15 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row, uin
         const InsertResult r = dir_find_or_insert(d, key);
         kind = r.kind;
         word = r.row_word;
+        // found: published, claimed and not yet published (3), or erased and revived here
+        if (kind == kFound) kind = resolve_found(word, &row);
         if (kind == kInserted) {
-          row = atomicAdd(next_row, 1u);
-          if (row >= capacity) {
+          row = take_row(ra);
+          if (row >= ra.capacity) {
             raise_status(status, kStatusTableFull);
             kind = kFull;
           }
-        } else if (kind == kFound) {
-          row = __ldcg(word);
-          if (row == kNoRow) kind = 3;  // claimed, not yet published
-        } else {
+        } else if (kind == kFull) {
           raise_status(status, kStatusTableFull);
         }
       }

@@ -16,6 +16,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <unordered_set>
 #include <vector>
 
 #include "se_common.cuh"
@@ -141,8 +142,7 @@ __device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const 
 // the claim before the row was published and are finished by k_deferred.
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256)
-k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_row,
-                   uint64_t capacity, InitSpec init, const void *__restrict__ keys, int kdt,
+k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init, const void *__restrict__ keys, int kdt,
                    size_t n, void *__restrict__ out, uint32_t *def_count, uint32_t *def_pos,
                    unsigned long long *def_word, uint32_t *status) {
   pdl_wait();
@@ -160,16 +160,15 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, uint32_t *next_
     const InsertResult r = dir_find_or_insert(d, key);
     kind = r.kind;
     word = r.row_word;
+    // found: published, claimed in this launch (3), or erased and revived here
+    if (kind == kFound) kind = resolve_found(word, &row);
     if (kind == kInserted) {
-      row = atomicAdd(next_row, 1u);
-      if (row >= capacity) {
+      row = take_row(ra);
+      if (row >= ra.capacity) {
         raise_status(status, kStatusTableFull);
         kind = kFull;
       }
-    } else if (kind == kFound) {
-      row = __ldcg(word);
-      if (row == kNoRow) kind = 3;  // claimed in this launch, row not yet published
-    } else {
+    } else if (kind == kFull) {
       raise_status(status, kStatusTableFull);
     }
   }
@@ -879,8 +878,148 @@ __global__ void k_rehash(const Bucket *__restrict__ old_b, uint64_t old_n, Dir n
   const Bucket &b = old_b[slot / kBucketSlots];
   const int s = int(slot % kBucketSlots);
   const uint64_t key = b.keys[s];
-  if (key == kEmptyKey) return;
+  if (key == kEmptyKey || b.rows[s] == kDeadRow) return;  // erased keys are dropped here
   if (!dir_insert_unique(nd, key, b.rows[s])) raise_status(status, kStatusTableFull);
+}
+
+// ---------------------------------------------------------------------------
+// Mutation API: contains, assign, erase (hogwild_embedding_store.hpp:4838-5106)
+// ---------------------------------------------------------------------------
+
+// contains (hogwild_embedding_store.hpp:4983-5009): a key is present when any
+// table holds it; one launch per table, the first one overwrites `out`.
+__global__ void __launch_bounds__(256)
+k_contains(Dir d, const void *__restrict__ keys, int kdt, size_t n, uint8_t *__restrict__ out, int first) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const bool found = dir_find<false>(d, load_key(keys, kdt, i)) != kNoRow;
+  out[i] = uint8_t(found || (!first && out[i] != 0));
+}
+
+// Optimizer state of a row that is created with given parameters.
+template <int LANES, int VEC>
+__device__ __forceinline__ void init_state(const Layout &L, uint8_t *slab, const InitSpec &init, uint32_t lane) {
+  for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+    if (L.nstate >= 1) {
+      float s[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s[j] = init.state0;
+      stv<VEC>(slab + L.state0, L.odt, e, s);
+    }
+    if (L.nstate >= 2) {
+      float s[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) s[j] = 0.0f;
+      stv<VEC>(slab + L.state1, L.odt, e, s);
+    }
+  }
+  if (L.nstate >= 2 && lane == 0) *reinterpret_cast<uint32_t *>(slab + L.step) = 0u;
+}
+
+// assign (hogwild_embedding_store.hpp:4838-4923): a present key's parameters
+// are overwritten and its optimizer state kept; an absent (or erased) key is
+// inserted with the given parameters and fresh optimizer state. The host has
+// checked that the keys are distinct.
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_assign(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init, const void *__restrict__ keys,
+         int kdt, size_t n, const void *__restrict__ values, uint32_t *status) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t i = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (i >= n) return;
+  const unsigned mask = group_mask<LANES>();
+  int kind = kFound;
+  uint32_t row = kNoRow;
+  uint32_t *word = nullptr;
+  if (lane == 0) {
+    const InsertResult r = dir_find_or_insert(d, load_key(keys, kdt, i));
+    kind = r.kind;
+    word = r.row_word;
+    // unpublished (3) only after an insert that found the arena full
+    if (kind == kFound) kind = resolve_found(word, &row);
+    if (kind == kInserted) row = take_row(ra);
+    if (kind != kFound && kind != kInserted) kind = kFull;
+    if (kind == kFull || row >= ra.capacity) {
+      raise_status(status, kStatusTableFull);
+      kind = kFull;
+    }
+  }
+  kind = __shfl_sync(mask, kind, 0, LANES);
+  row = __shfl_sync(mask, row, 0, LANES);
+  if (kind == kFull) return;
+  uint8_t *slab = slabs + size_t(row) * L.stride;
+  const void *src = static_cast<const uint8_t *>(values) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
+  copy_row<VEC>(slab, src, L.pdt, L.dim, lane * VEC, LANES * VEC);
+  if (kind == kInserted) {
+    init_state<LANES, VEC>(L, slab, init, lane);
+    __threadfence();  // the slab is written device-wide ...
+    __syncwarp(mask);
+    if (lane == 0) atomicExch(word, row);  // ... before its row is published
+  }
+}
+
+// Rows popped past the bottom of the free stack leave it below zero.
+__global__ void k_free_clamp(int *free_top) {
+  if (*free_top < 0) *free_top = 0;
+}
+
+// erase / erase_dimension (hogwild_embedding_store.hpp:5011-5106): the key's
+// slot becomes a tombstone (the all-ones key's side slot returns to "never
+// inserted") and its row goes on the free stack, to be taken by a later
+// insert. Absent keys and repeats are no-ops.
+__global__ void __launch_bounds__(256)
+k_erase(Dir d, const void *__restrict__ keys, int kdt, size_t n, int *free_top, uint32_t *free_rows,
+        uint64_t capacity) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t key = load_key(keys, kdt, i);
+  uint32_t *word = dir_slot(d, key);
+  if (word == nullptr) return;
+  const bool side = key == kEmptyKey;
+  const uint32_t old = atomicExch(word, side ? kNoRow : kDeadRow);
+  if (side) atomicExch(d.special, 0u);
+  if (old < kDeadRow && old < capacity) {
+    const int j = atomicAdd(free_top, 1);
+    if (uint64_t(j) < capacity) free_rows[j] = old;
+  }
+}
+
+// After an erase, pending gradients are counted again from their keys'
+// current rows: optimizer_step resolves keys when it runs
+// (hogwild_embedding_store.hpp:2745-2750), so gradients of an erased key are
+// dropped at the step, or applied to its new row if the key is inserted again
+// before it. First the old counts are cleared ...
+__global__ void __launch_bounds__(256)
+k_requeue_clear(const uint32_t *__restrict__ prows, const uint32_t *count_p, uint32_t cap, uint64_t rows_cap,
+                CountWs c) {
+  const uint32_t count = min(*count_p, cap);
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tid == 0) {
+    *c.seg_ctr = 0u;
+    *c.unres_ctr = 0u;
+  }
+  for (uint32_t i = tid; i < count; i += gridDim.x * blockDim.x) {
+    const uint32_t r = prows[i];
+    if (r < rows_cap) c.row_cnt[r] = 0u;
+  }
+}
+
+// ... then every entry is probed and counted again (keys absent now are
+// listed for the step's probe, k_group_fix).
+__global__ void __launch_bounds__(256)
+k_requeue_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t *__restrict__ prows,
+                const uint32_t *count_p, uint32_t cap, CountWs c) {
+  const uint32_t count = min(*count_p, cap);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  for (uint32_t i0 = tid - (tid & 31u); i0 < count; i0 += stride) {
+    const uint32_t i = i0 + (tid & 31u);
+    const bool valid = i < count;
+    const uint32_t row = valid ? dir_find<true>(d, pkeys[i]) : kNoRow;
+    if (valid) prows[i] = row;
+    count_entries(c, valid, row, i);
+  }
 }
 
 // Reads the rows of a few keys (state inspection for tests).
@@ -977,6 +1116,7 @@ enum Ctr : int {
   kCtrPendingBackup = 15,
   kCtrUnres = 16,      // pending entries whose key was absent when appended (cleared after each step)
   kCtrStepDone = 17,   // blocks of the running k_group_hot that have finished
+  kCtrFreeTop = 18,    // int: rows of erased keys on the free stack (may read below zero; see take_row)
   kCtrWords = 20,
 };
 
@@ -1004,6 +1144,10 @@ struct Table {
   uint64_t pcap = 0, pcount = 0;
   // per-row grouping counters of optimizer_step (capacity entries each)
   uint32_t *row_cnt = nullptr, *row_seg = nullptr;
+  // rows of erased keys, reused by inserts (capacity entries)
+  uint32_t *free_rows = nullptr;
+  uint64_t tombs = 0;  // upper bound of erased keys' tombstones in the directory
+  bool erased = false;  // inserts look at the free stack only once a key was erased
   // step and insert work buffers
   Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_long, def_pos;
   Scratch<uint4> g_items;
@@ -1012,6 +1156,10 @@ struct Table {
   uint64_t seg_fill_zeroed = 0;  // entries of g_seg_fill known to be zero
 
   Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
+  RowAlloc alloc() const {
+    return RowAlloc{ctr + kCtrNextRow, erased ? reinterpret_cast<int *>(ctr + kCtrFreeTop) : nullptr, free_rows,
+                    capacity};
+  }
   ~Table() {
     dfree(buckets);
     dfree(slabs);
@@ -1021,6 +1169,7 @@ struct Table {
     dfree(pgrads);
     dfree(row_cnt);
     dfree(row_seg);
+    dfree(free_rows);
     dfree(seg_row);
     dfree(unres);
   }
@@ -1148,17 +1297,20 @@ struct StoreImpl {
   // Rows counted since the last step keep their counts and segments when
   // the arena grows (the first `keep` rows are copied).
   void alloc_row_arrays(Table &t, uint64_t cap, uint64_t keep = 0, cudaStream_t st = nullptr) {
-    uint32_t *nc = dalloc<uint32_t>(cap), *ns = dalloc<uint32_t>(cap);
+    uint32_t *nc = dalloc<uint32_t>(cap), *ns = dalloc<uint32_t>(cap), *nf = dalloc<uint32_t>(cap);
     cuda_check(cudaMemsetAsync(nc, 0, cap * 4, st), "memset row counters");
     if (keep) {
       cuda_check(cudaMemcpyAsync(nc, t.row_cnt, keep * 4, cudaMemcpyDeviceToDevice, st), "grow row counters");
       cuda_check(cudaMemcpyAsync(ns, t.row_seg, keep * 4, cudaMemcpyDeviceToDevice, st), "grow row counters");
+      cuda_check(cudaMemcpyAsync(nf, t.free_rows, keep * 4, cudaMemcpyDeviceToDevice, st), "grow free rows");
     }
     cuda_check(cudaStreamSynchronize(st), "sync");
     dfree(t.row_cnt);
     dfree(t.row_seg);
+    dfree(t.free_rows);
     t.row_cnt = nc;
     t.row_seg = ns;
+    t.free_rows = nf;
   }
 
   uint64_t read_rows_used(Table &t, cudaStream_t st) {
@@ -1167,6 +1319,16 @@ struct StoreImpl {
     const uint64_t used = status_host[0];
     check_status(t, st);
     return used;
+  }
+
+  // Keys present: rows taken from the arena minus the rows of erased keys
+  // waiting on the free stack.
+  uint64_t read_live_keys(Table &t, cudaStream_t st) {
+    const uint64_t used = read_rows_used(t, st);
+    cuda_check(cudaMemcpyAsync(status_host, t.ctr + kCtrFreeTop, 4, cudaMemcpyDeviceToHost, st), "read rows");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    const int32_t free_top = int32_t(status_host[0]);
+    return used - uint64_t(free_top > 0 ? free_top : 0);
   }
 
   static bool capturing(cudaStream_t st) {
@@ -1188,7 +1350,7 @@ struct StoreImpl {
     if (capturing(st)) {
       t.bound_stale = true;
       const uint64_t need = t.rows_bound + extra;
-      if (need > t.capacity || need > uint64_t(double(t.nbuckets) * kMaxLoadPerBucket))
+      if (need > t.capacity || need + t.tombs > uint64_t(double(t.nbuckets) * kMaxLoadPerBucket))
         throw Error(SE_ERR_TABLE_FULL, "insert captured in a CUDA graph needs " + std::to_string(extra) +
                                            " reserved rows; reserve capacity before capturing");
       return;
@@ -1199,7 +1361,9 @@ struct StoreImpl {
     }
     uint64_t need = t.rows_bound + extra;
     const auto dir_limit = [&](uint64_t nb) { return uint64_t(double(nb) * kMaxLoadPerBucket); };
-    if (need > t.capacity || need > dir_limit(t.nbuckets)) {
+    // Directory slots in use: at most the rows ever taken plus the erased
+    // keys' tombstones (a rehash drops those).
+    if (need > t.capacity || need + t.tombs > dir_limit(t.nbuckets)) {
       t.rows_bound = read_rows_used(t, st);
       need = t.rows_bound + extra;
       if (need > 0xfffffff0ull) throw Error(SE_ERR_TABLE_FULL, "table exceeds 2^32 rows");
@@ -1215,7 +1379,7 @@ struct StoreImpl {
         t.capacity = ncap;
         alloc_row_arrays(t, ncap, old_cap, st);
       }
-      if (need > dir_limit(t.nbuckets)) {
+      if (need + t.tombs > dir_limit(t.nbuckets)) {
         uint64_t nb = t.nbuckets;
         while (dir_limit(nb) < std::max(need, t.capacity)) nb *= 2;
         Bucket *nbk = dalloc<Bucket>(nb);
@@ -1229,6 +1393,7 @@ struct StoreImpl {
         dfree(t.buckets);
         t.buckets = nbk;
         t.nbuckets = nb;
+        t.tombs = 0;
       }
     }
     t.rows_bound = need;
@@ -1350,7 +1515,7 @@ struct StoreImpl {
         {
           Prof pr(this, "k_lookup_or_insert", st);
           pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
-              t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity, init, dkeys, cfg.key_dtype, n,
+              t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n,
               dout, t.ctr + kCtrDeferred, dpos, dword, t.ctr + kCtrStatus);
           launched("k_lookup_or_insert");
         }
@@ -1400,6 +1565,140 @@ struct StoreImpl {
           "gradient scale storage exceeds configured dtype (a device gradient batch failed validation; "
           "its accumulation window was discarded)");
     }
+  }
+
+  // ---- mutation API ----------------------------------------------------------
+  // Keys widened to u64 on the host (for checks that need them there).
+  std::vector<uint64_t> host_keys(const void *keys, size_t n, cudaStream_t st) {
+    const size_t kb = key_bytes(cfg.key_dtype);
+    std::vector<uint8_t> raw(n * kb);
+    if (is_device_ptr(keys)) {
+      cuda_check(cudaMemcpyAsync(raw.data(), keys, n * kb, cudaMemcpyDeviceToHost, st), "copy keys");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+    } else {
+      std::memcpy(raw.data(), keys, n * kb);
+    }
+    std::vector<uint64_t> k(n);
+    for (size_t i = 0; i < n; ++i) {
+      switch (cfg.key_dtype) {
+      case SE_KEY_INT32: { int32_t v; std::memcpy(&v, raw.data() + 4 * i, 4); k[i] = uint64_t(int64_t(v)); break; }
+      case SE_KEY_UINT32: { uint32_t v; std::memcpy(&v, raw.data() + 4 * i, 4); k[i] = v; break; }
+      default: std::memcpy(&k[i], raw.data() + 8 * i, 8); break;
+      }
+    }
+    return k;
+  }
+
+  // contains (hogwild_embedding_store.hpp:4983-5009).
+  void contains(const void *keys, size_t n, uint8_t *out, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (n == 0) return;
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const bool host_out = !is_device_ptr(out);
+    uint8_t *dout = host_out ? stage_vals.get(n) : out;
+    if (tables.empty()) cuda_check(cudaMemsetAsync(dout, 0, n, st), "memset");
+    int first = 1;
+    for (auto &t : tables) {
+      Prof pr(this, "k_contains", st);
+      k_contains<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t->dir(), dkeys, cfg.key_dtype, n, dout, first);
+      launched("k_contains");
+      first = 0;
+    }
+    if (host_out) {
+      cuda_check(cudaMemcpyAsync(out, dout, n, cudaMemcpyDeviceToHost, st), "copy out");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+    }
+  }
+
+  // assign (hogwild_embedding_store.hpp:4838-4923) with the batch check of
+  // validate_unique_mutation_batch (5278-5305).
+  void assign(const void *keys, size_t n, int64_t dim, const void *values, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("dim must be > 0");
+    Table &t = table(dim);
+    if (n == 0) return;
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    {
+      const std::vector<uint64_t> k = host_keys(keys, n, st);
+      std::unordered_set<uint64_t> seen;
+      seen.reserve(n * 2);
+      for (uint64_t x : k)
+        if (!seen.insert(x).second) throw std::invalid_argument("mutation batch contains duplicate dimension and key");
+    }
+    ensure_rows(t, n, st);
+    const size_t vb = value_bytes(cfg.value_dtype);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const void *dvals = stage_in(stage_vals, values, n * size_t(dim) * vb, st);
+    InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
+                  cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
+    const bool vec4 = t.vec == 4 && (uintptr_t(dvals) % 16 == 0);
+    auto go = [&](auto lanes_tag, auto vec_tag) {
+      constexpr int LN = decltype(lanes_tag)::value;
+      constexpr int VC = decltype(vec_tag)::value;
+      Prof pr(this, "k_assign", st);
+      k_assign<LN, VC><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+          t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n, dvals, t.ctr + kCtrStatus);
+      launched("k_assign");
+    };
+    auto by_lanes = [&](auto vec_tag) {
+      const uint32_t ln = gather_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim));
+      switch (ln) {
+      case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+      case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+      case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+      default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+      }
+    };
+    if (vec4) by_lanes(std::integral_constant<int, 4>{});
+    else by_lanes(std::integral_constant<int, 1>{});
+    if (!is_device_ptr(keys) || !is_device_ptr(values)) check_status(t, st);
+  }
+
+  // erase (hogwild_embedding_store.hpp:5011-5062): every table; or
+  // erase_dimension (5064-5106): the table of `dim`.
+  void erase(const void *keys, size_t n, int64_t dim, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    Table *only = nullptr;
+    if (dim != 0) {
+      for (auto &t : tables)
+        if (t->dim == dim) only = t.get();
+      if (only == nullptr) throw std::invalid_argument("erase dimension is not configured");
+    }
+    if (n == 0) return;
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    for (auto &tp : tables) {
+      Table &t = *tp;
+      if (only != nullptr && only != &t) continue;
+      int *free_top = reinterpret_cast<int *>(t.ctr + kCtrFreeTop);
+      k_free_clamp<<<1, 1, 0, st>>>(free_top);
+      launched("k_free_clamp");
+      {
+        Prof pr(this, "k_erase", st);
+        k_erase<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, free_top,
+                                                               t.free_rows, t.capacity);
+        launched("k_erase");
+      }
+      t.tombs += n;
+      t.erased = true;
+      if (t.pcount > 0) {
+        const unsigned grid = grid_for(t.pcount, 256, 148 * 8);
+        k_requeue_clear<<<grid, 256, 0, st>>>(t.prows, t.ctr + kCtrPending, uint32_t(t.pcap), t.capacity,
+                                              t.count_ws());
+        launched("k_requeue_clear");
+        k_requeue_count<<<grid, 256, 0, st>>>(t.dir(), t.pkeys, t.prows, t.ctr + kCtrPending, uint32_t(t.pcap),
+                                              t.count_ws());
+        launched("k_requeue_count");
+      }
+    }
+    if (!is_device_ptr(keys)) cuda_check(cudaStreamSynchronize(st), "sync");
   }
 
   void accumulate(const void *keys, size_t n, int64_t dim, const void *grads, void *sp) {
@@ -1838,7 +2137,7 @@ struct ExchangeImpl {
       const unsigned grid = grid_for(M * LN, 256, 148 * 16);
       StoreImpl::Prof pr(store, "k_ex_owner", st);
       if (insert) {
-        pdl(k_ex_owner<LN, VC, true>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+        pdl(k_ex_owner<LN, VC, true>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.alloc(),
                                                         init, view, t.ctr + kCtrDeferred, def_idx, def_word,
                                                         t.ctr + kCtrStatus);
         launched("k_ex_owner");
@@ -1846,7 +2145,7 @@ struct ExchangeImpl {
                                                              def_word, t.ctr + kCtrStatus);
         launched("k_ex_owner_deferred");
       } else {
-        pdl(k_ex_owner<LN, VC, false>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.ctr + kCtrNextRow, t.capacity,
+        pdl(k_ex_owner<LN, VC, false>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.alloc(),
                                                          init, view, nullptr, nullptr, nullptr,
                                                          t.ctr + kCtrStatus);
         launched("k_ex_owner");
@@ -2082,6 +2381,36 @@ int se_lookup_or_insert(se_store *store, const void *keys, size_t n, void *out, 
   });
 }
 
+int se_contains(se_store *store, const void *keys, size_t n, uint8_t *out, void *stream) {
+  return guarded([&] { checked(store)->impl.contains(keys, n, out, stream); });
+}
+
+int se_assign_dim(se_store *store, const void *keys, size_t n, int64_t dim, const void *values, void *stream) {
+  return guarded([&] { checked(store)->impl.assign(keys, n, dim, values, stream); });
+}
+
+int se_assign(se_store *store, const void *keys, size_t n, const void *values, size_t num_values,
+              const int64_t *row_lengths, size_t num_row_lengths, void *stream) {
+  return guarded([&] {
+    const int64_t d = uniform_dim(row_lengths, n, num_row_lengths, false);
+    if (n == 0) return;
+    if (num_values != n * size_t(d)) throw std::invalid_argument("values size does not match row lengths");
+    checked(store)->impl.assign(keys, n, d, values, stream);
+  });
+}
+
+int se_erase(se_store *store, const void *keys, size_t n, void *stream) {
+  return guarded([&] { checked(store)->impl.erase(keys, n, 0, stream); });
+}
+
+int se_erase_dimension(se_store *store, int64_t dim, const void *keys, size_t n, void *stream) {
+  return guarded([&] {
+    if (dim <= 0) throw std::invalid_argument(dim < 0 ? "erase dimension must be non-negative"
+                                                      : "erase dimension is not configured");
+    checked(store)->impl.erase(keys, n, dim, stream);
+  });
+}
+
 int se_accumulate_gradients_dim(se_store *store, const void *keys, size_t n, int64_t dim,
                                 const void *grads, void *stream) {
   return guarded([&] { checked(store)->impl.accumulate(keys, n, dim, grads, stream); });
@@ -2110,7 +2439,7 @@ int se_store_size(se_store *store, uint64_t *out) {
     DeviceGuard dg(s.device);
     cuda_check(cudaDeviceSynchronize(), "sync");
     uint64_t total = 0;
-    for (auto &t : s.tables) total += s.read_rows_used(*t, s.own);
+    for (auto &t : s.tables) total += s.read_live_keys(*t, s.own);
     *out = total;
   });
 }
@@ -2121,7 +2450,7 @@ int se_store_dim_size(se_store *store, int64_t dim, uint64_t *out) {
     std::lock_guard<std::mutex> lock(s.mu);
     DeviceGuard dg(s.device);
     cuda_check(cudaDeviceSynchronize(), "sync");
-    *out = s.read_rows_used(s.table(dim), s.own);
+    *out = s.read_live_keys(s.table(dim), s.own);
   });
 }
 

@@ -24,6 +24,10 @@ namespace se_gpu {
 
 constexpr uint64_t kEmptyKey = ~0ull;
 constexpr uint32_t kNoRow = 0xffffffffu;
+// Row word of an erased key (a tombstone): the key keeps its slot, so probe
+// sequences stay intact, and reads as absent; an insert of the same key
+// revives the slot, a rehash drops it.
+constexpr uint32_t kDeadRow = 0xfffffffeu;
 constexpr int kBucketSlots = 5;
 
 struct alignas(64) Bucket {
@@ -75,10 +79,10 @@ __device__ __forceinline__ void load_bucket(const Bucket *b, uint64_t (&k)[kBuck
   r[0] = a2.z; r[1] = a2.w; r[2] = a3.x; r[3] = a3.y; r[4] = a3.z;
 }
 
-// Row of `key`, or kNoRow when absent. Probing stops at the first bucket that
-// holds the key or an empty slot; slots never return to empty, so the key
-// cannot sit past an empty slot of its probe sequence. Bounded by the bucket
-// count.
+// Row of `key`, or kNoRow when absent (or erased). Probing stops at the first
+// bucket that holds the key or an empty slot; slots never return to empty
+// (erasing leaves a tombstone), so the key cannot sit past an empty slot of
+// its probe sequence. Bounded by the bucket count.
 template <bool kCoherent>
 __device__ __forceinline__ uint32_t dir_find(const Dir &d, uint64_t key) {
   if (key == kEmptyKey) return kCoherent ? __ldcg(d.special + 1) : __ldg(d.special + 1);
@@ -91,7 +95,7 @@ __device__ __forceinline__ uint32_t dir_find(const Dir &d, uint64_t key) {
     bool empty = false;
 #pragma unroll
     for (int s = 0; s < kBucketSlots; ++s) {
-      if (k[s] == key) return r[s];
+      if (k[s] == key) return r[s] == kDeadRow ? kNoRow : r[s];
       empty |= k[s] == kEmptyKey;
     }
     if (empty) return kNoRow;
@@ -108,7 +112,8 @@ struct InsertResult {
 };
 
 // Find-or-claim by one thread. A claim CASes the key into the first empty
-// slot of its probe sequence; the claimant then owns the row word.
+// slot of its probe sequence; the claimant then owns the row word. A key
+// found with a tombstone row word is revived by the caller (revive_row).
 __device__ __forceinline__ InsertResult dir_find_or_insert(const Dir &d, uint64_t key) {
   if (key == kEmptyKey) {
     const uint32_t old = atomicCAS(d.special, 0u, 1u);
@@ -133,6 +138,56 @@ __device__ __forceinline__ InsertResult dir_find_or_insert(const Dir &d, uint64_
     b = (b + 1) & mask;
   }
   return {nullptr, kFull};
+}
+
+// A found key's row word: kInserted when it was a tombstone that this thread
+// claimed back (its row is then taken like a new key's), 3 when the row is
+// not published yet (claimed in this launch), else kFound with *row set.
+__device__ __forceinline__ int resolve_found(uint32_t *word, uint32_t *row) {
+  *row = __ldcg(word);
+  if (*row == kDeadRow) return atomicCAS(word, kDeadRow, kNoRow) == kDeadRow ? kInserted : 3;
+  return *row == kNoRow ? 3 : kFound;
+}
+
+// Row word of `key` (live, unpublished or a tombstone), or nullptr when the
+// key never had a slot. Used by erase.
+__device__ __forceinline__ uint32_t *dir_slot(const Dir &d, uint64_t key) {
+  if (key == kEmptyKey) return d.special + 1;
+  const uint64_t mask = d.nbuckets - 1;
+  uint64_t b = home_bucket(splitmix64(key), d.nbuckets);
+  for (uint64_t probe = 0; probe < d.nbuckets; ++probe) {
+    uint64_t k[kBucketSlots];
+    uint32_t r[kBucketSlots];
+    load_bucket<true>(d.buckets + b, k, r);
+    bool empty = false;
+#pragma unroll
+    for (int s = 0; s < kBucketSlots; ++s) {
+      if (k[s] == key) return &d.buckets[b].rows[s];
+      empty |= k[s] == kEmptyKey;
+    }
+    if (empty) return nullptr;
+    b = (b + 1) & mask;
+  }
+  return nullptr;
+}
+
+// Where a claimant takes its row: the rows of erased keys first (a stack,
+// `free_top` entries; pops of one launch may drive it below zero, which the
+// next push clamps), else the bump counter. free_top is null for a table
+// that never had a key erased.
+struct RowAlloc {
+  uint32_t *next_row;
+  int *free_top;
+  const uint32_t *free_rows;
+  uint64_t capacity;
+};
+
+__device__ __forceinline__ uint32_t take_row(const RowAlloc &a) {
+  if (a.free_top != nullptr && __ldcg(a.free_top) > 0) {
+    const int i = atomicSub(a.free_top, 1) - 1;
+    if (i >= 0) return __ldcg(a.free_rows + i);
+  }
+  return atomicAdd(a.next_row, 1u);
 }
 
 // Plain insert used when rebuilding a larger directory (keys are distinct).

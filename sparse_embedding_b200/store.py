@@ -378,6 +378,59 @@ class EmbeddingStore:
         stream = self._stream(g) or self._stream(k)
         N.check(self._lib.se_accumulate_gradients_dim(self._h, k.ptr, n, dim, g.ptr, stream))
 
+    # ---- mutation API -----------------------------------------------------------
+
+    def assign(self, keys, values) -> None:
+        """Sets the parameters of each key (inserting absent keys with fresh
+        optimizer state); keys must be distinct. SyncOpsImpl::assign shape rules
+        (bindings/typed/module_typed_sync.inl:92-126)."""
+        self._check_operational()
+        k = self._keys(keys)
+        v = as_input(values, "values")
+        self._check_device(v)
+        n = k.size
+        if len(v.shape) == 2:
+            if v.shape[0] != n:
+                raise ValueError("values shape[0] must match keys length")
+            dim = int(v.shape[1])
+        elif len(v.shape) == 1:
+            dim = 0
+            if n > 0:
+                if v.shape[0] % n != 0:
+                    raise ValueError("1D values length must be a multiple of keys length")
+                dim = int(v.shape[0]) // n
+        else:
+            raise ValueError("values must be a 1D or 2D tensor")
+        if v.dtype != self._value_dtype:
+            raise ValueError("dtype mismatch in dlpack_to_span")
+        if (k.cuda_device is None) != (v.cuda_device is None):
+            raise ValueError("keys and values must be in the same memory space")
+        if n == 0:
+            return
+        stream = self._stream(v) or self._stream(k)
+        N.check(self._lib.se_assign_dim(self._h, k.ptr, n, dim, v.ptr, stream))
+
+    def contains(self, keys):
+        """uint8 per key: 1 when any table holds it (module_wrapper_methods.inl:143-160)."""
+        k = self._keys(keys)
+        n = k.size
+        out = empty_like_space(k, (n,), "uint8")
+        if n:
+            N.check(self._lib.se_contains(self._h, k.ptr, n, data_ptr(out), self._stream(k)))
+        return out
+
+    def erase(self, keys) -> None:
+        """Removes the keys from every table; absent keys are ignored."""
+        k = self._keys(keys)
+        N.check(self._lib.se_erase(self._h, k.ptr, k.size, self._stream(k)))
+
+    def erase_dimension(self, keys, dimension: int) -> None:
+        """Removes the keys from the table of one dim (module_wrapper_methods.inl:195-210)."""
+        if int(dimension) < 0:
+            raise ValueError("erase dimension must be non-negative")
+        k = self._keys(keys)
+        N.check(self._lib.se_erase_dimension(self._h, int(dimension), k.ptr, k.size, self._stream(k)))
+
     def optimizer_step(self, normalization_steps: int, stream: int | None = None) -> None:
         # EmbeddingStoreWrapper::optimizer_step (module_wrapper_methods.inl:174-180)
         if not self._optimizer_enabled:
@@ -515,15 +568,6 @@ class EmbeddingStore:
 
     def _not_here(self, what: str):
         raise NotImplementedError(f"{what} is not provided by the GPU store")
-
-    def assign(self, keys, values):
-        self._not_here("assign")
-
-    def contains(self, keys):
-        self._not_here("contains")
-
-    def erase(self, keys):
-        self._not_here("erase")
 
     def export_page_images(self):
         self._not_here("export_page_images (host checkpointing)")
