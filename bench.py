@@ -624,8 +624,9 @@ def mutation_bench(store, torch, num_keys, peak):
     assert store.total_size() >= num_keys
     return {"workload": "65,536 distinct present keys per call on the train-step table, 8 calls each",
             "ops": out,
-            "note": "assign checks the batch for repeated keys on the host (copy + hash set), as the "
-                    "reference's validate_unique_mutation_batch does; the call time includes it"}
+            "note": "assign checks the batch for repeated keys on the device (k_assign_dups, a scratch hash "
+                    "set) and reads the verdict back before it returns, since the reference raises before it "
+                    "mutates anything (validate_unique_mutation_batch); the call time includes that wait"}
 
 
 def forward_wide_bench(se, torch, N, num_keys):

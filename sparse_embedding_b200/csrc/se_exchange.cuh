@@ -400,14 +400,16 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec i
         word = r.row_word;
         // found: published, claimed and not yet published (3), or erased and revived here
         if (kind == kFound) kind = resolve_found(word, &row);
-        if (kind == kInserted) {
-          row = take_row(ra);
-          if (row >= ra.capacity) {
-            raise_status(status, kStatusTableFull);
-            kind = kFull;
-          }
-        } else if (kind == kFull) {
+        else if (kind == kFull) raise_status(status, kStatusTableFull);
+      }
+      // lanes of this warp still in the loop: keys i - t / LANES + [0, total)
+      const size_t live = (size_t(total) - (i - t / LANES)) * LANES;
+      const uint32_t taken = take_rows_warp(ra, live_lanes(t, live), lane == 0 && kind == kInserted);
+      if (lane == 0 && kind == kInserted) {
+        row = taken;
+        if (row >= ra.capacity) {
           raise_status(status, kStatusTableFull);
+          kind = kFull;
         }
       }
       kind = __shfl_sync(mask, kind, 0, LANES);

@@ -16,7 +16,6 @@
 #include <memory>
 #include <mutex>
 #include <string>
-#include <unordered_set>
 #include <vector>
 
 #include "se_common.cuh"
@@ -162,14 +161,14 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, In
     word = r.row_word;
     // found: published, claimed in this launch (3), or erased and revived here
     if (kind == kFound) kind = resolve_found(word, &row);
-    if (kind == kInserted) {
-      row = take_row(ra);
-      if (row >= ra.capacity) {
-        raise_status(status, kStatusTableFull);
-        kind = kFull;
-      }
-    } else if (kind == kFull) {
+    else if (kind == kFull) raise_status(status, kStatusTableFull);
+  }
+  const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
+  if (lane == 0 && kind == kInserted) {
+    row = taken;
+    if (row >= ra.capacity) {
       raise_status(status, kStatusTableFull);
+      kind = kFull;
     }
   }
   kind = __shfl_sync(mask, kind, 0, LANES);
@@ -916,18 +915,46 @@ __device__ __forceinline__ void init_state(const Layout &L, uint8_t *slab, const
   if (L.nstate >= 2 && lane == 0) *reinterpret_cast<uint32_t *>(slab + L.step) = 0u;
 }
 
+// validate_unique_mutation_batch (hogwild_embedding_store.hpp:5278-5305) on
+// the device: the batch's keys go into a scratch open-addressing set of at
+// least twice as many slots (all-ones = empty); a key that finds itself
+// there already marks the batch. words[0] counts the all-ones key itself,
+// words[1] is the mark.
+__global__ void __launch_bounds__(256)
+k_assign_dups(const void *__restrict__ keys, int kdt, size_t n, unsigned long long *__restrict__ set,
+              uint64_t nslots, uint32_t *words) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t key = load_key(keys, kdt, i);
+  if (key == kEmptyKey) {
+    if (atomicAdd(words, 1u) > 0u) words[1] = 1u;
+    return;
+  }
+  const uint64_t mask = nslots - 1;
+  uint64_t pos = splitmix64(key) & mask;
+  for (uint64_t probe = 0; probe < nslots; ++probe) {
+    const unsigned long long old = atomicCAS(&set[pos], kEmptyKey, key);
+    if (old == kEmptyKey) return;
+    if (old == key) {
+      words[1] = 1u;
+      return;
+    }
+    pos = (pos + 1) & mask;
+  }
+}
+
 // assign (hogwild_embedding_store.hpp:4838-4923): a present key's parameters
 // are overwritten and its optimizer state kept; an absent (or erased) key is
-// inserted with the given parameters and fresh optimizer state. The host has
-// checked that the keys are distinct.
+// inserted with the given parameters and fresh optimizer state. A batch that
+// k_assign_dups marked (a key repeated) changes nothing.
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256)
 k_assign(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init, const void *__restrict__ keys,
-         int kdt, size_t n, const void *__restrict__ values, uint32_t *status) {
+         int kdt, size_t n, const void *__restrict__ values, const uint32_t *dup_mark, uint32_t *status) {
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
-  if (i >= n) return;
+  if (i >= n || *dup_mark != 0u) return;
   const unsigned mask = group_mask<LANES>();
   int kind = kFound;
   uint32_t row = kNoRow;
@@ -938,8 +965,11 @@ k_assign(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec ini
     word = r.row_word;
     // unpublished (3) only after an insert that found the arena full
     if (kind == kFound) kind = resolve_found(word, &row);
-    if (kind == kInserted) row = take_row(ra);
     if (kind != kFound && kind != kInserted) kind = kFull;
+  }
+  const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
+  if (lane == 0) {
+    if (kind == kInserted) row = taken;
     if (kind == kFull || row >= ra.capacity) {
       raise_status(status, kStatusTableFull);
       kind = kFull;
@@ -1198,6 +1228,8 @@ struct StoreImpl {
   uint32_t *status_host = nullptr;  // pinned
   uint64_t *u64_host = nullptr;     // pinned
   Scratch<uint8_t> stage_keys, stage_vals;
+  Scratch<unsigned long long> dup_set;  // assign's repeated-key check
+  Scratch<uint32_t> dup_words;
   bool profiling = false;
   std::vector<ProfRec> prof;
   std::vector<cudaEvent_t> event_pool;
@@ -1568,27 +1600,6 @@ struct StoreImpl {
   }
 
   // ---- mutation API ----------------------------------------------------------
-  // Keys widened to u64 on the host (for checks that need them there).
-  std::vector<uint64_t> host_keys(const void *keys, size_t n, cudaStream_t st) {
-    const size_t kb = key_bytes(cfg.key_dtype);
-    std::vector<uint8_t> raw(n * kb);
-    if (is_device_ptr(keys)) {
-      cuda_check(cudaMemcpyAsync(raw.data(), keys, n * kb, cudaMemcpyDeviceToHost, st), "copy keys");
-      cuda_check(cudaStreamSynchronize(st), "sync");
-    } else {
-      std::memcpy(raw.data(), keys, n * kb);
-    }
-    std::vector<uint64_t> k(n);
-    for (size_t i = 0; i < n; ++i) {
-      switch (cfg.key_dtype) {
-      case SE_KEY_INT32: { int32_t v; std::memcpy(&v, raw.data() + 4 * i, 4); k[i] = uint64_t(int64_t(v)); break; }
-      case SE_KEY_UINT32: { uint32_t v; std::memcpy(&v, raw.data() + 4 * i, 4); k[i] = v; break; }
-      default: std::memcpy(&k[i], raw.data() + 8 * i, 8); break;
-      }
-    }
-    return k;
-  }
-
   // contains (hogwild_embedding_store.hpp:4983-5009).
   void contains(const void *keys, size_t n, uint8_t *out, void *sp) {
     std::lock_guard<std::mutex> lock(mu);
@@ -1623,17 +1634,18 @@ struct StoreImpl {
     if (n == 0) return;
     if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
     cudaStream_t st = pick(sp);
-    {
-      const std::vector<uint64_t> k = host_keys(keys, n, st);
-      std::unordered_set<uint64_t> seen;
-      seen.reserve(n * 2);
-      for (uint64_t x : k)
-        if (!seen.insert(x).second) throw std::invalid_argument("mutation batch contains duplicate dimension and key");
-    }
     ensure_rows(t, n, st);
     const size_t vb = value_bytes(cfg.value_dtype);
     const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
     const void *dvals = stage_in(stage_vals, values, n * size_t(dim) * vb, st);
+    // repeated keys: checked on the device before anything is written
+    const uint64_t nslots = next_pow2(2 * uint64_t(n));
+    unsigned long long *set = dup_set.get(nslots);
+    uint32_t *words = dup_words.get(2);
+    cuda_check(cudaMemsetAsync(set, 0xff, nslots * 8, st), "memset");
+    cuda_check(cudaMemsetAsync(words, 0, 8, st), "memset");
+    k_assign_dups<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(dkeys, cfg.key_dtype, n, set, nslots, words);
+    launched("k_assign_dups");
     InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
                   cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
     const bool vec4 = t.vec == 4 && (uintptr_t(dvals) % 16 == 0);
@@ -1642,7 +1654,7 @@ struct StoreImpl {
       constexpr int VC = decltype(vec_tag)::value;
       Prof pr(this, "k_assign", st);
       k_assign<LN, VC><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
-          t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n, dvals, t.ctr + kCtrStatus);
+          t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n, dvals, words + 1, t.ctr + kCtrStatus);
       launched("k_assign");
     };
     auto by_lanes = [&](auto vec_tag) {
@@ -1656,6 +1668,10 @@ struct StoreImpl {
     };
     if (vec4) by_lanes(std::integral_constant<int, 4>{});
     else by_lanes(std::integral_constant<int, 1>{});
+    // the reference raises before it mutates anything: read the mark now
+    cuda_check(cudaMemcpyAsync(status_host, words + 1, 4, cudaMemcpyDeviceToHost, st), "read mark");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    if (status_host[0] != 0u) throw std::invalid_argument("mutation batch contains duplicate dimension and key");
     if (!is_device_ptr(keys) || !is_device_ptr(values)) check_status(t, st);
   }
 

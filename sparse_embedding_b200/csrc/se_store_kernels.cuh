@@ -171,10 +171,10 @@ __device__ __forceinline__ uint32_t *dir_slot(const Dir &d, uint64_t key) {
   return nullptr;
 }
 
-// Where a claimant takes its row: the rows of erased keys first (a stack,
-// `free_top` entries; pops of one launch may drive it below zero, which the
-// next push clamps), else the bump counter. free_top is null for a table
-// that never had a key erased.
+// Where claimants take their rows: the rows of erased keys first (a stack,
+// `free_top` entries; pops may drive it below zero, which the next push
+// clamps), else the bump counter. free_top is null for a table that never
+// had a key erased.
 struct RowAlloc {
   uint32_t *next_row;
   int *free_top;
@@ -182,12 +182,40 @@ struct RowAlloc {
   uint64_t capacity;
 };
 
-__device__ __forceinline__ uint32_t take_row(const RowAlloc &a) {
-  if (a.free_top != nullptr && __ldcg(a.free_top) > 0) {
-    const int i = atomicSub(a.free_top, 1) - 1;
-    if (i >= 0) return __ldcg(a.free_rows + i);
+// Lanes of the calling warp whose global thread index t is below `active`
+// (threads past the end of a launch's work have returned).
+__device__ __forceinline__ unsigned live_lanes(size_t t, size_t active) {
+  const size_t base = t & ~size_t(31);
+  if (active >= base + 32) return 0xffffffffu;
+  return active > base ? (1u << unsigned(active - base)) - 1u : 0u;
+}
+
+// Rows for the claimants of one warp (`claim` set) with one atomic per
+// warp and source: every lane of `lanes` calls it; claimants get their row,
+// others kNoRow. A row at or past the arena's capacity means it is full.
+__device__ __forceinline__ uint32_t take_rows_warp(const RowAlloc &a, unsigned lanes, bool claim) {
+  const unsigned claims = __ballot_sync(lanes, claim);
+  if (claims == 0u) return kNoRow;
+  const uint32_t lane = threadIdx.x & 31u;
+  const int leader = __ffs(claims) - 1;
+  const int cnt = __popc(claims);
+  int top = 0;
+  uint32_t bump = 0;
+  if (int(lane) == leader) {
+    if (a.free_top != nullptr && __ldcg(a.free_top) > 0) {
+      top = atomicSub(a.free_top, cnt);
+      if (uint64_t(max(top, 0)) > a.capacity) top = int(a.capacity);  // never more free rows than the arena holds
+    }
+    const int from_free = min(max(top, 0), cnt);
+    if (from_free < cnt) bump = atomicAdd(a.next_row, uint32_t(cnt - from_free));
   }
-  return atomicAdd(a.next_row, 1u);
+  top = __shfl_sync(lanes, top, leader);
+  bump = __shfl_sync(lanes, bump, leader);
+  if (!claim) return kNoRow;
+  const int from_free = min(max(top, 0), cnt);
+  const int rank = __popc(claims & ((1u << lane) - 1u));
+  if (rank < from_free) return __ldcg(a.free_rows + (top - 1 - rank));  // entries [top - from_free, top)
+  return bump + uint32_t(rank - from_free);
 }
 
 // Plain insert used when rebuilding a larger directory (keys are distinct).

@@ -196,6 +196,32 @@ def test_erase_with_pending_gradients():
         assert f1 and f2 and t1 == t2
 
 
+def test_bulk_inserts_into_recycled_rows():
+    """Whole batches of new keys after large erases: rows come off the free
+    stack a warp at a time, partly from it and partly from the arena's end."""
+    rng = np.random.default_rng(6)
+    dim = 32
+    gpu, orc = pair([dim], key_dtype="uint64", opt="adam", lr=1e-2, capacity=1 << 16)
+    base = rng.integers(0, 2**64 - 1, size=40_000, dtype=np.uint64)
+    gpu.lookup_or_insert(base, dim)
+    orc.lookup_or_insert(base, dim)
+    for r in range(3):
+        gone = np.ascontiguousarray(base[r * 10_000:(r + 1) * 10_000 - 37 * r])
+        gpu.erase(gone)
+        orc.erase(gone)
+        fresh = rng.integers(0, 2**64 - 1, size=10_000 + 5_000 * r, dtype=np.uint64)
+        got, _ = gpu.lookup_or_insert(torch.from_numpy(fresh.view(np.int64)).cuda().view(torch.uint64), dim)
+        np.testing.assert_array_equal(bits(got), bits(orc.lookup_or_insert(fresh, dim)))
+        vals = rng.uniform(-1, 1, (4_000, dim)).astype(np.float32)
+        akeys = np.unique(rng.integers(0, 2**64 - 1, size=4_000, dtype=np.uint64))
+        gpu.assign(akeys, vals[: len(akeys)])
+        orc.assign(akeys, vals[: len(akeys)], dim)
+        assert gpu.total_size() == orc.size()
+        base = np.concatenate([base, fresh, akeys])
+    got, _ = gpu.lookup(base, dim)
+    np.testing.assert_array_equal(bits(got), bits(orc.lookup(base, dim)))
+
+
 def test_erase_dimension_touches_one_table():
     gpu, orc = pair([8, 32], opt="sgd")
     keys = np.arange(1000, dtype=np.int64)
@@ -231,6 +257,8 @@ def test_assign_argument_errors():
     with pytest.raises(ValueError, match="duplicate dimension and key"):
         gpu.assign(torch.tensor([7, 7], dtype=torch.int64, device="cuda"),
                    torch.zeros((2, 128), device="cuda"))
+    with pytest.raises(ValueError, match="duplicate dimension and key"):
+        gpu.assign(np.array([-1, 3, -1], dtype=np.int64), np.zeros((3, 128), dtype=np.float32))
     with pytest.raises(RuntimeError, match="invalid dim access"):
         gpu.assign(keys, np.zeros((3, 64), dtype=np.float32))
     assert gpu.total_size() == 0
