@@ -432,10 +432,11 @@ def run_ours(args):
            "d2h_bytes_per_step": BATCH * R * world,
            "pipeline": "H2D, compute and D2H on separate streams, double-buffered"}
 
-    large = mut = None
+    large = mut = uniq = None
     if world == 1 and not args.no_forward:
         large = large_batch_bench(store, torch, args.num_keys, peak)
         mut = mutation_bench(store, torch, args.num_keys, peak)
+        uniq = unique_bench(se, torch, args.num_keys)
 
     fwd = wide = None
     if world == 1 and not args.no_forward:
@@ -468,6 +469,8 @@ def run_ours(args):
         result["train_step_large_batch"] = large
     if mut:
         result["mutation"] = mut
+    if uniq:
+        result["unique"] = uniq
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
     if api is not store:
@@ -627,6 +630,34 @@ def mutation_bench(store, torch, num_keys, peak):
             "note": "assign checks the batch for repeated keys on the device (k_assign_dups, a scratch hash "
                     "set) and reads the verdict back before it returns, since the reference raises before it "
                     "mutates anything (validate_unique_mutation_batch); the call time includes that wait"}
+
+
+def unique_bench(se, torch, num_keys):
+    """se.unique (distinct keys, inverse, first positions, counts) of
+    device-resident batches shaped like the train step's: 65,536 and
+    524,288 int64 keys, Zipf(1.05) + 5% new. Per call, CUDA events around the
+    call (which waits for the distinct count)."""
+    from sparse_embedding_b200.workloads import TrainWorkload
+
+    out = {}
+    for batch in (BATCH, 8 * BATCH):
+        wl = TrainWorkload(num_keys=num_keys, batch=batch, dim=DIM, rank=0)
+        keys_np, _ = wl.make_batches(6, start_step=90_000)
+        keys = torch.from_numpy(keys_np).cuda()
+        for i in range(2):
+            se.unique(keys[i], return_first_indices=True, return_counts=True)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(2, 6):
+            u = se.unique(keys[i], return_first_indices=True, return_counts=True)[0]
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) / 4 * 1e3
+        out[str(batch)] = {"us_per_call": round(us, 1), "keys_per_s": batch / (us / 1e6),
+                           "unique_keys": int(u.numel())}
+    return {"workload": "unique with inverse, first positions and counts of train-step batches (int64, "
+                        "Zipf 1.05 + 5% new), device-resident", "batches": out}
 
 
 def forward_wide_bench(se, torch, N, num_keys):

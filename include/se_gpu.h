@@ -180,6 +180,21 @@ int se_filter(int32_t kind, uint32_t num_partitions, int32_t key_dtype, const vo
               size_t num_keys, uint32_t target_partition, uint8_t *out_mask, int32_t device,
               void *stream);
 
+/* se::ops::unique_keys_inverse (sparse_embedding/src/ops/unique_ops.hpp:73-418;
+ * Python async_unique, sparse_embedding/src/bindings/module.cpp:959-1072):
+ * the distinct keys of keys[0, num_keys) in order of first appearance (the
+ * reference leaves the order unspecified; its sequential path uses this
+ * one), with int32 inverse indices (unique_keys_out[inverse[i]] == keys[i]),
+ * the position of each key's first appearance and its number of
+ * appearances. unique_keys_out (key_dtype), first_indices_out and counts_out
+ * need room for num_keys entries, inverse_out for num_keys; any of the last
+ * three may be null (not computed). *num_unique_out receives the count.
+ * Host or device pointers; the call waits for its results. num_keys must be
+ * below 2^31 (validate_unique_input_size, unique_ops.hpp:42-47). */
+int se_unique(int32_t key_dtype, const void *keys, size_t num_keys, void *unique_keys_out,
+              int32_t *inverse_out, int32_t *first_indices_out, int32_t *counts_out,
+              uint64_t *num_unique_out, int32_t device, void *stream);
+
 /*
  * Exchange routing (no reference counterpart: the reference leaves routing to
  * the caller, sparse_embedding/partitioner.py:84-100). Device pointers only.

@@ -288,6 +288,23 @@ class OracleStore:
         return bool(found), p, s[: nstate * dim], int(step[0])
 
 
+def unique_first_occurrence(keys):
+    """se::ops::unique_keys_inverse_sequential (sparse_embedding/src/ops/unique_ops.hpp:73-125):
+    the distinct keys in order of first appearance (the insertion order of its
+    map, which is also the uid each key receives), int32 inverse indices,
+    first positions and counts."""
+    keys = np.asarray(keys)
+    if keys.size == 0:
+        e = np.empty(0, dtype=np.int32)
+        return keys[:0].copy(), e, e, e
+    u, first, inv, counts = np.unique(keys, return_index=True, return_inverse=True, return_counts=True)
+    order = np.argsort(first, kind="stable")
+    rank = np.empty_like(order)
+    rank[order] = np.arange(len(order))
+    return (u[order], rank[inv.reshape(-1)].astype(np.int32), first[order].astype(np.int32),
+            counts[order].astype(np.int32))
+
+
 def cpu_count() -> int:
     try:
         return len(os.sched_getaffinity(0))

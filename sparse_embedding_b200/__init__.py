@@ -28,6 +28,7 @@ from .partitioner import (
     partition,
     register_partitioner,
 )
+from .unique import async_unique, unique
 from .store import (
     Adagrad,
     Adam,

@@ -95,6 +95,7 @@ _SIGNATURES = {
     "se_store_profile_enable": [_vp, _i32],
     "se_store_profile_read": [_vp, C.c_char_p, C.POINTER(C.c_double), C.POINTER(_u64)],
     "se_partition": [_i32, _u32, _i32, _vp, _sz, _vp, _i32, _vp],
+    "se_unique": [_i32, _vp, _sz, _vp, _vp, _vp, _vp, C.POINTER(_u64), _i32, _vp],
     "se_filter": [_i32, _u32, _i32, _vp, _sz, _u32, _vp, _i32, _vp],
     "se_partition_route": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],
     "se_partition_route_noalloc": [_i32, _u32, _i32, _vp, _sz, _vp, _vp, _vp, _i32, _vp],

@@ -19,7 +19,7 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libse_gpu.so"
-SOURCES = ["se_store.cu", "se_partition.cu"]
+SOURCES = ["se_store.cu", "se_partition.cu", "se_unique.cu"]
 HEADERS = ["se_common.cuh", "se_host.hpp", "se_store_kernels.cuh", "se_partition.cuh", "se_exchange.cuh"]
 
 NVCC_FLAGS = [

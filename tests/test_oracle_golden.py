@@ -141,3 +141,25 @@ def test_threaded_oracle_matches_serial():
             s.optimizer_step(1)
         outs.append(s.lookup(np.unique(keys), 64))
     np.testing.assert_array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+def test_unique_oracle_reference_cases():
+    """The oracle's unique against the reference's own cases (tests/test_ops.py:9-153):
+    exact reconstruction, first positions, counts, all four key dtypes, empty input."""
+    keys = np.array([10, 20, 10, 30, 20, 40], dtype=np.int64)
+    u, inv, first, counts = O.unique_first_occurrence(keys)
+    assert u.tolist() == [10, 20, 30, 40] and inv.tolist() == [0, 1, 0, 2, 1, 3]
+    assert first.tolist() == [0, 1, 3, 5] and counts.tolist() == [2, 2, 1, 1]
+    np.random.seed(42)
+    for dtype in [np.int32, np.uint32, np.int64, np.uint64]:
+        keys = np.random.randint(0, 5000, size=50000, dtype=dtype)
+        u, inv, first, counts = O.unique_first_occurrence(keys)
+        np.testing.assert_array_equal(u[inv], keys)
+        ek, ef, ec = np.unique(keys, return_index=True, return_counts=True)
+        np.testing.assert_array_equal(np.sort(u), ek)
+        pos = np.searchsorted(ek, u)
+        np.testing.assert_array_equal(first, ef[pos])
+        np.testing.assert_array_equal(counts, ec[pos])
+        assert (np.diff(first) > 0).all()  # order of first appearance
+        e = O.unique_first_occurrence(np.empty(0, dtype=dtype))
+        assert all(x.size == 0 for x in e)
