@@ -432,11 +432,12 @@ def run_ours(args):
            "d2h_bytes_per_step": BATCH * R * world,
            "pipeline": "H2D, compute and D2H on separate streams, double-buffered"}
 
-    large = mut = uniq = None
+    large = mut = uniq = bag = None
     if world == 1 and not args.no_forward:
         large = large_batch_bench(store, torch, args.num_keys, peak)
         mut = mutation_bench(store, torch, args.num_keys, peak)
         uniq = unique_bench(se, torch, args.num_keys)
+        bag = dlrm_bag_bench(se, torch, peak)
 
     fwd = wide = None
     if world == 1 and not args.no_forward:
@@ -471,6 +472,8 @@ def run_ours(args):
         result["mutation"] = mut
     if uniq:
         result["unique"] = uniq
+    if bag:
+        result["embedding_bag"] = bag
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
     if api is not store:
@@ -658,6 +661,72 @@ def unique_bench(se, torch, num_keys):
                            "unique_keys": int(u.numel())}
     return {"workload": "unique with inverse, first positions and counts of train-step batches (int64, "
                         "Zipf 1.05 + 5% new), device-resident", "batches": out}
+
+
+def dlrm_bag_bench(se, torch, peak):
+    """DLRM-shaped embedding-bag step: 26 tables' pre-mixed u64 keys in one
+    dim-128 fp32 store with Adam(1e-3); 8,192 samples x 26 tables x
+    max(1, Poisson(20)) ids (~4.3M ids per step) drawn Zipf(1.2) over each
+    table's rows (1e3..2e6 rows per table, log-uniform: the reference config's
+    shape with its row ranges scaled down so the batches are generated in
+    seconds); step = embedding_bag with insert -> embedding_bag_backward of
+    N(0, 1e-3) pooled gradients -> optimizer_step(1). Eager calls, CUDA events."""
+    from sparse_embedding_b200.workloads import DlrmWorkload
+
+    wl = DlrmWorkload(max_rows=2_000_000)
+    dim = wl.dim
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", initial_capacity=8_000_000),
+                              optimizer_config=se.Adam(lr=1e-3))
+    steps, warm = 4, 2
+    batches = []
+    for s in range(warm + steps):
+        k, o, g = wl.make_bags(s)
+        batches.append((torch.from_numpy(k.view(np.int64)).cuda().view(torch.uint64), torch.from_numpy(o).cuda(),
+                        torch.from_numpy(g).cuda()))
+    ids = [int(b[0].numel()) for b in batches[warm:]]
+    uniq = [int(torch.unique(b[0].view(torch.int64)).numel()) for b in batches[warm:]]
+
+    def step(b):
+        k, o, g = b
+        store.embedding_bag(k, o, dim, insert=True)
+        store.embedding_bag_backward(k, o, g)
+        store.optimizer_step(1)
+    for b in batches[:warm]:
+        step(b)
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for b in batches[warm:]:
+        step(b)
+    e.record()
+    torch.cuda.synchronize()
+    el = a.elapsed_time(e) / 1e3
+    store.profile(True)
+    for b in batches[warm:]:
+        step(b)
+    torch.cuda.synchronize()
+    kern = {}
+    for nm in ["k_bag_insert", "k_bag_pool", "k_accumulate", "k_group_fix", "k_group_alloc", "k_group_place",
+               "k_group_apply", "k_group_hot"]:
+        ms, cnt = store.profile_read(nm)
+        if cnt:
+            kern[nm] = round(ms / cnt * 1e3, 1)
+    store.profile(False)
+    R = dim * 4
+    nb = wl.batch * wl.tables
+    # each distinct row read once, a row number per id, the pooled rows written
+    pool_bytes = sum(uniq) / len(uniq) * R + sum(ids) / len(ids) * 4 + nb * R
+    pool_gbs = pool_bytes / (kern.get("k_bag_pool", float("nan")) / 1e6) / 1e9
+    out = {"workload": "DLRM-shaped bag step: 26 tables, 8,192 samples, ~4.3M ids/step, dim 128 fp32, Adam; "
+                       "rows per table 1e3..2e6 (scaled down from 4e7)",
+           "ids_per_step": int(sum(ids) / len(ids)), "unique_ids_per_step": int(sum(uniq) / len(uniq)),
+           "bags_per_step": nb, "us_per_step": round(el / steps * 1e6, 1),
+           "value": sum(ids) / el, "unit": "ids/s", "kernel_us": kern, "rows": store.total_size(),
+           "k_bag_pool": {"algorithmic_bytes": int(pool_bytes), "achieved_gbs": round(pool_gbs, 1),
+                          "frac": round(pool_gbs / peak, 4)}}
+    del store
+    torch.cuda.empty_cache()
+    return out
 
 
 def forward_wide_bench(se, torch, N, num_keys):

@@ -151,6 +151,24 @@ int se_assign_dim(se_store *store, const void *keys, size_t num_keys, int64_t di
 int se_erase(se_store *store, const void *keys, size_t num_keys, void *stream);
 int se_erase_dimension(se_store *store, int64_t dim, const void *keys, size_t num_keys, void *stream);
 
+/* Embedding bag (no counterpart in the reference, whose DLRM users pool the
+ * rows of lookup / lookup_or_insert themselves): sum pooling of multi-hot
+ * bags. Bag b holds keys [offsets[b], offsets[b+1]) (int64 CSR offsets,
+ * num_bags + 1 entries); out_pooled[b] (dim values of ParamT) is the sum of
+ * their parameter rows in key order, in fp32 from +0.0, rounded once to
+ * ParamT. Absent keys add a zero row, or with insert != 0 are inserted first
+ * as lookup_or_insert does. Offsets in host memory must start at 0, be
+ * non-decreasing and end at num_keys; device offsets are clamped to
+ * [0, num_keys]. */
+int se_embedding_bag(se_store *store, const void *keys, size_t num_keys, const int64_t *offsets,
+                     size_t num_bags, int64_t dim, void *out_pooled, int32_t insert, void *stream);
+/* Backward of se_embedding_bag: every key of bag b accumulates pooled_grads[b]
+ * (dim values of the gradient dtype) - the same result as
+ * se_accumulate_gradients with the pooled gradient repeated for each key,
+ * without building the repeated rows. */
+int se_embedding_bag_backward(se_store *store, const void *keys, size_t num_keys, const int64_t *offsets,
+                              size_t num_bags, int64_t dim, const void *pooled_grads, void *stream);
+
 /* Metadata conventions (embedding_table_interface.hpp:317-396). */
 int se_store_size(se_store *store, uint64_t *out_size);
 int se_store_dim_size(se_store *store, int64_t dim, uint64_t *out_size);

@@ -305,6 +305,22 @@ def unique_first_occurrence(keys):
             counts[order].astype(np.int32))
 
 
+def pool_bags(rows, offsets):
+    """Sum pooling of multi-hot bags as the DLRM harness does it (a fixed id
+    order per (sample, table)): out[b] = rows[offsets[b]] + rows[offsets[b]+1]
+    + ... in float32, one add at a time in key order from +0.0 (numpy's
+    reductions may add pairwise, so the adds are stepped by position)."""
+    rows = np.asarray(rows, dtype=np.float32)
+    offsets = np.asarray(offsets, dtype=np.int64)
+    nb = len(offsets) - 1
+    lens = np.diff(offsets)
+    out = np.zeros((nb, rows.shape[1]), dtype=np.float32)
+    for k in range(int(lens.max()) if nb else 0):
+        live = np.nonzero(lens > k)[0]
+        out[live] = out[live] + rows[offsets[live] + k]
+    return out
+
+
 def cpu_count() -> int:
     try:
         return len(os.sched_getaffinity(0))

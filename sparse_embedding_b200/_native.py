@@ -83,6 +83,8 @@ _SIGNATURES = {
     "se_assign": [_vp, _vp, _sz, _vp, _sz, C.POINTER(_i64), _sz, _vp],
     "se_assign_dim": [_vp, _vp, _sz, _i64, _vp, _vp],
     "se_erase": [_vp, _vp, _sz, _vp],
+    "se_embedding_bag": [_vp, _vp, _sz, _vp, _sz, _i64, _vp, _i32, _vp],
+    "se_embedding_bag_backward": [_vp, _vp, _sz, _vp, _sz, _i64, _vp, _vp],
     "se_erase_dimension": [_vp, _i64, _vp, _sz, _vp],
     "se_store_size": [_vp, C.POINTER(_u64)],
     "se_store_dim_size": [_vp, _i64, C.POINTER(_u64)],

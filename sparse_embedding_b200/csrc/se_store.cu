@@ -9,6 +9,7 @@
 
 #include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
+#include <cub/device/device_radix_sort.cuh>
 
 #include <algorithm>
 #include <cmath>
@@ -269,13 +270,17 @@ __device__ __forceinline__ void count_entries(const CountWs &c, bool valid, uint
 // (106-128): scaled = g / gradient_scale must be finite and within both the
 // gradient and the parameter dtype; the stored row is g (scale 1) or the
 // scaled value rounded to the gradient dtype.
-template <int VEC>
+//
+// With kBag the gradient row of entry i is row grad_row[i] of `grads` (the
+// backward of a sum-pooled bag: every key of bag b gets the bag's gradient).
+template <int VEC, bool kBag = false>
 __global__ void __launch_bounds__(256)
 k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
              void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
-             uint32_t *err, CountWs cw, int count_rows, const uint32_t *__restrict__ known_rows) {
+             uint32_t *err, CountWs cw, int count_rows, const uint32_t *__restrict__ known_rows,
+             const uint32_t *__restrict__ grad_row) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t stride = size_t(gridDim.x) * blockDim.x;
@@ -316,8 +321,15 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
   for (size_t c0 = tid; c0 < chunks; c0 += stride * kIlp) {
     float g[kIlp][VEC];
 #pragma unroll
-    for (int k = 0; k < kIlp; ++k)
-      if (c0 + k * stride < chunks) ldv<VEC>(grads, gdt, (c0 + k * stride) * VEC, g[k]);
+    for (int k = 0; k < kIlp; ++k) {
+      if (c0 + k * stride >= chunks) continue;
+      size_t e = (c0 + k * stride) * VEC;
+      if constexpr (kBag) {
+        const size_t i = e / dim;  // VEC divides dim: a chunk stays inside one entry
+        e = size_t(grad_row[i]) * dim + (e - i * dim);
+      }
+      ldv<VEC>(grads, gdt, e, g[k]);
+    }
 #pragma unroll
     for (int k = 0; k < kIlp; ++k) {
       if (c0 + k * stride >= chunks) continue;
@@ -482,6 +494,7 @@ struct GroupWs {
   uint32_t *long_list;  // [P] segments of short_max+1 .. long_max rows (listed by k_group_alloc)
   uint32_t short_max, long_max;  // row bounds of the apply kernel's short and long segments
   uint32_t cap;        // P: entries the [P] buffers hold (the host's pending count)
+  uint32_t sorted;     // 1: pos was filled by a stable sort (each segment's slice in arrival order)
   uint32_t *status;    // table status word (kStatusPendingOverflow)
   // cleared by the last block of k_group_hot, the step's last kernel, for
   // the next window: ctr[0..3], the unresolved count, the pending count
@@ -567,8 +580,10 @@ __global__ void __launch_bounds__(256) k_group_alloc(GroupWs w, const uint32_t *
     if (cnt > w.short_max && cnt <= w.long_max) w.long_list[atomicAdd(&w.ctr[3], 1u)] = sid;
     if (cnt > w.long_max) {
       // work items of k_group_hot: windows of the batch's positions
+      // parts: ranks of a sorted slice, or windows of the batch's positions
       const uint32_t count = step_count(count_p, w);
-      const uint32_t nparts = max((cnt + kPartEntries - 1) / kPartEntries, (count + kHotWindowBits - 1) / kHotWindowBits);
+      const uint32_t by_rows = (cnt + kPartEntries - 1) / kPartEntries;
+      const uint32_t nparts = w.sorted ? by_rows : max(by_rows, (count + kHotWindowBits - 1) / kHotWindowBits);
       const uint32_t base = atomicAdd(&w.ctr[2], nparts);
       for (uint32_t q = 0; q < nparts; ++q) w.items[base + q] = make_uint4(sid, q, nparts, base);
     }
@@ -590,6 +605,23 @@ __global__ void __launch_bounds__(256) k_group_place(const uint32_t *count_p, Gr
   if (sid != 0xffffffffu && rank == 0) base = atomicAdd(&w.seg_fill[sid], uint32_t(__popc(peers)));
   base = __shfl_sync(0xffffffffu, base, __ffs(peers) - 1);
   if (sid != 0xffffffffu) w.pos[w.seg_off[sid] + base + rank] = i;
+}
+
+// Phase 3 for large windows (more pending rows than one hot-key bitmap
+// window): the key of each entry is its segment's first slot, so a stable
+// radix sort of (key, position) lays every segment's positions out in
+// arrival order. Entries without a row sort past every segment.
+__global__ void __launch_bounds__(256)
+k_group_sortkeys(const uint32_t *count_p, GroupWs w, uint32_t *__restrict__ keys, uint32_t *__restrict__ vals,
+                 uint32_t last_key) {
+  pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
+  const uint32_t count = step_count(count_p, w);
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= w.cap) return;
+  const uint32_t row = i < count ? w.rows[i] : kNoRow;
+  keys[i] = row != kNoRow ? w.seg_off[w.row_seg[row]] : last_key;
+  vals[i] = i;
 }
 
 __device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
@@ -752,23 +784,35 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
     win = (win + 31u) & ~31u;
     const uint32_t w0 = min(q * win, count), w1 = min(w0 + win, count);
     const uint32_t nwords = (w1 - w0 + 31u) / 32u;
-    // The segment's rows inside [w0, w1), as a bitmap over the window.
-    for (uint32_t j = 0; j < WPT; ++j) bitmap[threadIdx.x * WPT + j] = 0u;
-    __syncthreads();
-    for (uint32_t k = threadIdx.x; k < cnt; k += kBlockThreads) {
-      const uint32_t p = w.pos[off + k];
-      if (p >= w0 && p < w1) atomicOr(&bitmap[(p - w0) >> 5], 1u << ((p - w0) & 31u));
+    // Sorted: the part is ranks [lo, lo + total) of the segment's slice.
+    const uint32_t per = (cnt + nparts - 1) / nparts;
+    const uint32_t lo = min(q * per, cnt);
+    uint32_t excl = 0, total = 0;
+    if (w.sorted) {
+      total = min(lo + per, cnt) - lo;
+    } else {
+      // The segment's rows inside [w0, w1), as a bitmap over the window.
+      for (uint32_t j = 0; j < WPT; ++j) bitmap[threadIdx.x * WPT + j] = 0u;
+      __syncthreads();
+      for (uint32_t k = threadIdx.x; k < cnt; k += kBlockThreads) {
+        const uint32_t p = w.pos[off + k];
+        if (p >= w0 && p < w1) atomicOr(&bitmap[(p - w0) >> 5], 1u << ((p - w0) & 31u));
+      }
+      __syncthreads();
+      uint32_t bits = 0;
+      for (uint32_t j = 0; j < WPT; ++j) {
+        const uint32_t wi = threadIdx.x * WPT + j;
+        bits += wi < nwords ? __popc(bitmap[wi]) : 0u;
+      }
+      Scan(scan_tmp).ExclusiveSum(bits, excl, total);
     }
-    __syncthreads();
-    uint32_t bits = 0;
-    for (uint32_t j = 0; j < WPT; ++j) {
-      const uint32_t wi = threadIdx.x * WPT + j;
-      bits += wi < nwords ? __popc(bitmap[wi]) : 0u;
-    }
-    uint32_t excl, total;
-    Scan(scan_tmp).ExclusiveSum(bits, excl, total);
-    // Compacts the window's rows of rank [r0, r0 + kRoundEntries) into s_pos.
+    // Compacts the part's rows of rank [r0, r0 + kRoundEntries) into s_pos.
     auto compact = [&](uint32_t r0) {
+      if (w.sorted) {
+        const uint32_t m = min(total - r0, kRoundEntries);
+        for (uint32_t k = threadIdx.x; k < m; k += kBlockThreads) s_pos[k] = w.pos[off + lo + r0 + k];
+        return;
+      }
       uint32_t rank = excl;
       for (uint32_t j = 0; j < WPT; ++j) {
         const uint32_t wi = threadIdx.x * WPT + j;
@@ -842,8 +886,9 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
       __threadfence();
       __syncthreads();
       if (threadIdx.x == 0) {
-        const uint32_t old = atomicAdd(&w.seg_fill[s], 1u);  // placement left it at cnt
-        s_last = old == cnt + nparts - 1 ? 1u : 0u;
+        // atomic placement left the counter at cnt, sorted placement at 0
+        const uint32_t old = atomicAdd(&w.seg_fill[s], 1u);
+        s_last = old == (w.sorted ? 0u : cnt) + nparts - 1 ? 1u : 0u;
         s_step = (s_last && !poisoned && o.kind == SE_OPT_ADAM) ? next_step(L, slab) : 0u;
       }
       __syncthreads();
@@ -1052,6 +1097,149 @@ k_requeue_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t *_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Embedding bag: sum-pooled gather of multi-hot bags and its backward
+// ---------------------------------------------------------------------------
+
+// Rows of a bag batch's keys, inserting absent ones with lookup_or_insert's
+// claim and initialisation (hogwild_embedding_store.hpp:4925-4980), written
+// as row numbers for the pooling kernel; keys claimed by another group of
+// the same launch are finished by k_bag_deferred.
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_bag_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init, const void *__restrict__ keys,
+             int kdt, size_t n, uint32_t *__restrict__ rows_out, uint32_t *def_count, uint32_t *def_pos,
+             unsigned long long *def_word, uint32_t *status) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t i = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (i >= n) return;
+  const unsigned mask = group_mask<LANES>();
+  const uint64_t key = load_key(keys, kdt, i);
+  int kind = kFound;
+  uint32_t row = kNoRow;
+  uint32_t *word = nullptr;
+  if (lane == 0) {
+    const InsertResult r = dir_find_or_insert(d, key);
+    kind = r.kind;
+    word = r.row_word;
+    if (kind == kFound) kind = resolve_found(word, &row);
+    else if (kind == kFull) raise_status(status, kStatusTableFull);
+  }
+  const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
+  if (lane == 0 && kind == kInserted) {
+    row = taken;
+    if (row >= ra.capacity) {
+      raise_status(status, kStatusTableFull);
+      kind = kFull;
+    }
+  }
+  kind = __shfl_sync(mask, kind, 0, LANES);
+  row = __shfl_sync(mask, row, 0, LANES);
+  if (kind == kInserted) {
+    uint8_t *slab = slabs + size_t(row) * L.stride;
+    init_slab<LANES, VEC>(L, slab, init, key, lane, slab);  // no copy out: the parameters go to the slab only
+    __threadfence();
+    __syncwarp(mask);
+    if (lane == 0) atomicExch(word, row);
+  }
+  if (lane == 0) {
+    if (kind == 3) {
+      const uint32_t j = atomicAdd(def_count, 1u);
+      def_pos[j] = uint32_t(i);
+      def_word[j] = reinterpret_cast<unsigned long long>(word);
+    } else {
+      rows_out[i] = (kind == kFound || kind == kInserted) ? row : kNoRow;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+k_bag_deferred(const uint32_t *def_count, const uint32_t *def_pos, const unsigned long long *def_word,
+               uint32_t *__restrict__ rows_out, uint32_t *status) {
+  const uint32_t count = *def_count;
+  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < count; j += gridDim.x * blockDim.x) {
+    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
+    if (row == kNoRow) raise_status(status, kStatusTableFull);
+    rows_out[def_pos[j]] = row;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+k_bag_find(Dir d, const void *__restrict__ keys, int kdt, size_t n, uint32_t *__restrict__ rows_out) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) rows_out[i] = dir_find<false>(d, load_key(keys, kdt, i));
+}
+
+// Bag of every key position: bag b covers [offsets[b], offsets[b+1]) clamped
+// to [0, n] (positions outside every bag keep bag 0, so any offsets index in
+// bounds). One warp per bag.
+__global__ void __launch_bounds__(256)
+k_bag_of(const int64_t *__restrict__ offsets, size_t nbags, size_t n, uint32_t *__restrict__ bag_of) {
+  const size_t warps = size_t(gridDim.x) * blockDim.x / 32;
+  const uint32_t lane = threadIdx.x & 31u;
+  for (size_t b = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) / 32; b < nbags; b += warps) {
+    const int64_t lo = min(max(offsets[b], int64_t(0)), int64_t(n));
+    const int64_t hi = min(max(offsets[b + 1], lo), int64_t(n));
+    for (int64_t j = lo + lane; j < hi; j += 32) bag_of[j] = uint32_t(b);
+  }
+}
+
+// out[b] = sum of the parameter rows of keys [offsets[b], offsets[b+1]) in
+// key order: fp32 adds from +0.0 (an absent key adds a zero row), rounded
+// once to the value dtype. Offsets are clamped to [0, n]. A group of LANES
+// lanes per bag; each lane keeps four rows' loads in flight.
+template <int LANES, int VEC>
+__global__ void __launch_bounds__(256)
+k_bag_pool(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *__restrict__ rows, size_t n,
+           const int64_t *__restrict__ offsets, size_t nbags, void *__restrict__ out) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  const size_t pb = L.pdt == SE_FLOAT32 ? 4 : 2;
+  for (size_t b = t / LANES; b < nbags; b += groups) {
+    const int64_t lo = min(max(offsets[b], int64_t(0)), int64_t(n));
+    const int64_t hi = min(max(offsets[b + 1], lo), int64_t(n));
+    void *orow = static_cast<uint8_t *>(out) + b * size_t(L.dim) * pb;
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+      float acc[VEC];
+#pragma unroll
+      for (int x = 0; x < VEC; ++x) acc[x] = 0.0f;
+      int64_t j = lo;
+      for (; j + 4 <= hi; j += 4) {
+        float v[4][VEC];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t r = __ldg(rows + j + q);
+          if (r != kNoRow) {
+            ldv<VEC>(slabs + size_t(r) * L.stride, L.pdt, e, v[q]);
+          } else {
+#pragma unroll
+            for (int x = 0; x < VEC; ++x) v[q][x] = 0.0f;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int x = 0; x < VEC; ++x) acc[x] = __fadd_rn(acc[x], v[q][x]);
+      }
+      for (; j < hi; ++j) {
+        const uint32_t r = __ldg(rows + j);
+        float v[VEC];
+        if (r != kNoRow) {
+          ldv<VEC>(slabs + size_t(r) * L.stride, L.pdt, e, v);
+        } else {
+#pragma unroll
+          for (int x = 0; x < VEC; ++x) v[x] = 0.0f;
+        }
+#pragma unroll
+        for (int x = 0; x < VEC; ++x) acc[x] = __fadd_rn(acc[x], v[x]);
+      }
+      stv<VEC>(orow, L.pdt, e, acc);
+    }
+  }
+}
+
 // Reads the rows of a few keys (state inspection for tests).
 __global__ void k_find_rows(Dir d, const unsigned long long *keys, uint32_t n, uint32_t *rows) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1180,6 +1368,8 @@ struct Table {
   bool erased = false;  // inserts look at the free stack only once a key was erased
   // step and insert work buffers
   Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_long, def_pos;
+  Scratch<uint32_t> g_sort_kin, g_sort_kout, g_sort_vin;  // sorted placement of large windows
+  Scratch<uint8_t> g_sort_tmp;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -1230,6 +1420,8 @@ struct StoreImpl {
   Scratch<uint8_t> stage_keys, stage_vals;
   Scratch<unsigned long long> dup_set;  // assign's repeated-key check
   Scratch<uint32_t> dup_words;
+  Scratch<uint8_t> stage_offs;             // embedding-bag offsets staged from the host
+  Scratch<uint32_t> bag_rows, bag_of_buf;  // rows of a bag batch's keys; bag of each key
   bool profiling = false;
   std::vector<ProfRec> prof;
   std::vector<cudaEvent_t> event_pool;
@@ -1717,6 +1909,120 @@ struct StoreImpl {
     if (!is_device_ptr(keys)) cuda_check(cudaStreamSynchronize(st), "sync");
   }
 
+  // ---- embedding bag ------------------------------------------------------------
+  // Offsets in host memory are checked (CSR: start at 0, non-decreasing, end
+  // at n); device offsets are used as given, clamped by the kernels.
+  static void check_offsets(const int64_t *offsets, size_t nbags, size_t n) {
+    if (offsets == nullptr) throw std::invalid_argument("offsets is null");
+    if (is_device_ptr(offsets)) return;
+    if (offsets[0] != 0 || offsets[nbags] != int64_t(n))
+      throw std::invalid_argument("offsets must start at 0 and end at the number of keys");
+    for (size_t b = 0; b < nbags; ++b)
+      if (offsets[b + 1] < offsets[b]) throw std::invalid_argument("offsets must be non-decreasing");
+  }
+
+  void embedding_bag(const void *keys, size_t n, const int64_t *offsets, size_t nbags, int64_t dim, void *out,
+                     bool insert, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("dim must be > 0");
+    Table &t = table(dim);
+    if (nbags == 0) return;
+    check_offsets(offsets, nbags, n);
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    const size_t vb = value_bytes(cfg.value_dtype);
+    const size_t out_bytes = nbags * size_t(dim) * vb;
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const auto *doffs = static_cast<const int64_t *>(stage_in(stage_offs, offsets, (nbags + 1) * 8, st));
+    const bool host_out = !is_device_ptr(out);
+    void *dout = host_out ? stage_vals.get(out_bytes) : out;
+    uint32_t *rows = bag_rows.get(std::max<size_t>(n, 1));
+    const bool vec4 = t.vec == 4;
+    if (n > 0) {
+      if (insert) {
+        ensure_rows(t, n, st);
+        cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
+        uint32_t *dpos = t.def_pos.get(n);
+        unsigned long long *dword = t.def_word.get(n);
+        InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
+                      cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
+        auto go = [&](auto lanes_tag, auto vec_tag) {
+          constexpr int LN = decltype(lanes_tag)::value;
+          constexpr int VC = decltype(vec_tag)::value;
+          Prof pr(this, "k_bag_insert", st);
+          k_bag_insert<LN, VC><<<grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st>>>(
+              t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n, rows, t.ctr + kCtrDeferred, dpos,
+              dword, t.ctr + kCtrStatus);
+          launched("k_bag_insert");
+        };
+        auto by_lanes = [&](auto vec_tag) {
+          switch (pick_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim))) {
+          case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+          case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+          case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+          default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+          }
+        };
+        if (vec4) by_lanes(std::integral_constant<int, 4>{});
+        else by_lanes(std::integral_constant<int, 1>{});
+        k_bag_deferred<<<grid_for(n, 256, 148 * 4), 256, 0, st>>>(t.ctr + kCtrDeferred, dpos, dword, rows,
+                                                                  t.ctr + kCtrStatus);
+        launched("k_bag_deferred");
+      } else {
+        Prof pr(this, "k_bag_find", st);
+        k_bag_find<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, rows);
+        launched("k_bag_find");
+      }
+    }
+    const bool pool4 = vec4 && uintptr_t(dout) % 16 == 0;
+    auto pool = [&](auto lanes_tag, auto vec_tag) {
+      constexpr int LN = decltype(lanes_tag)::value;
+      constexpr int VC = decltype(vec_tag)::value;
+      Prof pr(this, "k_bag_pool", st);
+      k_bag_pool<LN, VC><<<grid_for(nbags * LN, 256, 148 * 64), 256, 0, st>>>(t.L, t.slabs, rows, n, doffs, nbags,
+                                                                               dout);
+      launched("k_bag_pool");
+    };
+    auto pool_lanes = [&](auto vec_tag) {
+      switch (pick_lanes(pool4 ? uint64_t(dim) / 4 : uint64_t(dim))) {
+      case 4: pool(std::integral_constant<int, 4>{}, vec_tag); break;
+      case 8: pool(std::integral_constant<int, 8>{}, vec_tag); break;
+      case 16: pool(std::integral_constant<int, 16>{}, vec_tag); break;
+      default: pool(std::integral_constant<int, 32>{}, vec_tag); break;
+      }
+    };
+    if (pool4) pool_lanes(std::integral_constant<int, 4>{});
+    else pool_lanes(std::integral_constant<int, 1>{});
+    if (host_out) {
+      cuda_check(cudaMemcpyAsync(out, dout, out_bytes, cudaMemcpyDeviceToHost, st), "copy out");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+      if (insert) check_status(t, st);
+    } else if (!is_device_ptr(keys) || !is_device_ptr(offsets)) {
+      cuda_check(cudaStreamSynchronize(st), "sync");  // the staging buffers are reused by the next call
+    }
+  }
+
+  // Backward of the sum pooling: every key of bag b accumulates pooled_grads[b]
+  // (accumulate_gradients of the expanded rows, without expanding them).
+  void embedding_bag_backward(const void *keys, size_t n, const int64_t *offsets, size_t nbags, int64_t dim,
+                              const void *pooled_grads, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("gradient row length must be positive");
+    table(dim);
+    if (nbags == 0 || n == 0) return;
+    check_offsets(offsets, nbags, n);
+    if (n > 0x7fffffffull) throw std::invalid_argument("batch exceeds 2^31 keys");
+    cudaStream_t st = pick(sp);
+    const auto *doffs = static_cast<const int64_t *>(stage_in(stage_offs, offsets, (nbags + 1) * 8, st));
+    uint32_t *bag_of = bag_of_buf.get(n);
+    cuda_check(cudaMemsetAsync(bag_of, 0, n * 4, st), "memset");
+    k_bag_of<<<grid_for(nbags * 32, 256, 148 * 32), 256, 0, st>>>(doffs, nbags, n, bag_of);
+    launched("k_bag_of");
+    accumulate_locked(keys, n, nullptr, dim, pooled_grads, sp, -1, nullptr, bag_of, nbags);
+  }
+
   void accumulate(const void *keys, size_t n, int64_t dim, const void *grads, void *sp) {
     std::lock_guard<std::mutex> lock(mu);
     accumulate_locked(keys, n, nullptr, dim, grads, sp);
@@ -1726,8 +2032,11 @@ struct StoreImpl {
   // whose size is only known on the device (exchanged batches); kdt: key
   // dtype of `keys` when it differs from the store's (exchanged keys are u64).
   // known_rows: the rows of `keys` when the caller resolved them already.
+  // grad_row: device array, the row of `grads` (grad_rows rows) that entry i
+  // takes (embedding-bag backward); null: row i.
   void accumulate_locked(const void *keys, size_t n, const uint32_t *n_dev, int64_t dim, const void *grads,
-                         void *sp, int kdt = -1, const uint32_t *known_rows = nullptr) {
+                         void *sp, int kdt = -1, const uint32_t *known_rows = nullptr,
+                         const uint32_t *grad_row = nullptr, size_t grad_rows = 0) {
     DeviceGuard dg(device);
     if (dim <= 0) throw std::invalid_argument("gradient row length must be positive");
     Table &t = table(dim);
@@ -1737,7 +2046,7 @@ struct StoreImpl {
     const size_t gb = value_bytes(cfg.gradient_dtype);
     if (kdt < 0) kdt = cfg.key_dtype;
     const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(kdt), st);
-    const void *dgrads = stage_in(stage_vals, grads, n * size_t(dim) * gb, st);
+    const void *dgrads = stage_in(stage_vals, grads, (grad_row ? grad_rows : n) * size_t(dim) * gb, st);
     const float maxv = std::min(host_dtype_max(cfg.gradient_dtype), host_dtype_max(cfg.value_dtype));
     // dim % 4 == 0 keeps every appended row 16-byte (fp32) / 8-byte aligned.
     const bool vec4 = dim % 4 == 0 && uintptr_t(dgrads) % 16 == 0;
@@ -1760,16 +2069,18 @@ struct StoreImpl {
       // 4 blocks per SM: enough 16-byte loads in flight to stream the rows,
       // and few blocks to count in for the commit
       const unsigned grid = grid_for(std::max(chunks, n), 256, 148 * 4);
-      if (vec4)
-        pdl(k_accumulate<4>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
-                                              size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows);
-      else
-        pdl(k_accumulate<1>, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
-                                              uint32_t(dim), cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads,
-                                              size_t(t.pcap), t.ctr + kCtrPending, t.ctr + kCtrAccDone, status_word,
-                                              t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows);
+      auto go = [&](auto kern) {
+        pdl(kern, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype, uint32_t(dim),
+            cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads, size_t(t.pcap), t.ctr + kCtrPending,
+            t.ctr + kCtrAccDone, status_word, t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows, grad_row);
+      };
+      if (grad_row) {
+        if (vec4) go(k_accumulate<4, true>);
+        else go(k_accumulate<1, true>);
+      } else {
+        if (vec4) go(k_accumulate<4, false>);
+        else go(k_accumulate<1, false>);
+      }
       launched("k_accumulate");
     }
     if (!device_inputs) {
@@ -1839,12 +2150,20 @@ struct StoreImpl {
     }
     // Upper bound on k_group_hot work items: segments of more than `lanes`
     // rows, each cut into max(ceil(rows / kPartEntries), ceil(P / window)) parts.
+    // Sorted placement (more than one window of pending rows): no window
+    // minimum, and only segments of more than long_max rows are items.
+    const bool sorted = P > kHotWindowBits && P <= 0x7fffffffu;  // the sort takes an int count
     const uint64_t min_parts = (uint64_t(P) + kHotWindowBits - 1) / kHotWindowBits;
-    const uint64_t max_items = uint64_t(P) / kPartEntries + 1 + (uint64_t(P) / 5 + 1) * (min_parts + 1);
+    const uint64_t max_items =
+        sorted ? uint64_t(P) / kPartEntries + uint64_t(P) / (uint64_t(w.long_max) + 1) + 1
+               : uint64_t(P) / kPartEntries + 1 + (uint64_t(P) / 5 + 1) * (min_parts + 1);
     w.items = reinterpret_cast<uint4 *>(t.g_items.get(max_items));
     w.partials = t.g_partials.get(max_items * uint64_t(t.dim));
     w.ctr = t.ctr + kCtrGroup;
     w.cap = P;
+    // More pending rows than one hot-key window: segments are laid out by a
+    // sort instead of windowed bitmaps (each bitmap pass costs P/32 words).
+    w.sorted = sorted ? 1u : 0u;
     w.status = t.ctr + kCtrStatus;
     // ctr[0] (segments) was counted with the entries; ctr[1..3] are zero
     // (cleared with the window's other counters by the previous step)
@@ -1863,7 +2182,25 @@ struct StoreImpl {
       pdl(k_group_alloc, g, 256, 0, st, w, t.ctr + kCtrPending);
       launched("k_group_alloc");
     }
-    {
+    if (w.sorted) {
+      // stable sort of (segment's first slot, position): the key needs
+      // bits for every slot below P plus one key past them
+      int end_bit = 1;
+      while ((uint64_t(1) << end_bit) <= uint64_t(P)) ++end_bit;
+      uint32_t *kin = t.g_sort_kin.get(P), *kout = t.g_sort_kout.get(P), *vin = t.g_sort_vin.get(P);
+      size_t tmp_bytes = 0;
+      cuda_check(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, kin, kout, vin, w.pos, int(P), 0, end_bit, st),
+                 "sort size");
+      uint8_t *tmp = t.g_sort_tmp.get(tmp_bytes);
+      {
+        Prof pr(this, "k_group_sortkeys", st);
+        pdl(k_group_sortkeys, g, 256, 0, st, t.ctr + kCtrPending, w, kin, vin, uint32_t((uint64_t(1) << end_bit) - 1));
+        launched("k_group_sortkeys");
+      }
+      Prof pr(this, "k_group_place", st);
+      cuda_check(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, kin, kout, vin, w.pos, int(P), 0, end_bit, st),
+                 "sort");
+    } else {
       Prof pr(this, "k_group_place", st);
       pdl(k_group_place, g, 256, 0, st, t.ctr + kCtrPending, w);
       launched("k_group_place");
@@ -2412,6 +2749,18 @@ int se_assign(se_store *store, const void *keys, size_t n, const void *values, s
     if (n == 0) return;
     if (num_values != n * size_t(d)) throw std::invalid_argument("values size does not match row lengths");
     checked(store)->impl.assign(keys, n, d, values, stream);
+  });
+}
+
+int se_embedding_bag(se_store *store, const void *keys, size_t n, const int64_t *offsets, size_t num_bags,
+                     int64_t dim, void *out, int32_t insert, void *stream) {
+  return guarded([&] { checked(store)->impl.embedding_bag(keys, n, offsets, num_bags, dim, out, insert != 0, stream); });
+}
+
+int se_embedding_bag_backward(se_store *store, const void *keys, size_t n, const int64_t *offsets,
+                              size_t num_bags, int64_t dim, const void *pooled_grads, void *stream) {
+  return guarded([&] {
+    checked(store)->impl.embedding_bag_backward(keys, n, offsets, num_bags, dim, pooled_grads, stream);
   });
 }
 

@@ -378,6 +378,56 @@ class EmbeddingStore:
         stream = self._stream(g) or self._stream(k)
         N.check(self._lib.se_accumulate_gradients_dim(self._h, k.ptr, n, dim, g.ptr, stream))
 
+    # ---- embedding bag ------------------------------------------------------------
+
+    def _offsets(self, offsets, k: Arr, what: str = "offsets") -> Arr:
+        o = as_input(offsets, what)
+        if len(o.shape) != 1 or o.size < 1:
+            raise ValueError("offsets must be a 1D tensor of num_bags + 1 entries")
+        if o.dtype != "int64":
+            raise ValueError("offsets must be int64")
+        if (o.cuda_device is None) != (k.cuda_device is None):
+            raise ValueError("keys and offsets must be in the same memory space")
+        return o
+
+    def embedding_bag(self, keys, offsets, dim: int, insert: bool = True):
+        """Sum-pooled rows of multi-hot bags: out[b] = sum of the rows of
+        keys[offsets[b]:offsets[b+1]] in key order (fp32 adds, rounded once to
+        the value dtype). With insert, absent keys are inserted first
+        (lookup_or_insert); else they add zero rows. Returns [num_bags, dim]."""
+        self._check_operational()
+        dim = int(dim)
+        if dim <= 0:
+            raise ValueError("dim must be > 0")
+        k = self._keys(keys)
+        o = self._offsets(offsets, k)
+        nb = o.size - 1
+        out = empty_like_space(k, (nb, dim), self._value_dtype)
+        N.check(self._lib.se_embedding_bag(self._h, k.ptr, k.size, o.ptr, nb, dim, data_ptr(out), int(bool(insert)),
+                                           self._stream(k)))
+        return out
+
+    def embedding_bag_backward(self, keys, offsets, pooled_grads) -> None:
+        """Accumulates pooled_grads[b] (gradient dtype, [num_bags, dim]) as the
+        gradient of every key of bag b."""
+        if not self._optimizer_enabled:
+            raise RuntimeError("accumulate_gradients requires optimizer enabled")
+        self._check_operational()
+        k = self._keys(keys)
+        o = self._offsets(offsets, k)
+        g = as_input(pooled_grads, "grads")
+        self._check_device(g)
+        nb = o.size - 1
+        if len(g.shape) != 2 or g.shape[0] != nb:
+            raise ValueError("pooled_grads must be [num_bags, dim]")
+        if g.dtype != self._gradient_dtype:
+            raise ValueError("dtype mismatch in dlpack_to_span")
+        if (k.cuda_device is None) != (g.cuda_device is None):
+            raise ValueError("keys and grads must be in the same memory space")
+        stream = self._stream(g) or self._stream(k)
+        N.check(self._lib.se_embedding_bag_backward(self._h, k.ptr, k.size, o.ptr, nb, int(g.shape[1]), g.ptr,
+                                                    stream))
+
     # ---- mutation API -----------------------------------------------------------
 
     def assign(self, keys, values) -> None:

@@ -150,6 +150,16 @@ class DlrmWorkload:
         pooled = rng.standard_normal((self.batch * self.tables, self.dim), dtype=np.float32) * np.float32(self.sigma)
         return np.concatenate(keys), np.concatenate(bags), pooled
 
+    def make_bags(self, step: int):
+        """The same batch grouped by bag: (keys u64 [n] ordered by bag, each
+        bag's ids in draw order; offsets int64 [batch * tables + 1]; pooled
+        grads [batch * tables, dim] float32)."""
+        keys, bag, pooled = self.make_batch(step)
+        order = np.argsort(bag, kind="stable")
+        offsets = np.zeros(self.batch * self.tables + 1, dtype=np.int64)
+        offsets[1:] = np.cumsum(np.bincount(bag, minlength=self.batch * self.tables))
+        return keys[order], offsets, pooled
+
 
 @dataclass
 class CapacityWorkload:
