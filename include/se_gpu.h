@@ -151,6 +151,28 @@ int se_assign_dim(se_store *store, const void *keys, size_t num_keys, int64_t di
 int se_erase(se_store *store, const void *keys, size_t num_keys, void *stream);
 int se_erase_dimension(se_store *store, int64_t dim, const void *keys, size_t num_keys, void *stream);
 
+/* Checkpoint export (EmbeddingTableFacade::export_batch / export_opt_state_batch,
+ * embedding_table_interface.hpp:259-267, 293-298; hogwild_embedding_store.hpp:6112-6300):
+ * se_export_snapshot lists the present keys of the table of `dim` in
+ * directory order (replacing an earlier list of that table) and returns
+ * their number; se_export_read copies entries [offset, offset + count) of the
+ * list: keys (key dtype), parameter rows (ParamT, dim each), optimizer state
+ * rows (OptT, dim x states each: Adam m then v, Adagrad accumulator; none
+ * for SGD) and Adam steps. Any output may be null; outputs are host or
+ * device memory. The list reflects the table when it was taken; rows are
+ * read when se_export_read runs. */
+int se_export_snapshot(se_store *store, int64_t dim, uint64_t *num_keys_out, void *stream);
+int se_export_read(se_store *store, int64_t dim, uint64_t offset, uint64_t count, void *keys_out,
+                   void *values_out, void *opt_states_out, uint32_t *steps_out, void *stream);
+/* assign_opt_states (hogwild_embedding_store.hpp:6278-6351): sets the optimizer
+ * state rows (num_keys x dim x states values of OptT, laid out as exported)
+ * and, when steps is not null, the Adam steps of present keys. Every key
+ * must be present ("assign_opt_states key is absent from dimension table");
+ * nothing is written otherwise. */
+int se_assign_opt_states(se_store *store, int64_t dim, const void *keys, size_t num_keys,
+                         const void *opt_states, size_t num_state_values, const uint32_t *steps,
+                         void *stream);
+
 /* Embedding bag (no counterpart in the reference, whose DLRM users pool the
  * rows of lookup / lookup_or_insert themselves): sum pooling of multi-hot
  * bags. Bag b holds keys [offsets[b], offsets[b+1]) (int64 CSR offsets,

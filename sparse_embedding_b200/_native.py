@@ -84,6 +84,9 @@ _SIGNATURES = {
     "se_assign_dim": [_vp, _vp, _sz, _i64, _vp, _vp],
     "se_erase": [_vp, _vp, _sz, _vp],
     "se_embedding_bag": [_vp, _vp, _sz, _vp, _sz, _i64, _vp, _i32, _vp],
+    "se_export_snapshot": [_vp, _i64, C.POINTER(_u64), _vp],
+    "se_export_read": [_vp, _i64, _u64, _u64, _vp, _vp, _vp, _vp, _vp],
+    "se_assign_opt_states": [_vp, _i64, _vp, _sz, _vp, _sz, _vp, _vp],
     "se_embedding_bag_backward": [_vp, _vp, _sz, _vp, _sz, _i64, _vp, _vp],
     "se_erase_dimension": [_vp, _i64, _vp, _sz, _vp],
     "se_store_size": [_vp, C.POINTER(_u64)],

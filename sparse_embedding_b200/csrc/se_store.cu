@@ -10,6 +10,7 @@
 #include <cub/block/block_reduce.cuh>
 #include <cub/block/block_scan.cuh>
 #include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
 
 #include <algorithm>
 #include <cmath>
@@ -1098,6 +1099,102 @@ k_requeue_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t *_
 }
 
 // ---------------------------------------------------------------------------
+// Checkpoint interop: export of a table's present keys with their rows and
+// optimizer state (export_batch / export_opt_state_batch,
+// hogwild_embedding_store.hpp:6112-6300), assign_opt_states (6278-6351)
+// ---------------------------------------------------------------------------
+
+// 1 for each directory slot holding a present key (slot index nslots: the
+// all-ones key's side slot).
+__global__ void __launch_bounds__(256)
+k_export_flag(Dir d, uint64_t nslots, uint32_t *__restrict__ flags) {
+  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i > nslots) return;
+  uint32_t row;
+  if (i == nslots) {
+    row = d.special[1];
+  } else {
+    const Bucket &b = d.buckets[i / kBucketSlots];
+    row = b.keys[i % kBucketSlots] == kEmptyKey ? kNoRow : b.rows[i % kBucketSlots];
+  }
+  flags[i] = row < kDeadRow ? 1u : 0u;
+}
+
+__global__ void __launch_bounds__(256)
+k_export_list(Dir d, uint64_t nslots, const uint32_t *__restrict__ flags, const uint32_t *__restrict__ at,
+              unsigned long long *__restrict__ keys, uint32_t *__restrict__ rows) {
+  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i > nslots || !flags[i]) return;
+  const uint32_t j = at[i];
+  if (i == nslots) {
+    keys[j] = kEmptyKey;
+    rows[j] = d.special[1];
+  } else {
+    const Bucket &b = d.buckets[i / kBucketSlots];
+    keys[j] = b.keys[i % kBucketSlots];
+    rows[j] = b.rows[i % kBucketSlots];
+  }
+}
+
+// Entries [offset, offset + count) of a snapshot: key (narrowed to the key
+// dtype), parameter row, optimizer state rows (state0 then state1), step.
+template <int LANES>
+__global__ void __launch_bounds__(256)
+k_export_gather(Layout L, const uint8_t *__restrict__ slabs, const unsigned long long *__restrict__ keys,
+                const uint32_t *__restrict__ rows, uint64_t offset, uint64_t count, int kdt, void *keys_out,
+                uint8_t *__restrict__ values_out, uint8_t *__restrict__ states_out, uint32_t *__restrict__ steps_out) {
+  const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t j = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (j >= count) return;
+  const uint64_t key = keys[offset + j];
+  const uint8_t *slab = slabs + size_t(rows[offset + j]) * L.stride;
+  const uint32_t pb = L.pdt == SE_FLOAT32 ? 4 : 2, ob = L.odt == SE_FLOAT32 ? 4 : 2;
+  if (lane == 0 && keys_out) {
+    if (kdt <= SE_KEY_UINT32) static_cast<uint32_t *>(keys_out)[j] = uint32_t(key);
+    else static_cast<unsigned long long *>(keys_out)[j] = key;
+  }
+  if (values_out)
+    for (uint32_t b = lane; b < L.dim * pb; b += LANES) values_out[j * L.dim * pb + b] = slab[b];
+  if (states_out && L.nstate > 0) {
+    const uint32_t sb = L.dim * ob;
+    for (uint32_t b = lane; b < sb; b += LANES) {
+      states_out[j * L.nstate * sb + b] = slab[L.state0 + b];
+      if (L.nstate >= 2) states_out[j * L.nstate * sb + sb + b] = slab[L.state1 + b];
+    }
+  }
+  if (lane == 0 && steps_out) steps_out[j] = L.nstate >= 2 ? *reinterpret_cast<const uint32_t *>(slab + L.step) : 0u;
+}
+
+// assign_opt_states: first every key must be present (mark[0] counts the
+// absent ones); the write pass runs only when none is.
+__global__ void __launch_bounds__(256)
+k_opt_find(Dir d, const void *__restrict__ keys, int kdt, size_t n, uint32_t *__restrict__ rows, uint32_t *mark) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  rows[i] = row;
+  if (row == kNoRow) atomicAdd(mark, 1u);
+}
+
+template <int LANES>
+__global__ void __launch_bounds__(256)
+k_opt_assign(Layout L, uint8_t *__restrict__ slabs, const uint32_t *__restrict__ rows, size_t n,
+             const uint8_t *__restrict__ states, const uint32_t *__restrict__ steps, const uint32_t *mark) {
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t i = t / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  if (i >= n || *mark != 0u) return;
+  uint8_t *slab = slabs + size_t(rows[i]) * L.stride;
+  const uint32_t sb = L.dim * (L.odt == SE_FLOAT32 ? 4 : 2);
+  for (uint32_t b = lane; b < sb; b += LANES) {
+    slab[L.state0 + b] = states[i * L.nstate * sb + b];
+    if (L.nstate >= 2) slab[L.state1 + b] = states[i * L.nstate * sb + sb + b];
+  }
+  if (lane == 0 && steps && L.nstate >= 2) *reinterpret_cast<uint32_t *>(slab + L.step) = steps[i];
+}
+
+// ---------------------------------------------------------------------------
 // Embedding bag: sum-pooled gather of multi-hot bags and its backward
 // ---------------------------------------------------------------------------
 
@@ -1370,6 +1467,11 @@ struct Table {
   Scratch<uint32_t> g_seg_cnt, g_seg_off, g_seg_fill, g_pos, g_long, def_pos;
   Scratch<uint32_t> g_sort_kin, g_sort_kout, g_sort_vin;  // sorted placement of large windows
   Scratch<uint8_t> g_sort_tmp;
+  // checkpoint export snapshot: present keys and their rows, directory order
+  Scratch<unsigned long long> exp_keys;
+  Scratch<uint32_t> exp_rows;
+  uint64_t exp_count = 0;
+  bool exp_taken = false;
   Scratch<uint4> g_items;
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
@@ -1907,6 +2009,113 @@ struct StoreImpl {
       }
     }
     if (!is_device_ptr(keys)) cuda_check(cudaStreamSynchronize(st), "sync");
+  }
+
+  // ---- checkpoint interop ------------------------------------------------------
+  Scratch<uint32_t> exp_flags, exp_at;
+  Scratch<uint8_t> exp_tmp;
+
+  // export_batch / export_opt_state_batch (hogwild_embedding_store.hpp:6112-6300):
+  // lists the table's present keys; se_export_read copies slices of the list.
+  uint64_t export_snapshot(int64_t dim, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    Table &t = table(dim);
+    cudaStream_t st = pick(sp);
+    const uint64_t nslots = t.nbuckets * kBucketSlots;
+    if (nslots + 1 > 0x7fffffffull) throw Error(SE_ERR_NOT_IMPLEMENTED, "export of a directory above 2^31 slots");
+    const int m = int(nslots + 1);
+    uint32_t *flags = exp_flags.get(m), *at = exp_at.get(m);
+    size_t tmp_bytes = 0;
+    cuda_check(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, flags, at, m, st), "scan size");
+    uint8_t *tmp = exp_tmp.get(tmp_bytes);
+    k_export_flag<<<grid_for(uint64_t(m), 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), nslots, flags);
+    launched("k_export_flag");
+    cuda_check(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, flags, at, m, st), "scan");
+    uint32_t last[2];
+    cuda_check(cudaMemcpyAsync(&last[0], at + m - 1, 4, cudaMemcpyDeviceToHost, st), "read count");
+    cuda_check(cudaMemcpyAsync(&last[1], flags + m - 1, 4, cudaMemcpyDeviceToHost, st), "read count");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    const uint64_t total = uint64_t(last[0]) + last[1];
+    unsigned long long *keys = t.exp_keys.get(std::max<uint64_t>(total, 1));
+    uint32_t *rows = t.exp_rows.get(std::max<uint64_t>(total, 1));
+    k_export_list<<<grid_for(uint64_t(m), 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), nslots, flags, at, keys, rows);
+    launched("k_export_list");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    t.exp_count = total;
+    t.exp_taken = true;
+    return total;
+  }
+
+  void export_read(int64_t dim, uint64_t offset, uint64_t count, void *keys_out, void *values_out,
+                   void *states_out, uint32_t *steps_out, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    Table &t = table(dim);
+    if (!t.exp_taken) throw std::logic_error("se_export_read needs a snapshot (se_export_snapshot) of this table");
+    if (offset > t.exp_count || count > t.exp_count - offset)
+      throw std::invalid_argument("export slice is outside the snapshot");
+    if (count == 0) return;
+    cudaStream_t st = pick(sp);
+    const size_t kb = key_bytes(cfg.key_dtype), vb = value_bytes(cfg.value_dtype) * size_t(dim);
+    const size_t sb = value_bytes(cfg.optimizer_dtype) * size_t(dim) * t.L.nstate;
+    // outputs in host memory go through one device buffer, copied back below
+    struct Out { void *user; size_t bytes; size_t at; };
+    Out outs[4] = {{keys_out, kb * count, 0}, {values_out, vb * count, 0}, {t.L.nstate ? states_out : nullptr,
+                   sb * count, 0}, {steps_out, 4 * count, 0}};
+    size_t staged = 0;
+    for (auto &o : outs)
+      if (o.user && !is_device_ptr(o.user)) {
+        o.at = staged;
+        staged += (o.bytes + 255) & ~size_t(255);
+      }
+    uint8_t *buf = staged ? stage_vals.get(staged) : nullptr;
+    void *dev[4];
+    for (int i = 0; i < 4; ++i)
+      dev[i] = outs[i].user == nullptr ? nullptr : is_device_ptr(outs[i].user) ? outs[i].user : buf + outs[i].at;
+    k_export_gather<32><<<grid_for(count * 32, 256, 0x7fffffffu), 256, 0, st>>>(
+        t.L, t.slabs, t.exp_keys.ptr, t.exp_rows.ptr, offset, count, cfg.key_dtype, dev[0],
+        static_cast<uint8_t *>(dev[1]), static_cast<uint8_t *>(dev[2]), static_cast<uint32_t *>(dev[3]));
+    launched("k_export_gather");
+    for (int i = 0; i < 4; ++i)
+      if (outs[i].user && dev[i] != outs[i].user)
+        cuda_check(cudaMemcpyAsync(outs[i].user, dev[i], outs[i].bytes, cudaMemcpyDeviceToHost, st), "copy out");
+    if (staged) cuda_check(cudaStreamSynchronize(st), "sync");
+  }
+
+  // assign_opt_states (hogwild_embedding_store.hpp:6278-6351): all keys must be
+  // present; nothing is written otherwise.
+  void assign_opt_states(int64_t dim, const void *keys, size_t n, const void *states, size_t num_values,
+                         const uint32_t *steps, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (dim <= 0) throw std::invalid_argument("assign_opt_states dimension has no physical table");
+    Table *tp = nullptr;
+    for (auto &x : tables)
+      if (x->dim == dim) tp = x.get();
+    if (tp == nullptr) throw std::invalid_argument("assign_opt_states dimension has no physical table");
+    Table &t = *tp;
+    if (!cfg.enable_optimizer || cfg.optimizer_kind == SE_OPT_NONE)
+      throw std::invalid_argument("assign_opt_states dimension has no optimizer");
+    const size_t opt_dim = size_t(dim) * t.L.nstate;
+    if (opt_dim == 0 || num_values != n * opt_dim)
+      throw std::invalid_argument("assign_opt_states payload size does not match dimension");
+    if (n == 0) return;
+    cudaStream_t st = pick(sp);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const void *dstates = stage_in(stage_vals, states, num_values * value_bytes(cfg.optimizer_dtype), st);
+    const uint32_t *dsteps = steps ? static_cast<const uint32_t *>(stage_in(stage_offs, steps, n * 4, st)) : nullptr;
+    uint32_t *rows = bag_rows.get(n);
+    uint32_t *mark = dup_words.get(2);
+    cuda_check(cudaMemsetAsync(mark, 0, 4, st), "memset");
+    k_opt_find<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, rows, mark);
+    launched("k_opt_find");
+    k_opt_assign<32><<<grid_for(n * 32, 256, 0x7fffffffu), 256, 0, st>>>(
+        t.L, t.slabs, rows, n, static_cast<const uint8_t *>(dstates), dsteps, mark);
+    launched("k_opt_assign");
+    cuda_check(cudaMemcpyAsync(status_host, mark, 4, cudaMemcpyDeviceToHost, st), "read mark");
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    if (status_host[0] != 0u) throw std::invalid_argument("assign_opt_states key is absent from dimension table");
   }
 
   // ---- embedding bag ------------------------------------------------------------
@@ -2749,6 +2958,27 @@ int se_assign(se_store *store, const void *keys, size_t n, const void *values, s
     if (n == 0) return;
     if (num_values != n * size_t(d)) throw std::invalid_argument("values size does not match row lengths");
     checked(store)->impl.assign(keys, n, d, values, stream);
+  });
+}
+
+int se_export_snapshot(se_store *store, int64_t dim, uint64_t *num_keys_out, void *stream) {
+  return guarded([&] {
+    if (num_keys_out == nullptr) throw std::invalid_argument("num_keys_out is null");
+    *num_keys_out = checked(store)->impl.export_snapshot(dim, stream);
+  });
+}
+
+int se_export_read(se_store *store, int64_t dim, uint64_t offset, uint64_t count, void *keys_out, void *values_out,
+                   void *opt_states_out, uint32_t *steps_out, void *stream) {
+  return guarded([&] {
+    checked(store)->impl.export_read(dim, offset, count, keys_out, values_out, opt_states_out, steps_out, stream);
+  });
+}
+
+int se_assign_opt_states(se_store *store, int64_t dim, const void *keys, size_t n, const void *opt_states,
+                         size_t num_state_values, const uint32_t *steps, void *stream) {
+  return guarded([&] {
+    checked(store)->impl.assign_opt_states(dim, keys, n, opt_states, num_state_values, steps, stream);
   });
 }
 
