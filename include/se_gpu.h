@@ -44,6 +44,16 @@ enum se_key_dtype { SE_KEY_INT32 = 0, SE_KEY_UINT32 = 1, SE_KEY_INT64 = 2, SE_KE
 enum se_value_dtype { SE_FLOAT32 = 0, SE_FLOAT16 = 1, SE_BFLOAT16 = 2 };
 enum se_optimizer_kind { SE_OPT_NONE = 0, SE_OPT_SGD = 1, SE_OPT_ADAM = 2, SE_OPT_ADAGRAD = 3 };
 enum se_init_kind { SE_INIT_ZEROS = 0, SE_INIT_UNIFORM = 1 };
+/* Score policies (ScorePolicyKind, sparse_embedding/src/eviction/score_policy.hpp:37):
+ * LFU counts lookups of a key, LRU stamps it with a store-wide access clock,
+ * manual scores change only through se_assign_scores. */
+enum se_score_policy { SE_SCORE_NONE = 0, SE_SCORE_LFU = 1, SE_SCORE_LRU = 2, SE_SCORE_MANUAL = 3 };
+/* Dynamic learning-rate policies (sparse_embedding/src/optimizer/dynamic_lr_policy.hpp:32-124):
+ * the row's learning rate as a function of its score. */
+enum se_lr_policy {
+  SE_LR_CONSTANT = 0, SE_LR_SQRT_DECAY = 1, SE_LR_LOG_DECAY = 2, SE_LR_INVERSE_DECAY = 3,
+  SE_LR_COSINE_FREQUENCY = 4, SE_LR_CUSTOM_LUT = 5
+};
 /* Registered partitioners: sparse_embedding.{modulo,hash,fast_range}. */
 enum se_partitioner_kind { SE_PART_MODULO = 0, SE_PART_HASH = 1, SE_PART_FAST_RANGE = 2 };
 
@@ -71,6 +81,12 @@ typedef struct se_store_config {
   int32_t device;            /* CUDA device ordinal                                */
   int32_t simd_width;        /* float lanes of the mirrored CPU build: 16 or 8     */
   int32_t internal_shards;   /* value reported by se_store_internal_shard_count    */
+  int32_t score_policy;      /* enum se_score_policy                               */
+  int32_t lr_policy;         /* enum se_lr_policy (needs a score policy unless constant) */
+  float lr_min_ratio;        /* cosine: learning rate at max_score, as a ratio     */
+  uint64_t lr_max_score;     /* cosine: score where the decay ends                 */
+  const float *lr_lut;       /* custom LUT: multiplier per score (last one beyond) */
+  size_t lr_lut_len;
 } se_store_config;
 
 typedef struct se_store se_store;
@@ -190,6 +206,13 @@ int se_embedding_bag(se_store *store, const void *keys, size_t num_keys, const i
  * without building the repeated rows. */
 int se_embedding_bag_backward(se_store *store, const void *keys, size_t num_keys, const int64_t *offsets,
                               size_t num_bags, int64_t dim, const void *pooled_grads, void *stream);
+
+/* assign_scores (hogwild_embedding_store.hpp:5202-5250): each key's score is
+ * set in the first table that holds it; absent keys are skipped. Needs a
+ * score policy. se_read_scores reads them back (0 for absent keys). */
+int se_assign_scores(se_store *store, const void *keys, size_t num_keys, const uint64_t *scores,
+                     void *stream);
+int se_read_scores(se_store *store, const void *keys, size_t num_keys, uint64_t *scores_out, void *stream);
 
 /* Metadata conventions (embedding_table_interface.hpp:317-396). */
 int se_store_size(se_store *store, uint64_t *out_size);

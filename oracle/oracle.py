@@ -66,6 +66,7 @@ def lib():
         L.or_store_create.argtypes = (
             [_vp, _c.c_size_t] + [_c.c_int] * 4 + [_c.c_float, _c.c_int, _c.c_int, _c.c_float, _c.c_float, _c.c_int]
             + [_c.c_float] * 6 + [_c.c_int, _c.c_int]
+            + [_c.c_int, _c.c_int, _c.c_float, _c.c_uint64, _vp, _c.c_size_t]
         )
         L.or_store_destroy.argtypes = [_vp]
         L.or_store_reserve.argtypes = [_vp, _c.c_int64, _c.c_size_t]
@@ -81,6 +82,8 @@ def lib():
         L.or_contains.argtypes = [_vp, _vp, _c.c_size_t, _vp]
         L.or_assign.argtypes = [_vp, _vp, _c.c_size_t, _c.c_int64, _vp]
         L.or_erase.argtypes = [_vp, _vp, _c.c_size_t, _c.c_int64]
+        L.or_assign_scores.argtypes = [_vp, _vp, _c.c_size_t, _vp]
+        L.or_read_scores.argtypes = [_vp, _vp, _c.c_size_t, _vp]
         _lib = L
     return _lib
 
@@ -208,6 +211,11 @@ class OracleStore:
         initial_accumulator=0.0,
         simd_width=16,
         threads=1,
+        score_policy="none",
+        lr_policy="constant",
+        lr_min_ratio=0.1,
+        lr_max_score=1024,
+        lr_lut=(),
     ):
         self.key_dtype = np.dtype(key_dtype)
         self.value_dtype = value_dtype
@@ -215,12 +223,16 @@ class OracleStore:
         self.gradient_dtype = gradient_dtype or value_dtype
         d = np.asarray(dims, dtype=np.int64)
         self._dims = d
+        self._lut = np.asarray(lr_lut, dtype=np.float32)
         self._h = lib().or_store_create(
             _ptr(d), len(d), KEY_CODES[self.key_dtype.name], VALUE_CODES[value_dtype],
             VALUE_CODES[self.optimizer_dtype], VALUE_CODES[self.gradient_dtype], gradient_scale,
             int(enable_optimizer), INIT_CODES[init], init_min, init_max,
             OPT_CODES[optimizer if enable_optimizer else "none"], lr, beta1, beta2, eps, weight_decay,
             initial_accumulator, simd_width, threads,
+            {"none": 0, "lfu": 1, "lru": 2, "manual": 3}[score_policy],
+            {"constant": 0, "sqrt": 1, "log": 2, "inverse": 3, "cosine": 4, "lut": 5}[lr_policy],
+            lr_min_ratio, lr_max_score, _ptr(self._lut) if len(self._lut) else None, len(self._lut),
         )
 
     def __del__(self):
@@ -271,6 +283,17 @@ class OracleStore:
     def erase(self, keys, dim=0):
         keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
         _check(lib().or_erase(self._h, _ptr(keys), len(keys), dim))
+
+    def assign_scores(self, keys, scores):
+        keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
+        scores = np.ascontiguousarray(scores, dtype=np.uint64)
+        lib().or_assign_scores(self._h, _ptr(keys), len(keys), _ptr(scores))
+
+    def read_scores(self, keys):
+        keys = np.ascontiguousarray(keys, dtype=self.key_dtype)
+        out = np.zeros(len(keys), dtype=np.uint64)
+        lib().or_read_scores(self._h, _ptr(keys), len(keys), _ptr(out))
+        return out
 
     def size(self, dim=0) -> int:
         return int(lib().or_store_size(self._h, dim))

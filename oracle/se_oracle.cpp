@@ -353,7 +353,31 @@ struct Config {
   float lr, beta1, beta2, eps, weight_decay, initial_accumulator;
   int simd_width;
   int threads;
+  // scores and dynamic learning rates (score_policy.hpp:37; dynamic_lr_policy.hpp:32-124)
+  int score_policy;          // 0 none, 1 lfu, 2 lru, 3 manual
+  int lr_policy;             // 0 constant, 1 sqrt, 2 log, 3 inverse, 4 cosine, 5 custom LUT
+  float lr_min_ratio;
+  uint64_t lr_max_score;
+  std::vector<float> lut;    // cosine table or custom LUT
 };
+
+// compute_lr of the reference's policies (dynamic_lr_policy.hpp:32-110). The
+// reference's compiled cosine step fuses (base - min) * lut + min.
+inline float policy_lr(const Config &c, uint64_t score) {
+  const float base = c.lr;
+  switch (c.lr_policy) {
+  case 1: return score == 0 ? base : base / std::sqrt(static_cast<float>(score));
+  case 2: return base / std::log2(2.0f + static_cast<float>(score));
+  case 3: return score == 0 ? base : base / static_cast<float>(score);
+  case 4: {
+    const float min_lr = base * c.lr_min_ratio;
+    if (score >= c.lr_max_score) return min_lr;
+    return std::fma(base - min_lr, c.lut[size_t(score)], min_lr);
+  }
+  case 5: return base * c.lut[size_t(score >= c.lr_max_score ? c.lr_max_score : score)];
+  default: return base;
+  }
+}
 
 struct TableBase {
   virtual ~TableBase() = default;
@@ -368,6 +392,9 @@ struct TableBase {
   virtual void contains(const void *keys, size_t n, uint8_t *out) const = 0;
   virtual void assign(const void *keys, size_t n, const void *values) = 0;
   virtual void erase(const void *keys, size_t n) = 0;
+  virtual void touch(const void *keys, size_t n, uint64_t *clock) = 0;
+  virtual bool set_score(uint64_t key, uint64_t score) = 0;
+  virtual bool get_score(uint64_t key, uint64_t *score) const = 0;
 };
 
 template <class F> void parallel_for(size_t n, int threads, F &&f) {
@@ -389,6 +416,7 @@ template <class P, class O, class G> struct Table final : TableBase {
   std::vector<P> params;
   std::vector<O> s0, s1;    // Adam m, v  |  Adagrad acc (s0)
   std::vector<uint32_t> steps;
+  std::vector<uint64_t> scores;  // per row, 0 at creation
   std::vector<float> bc1, bc2;
   // Transient accumulation (TransientArena), one shard per worker thread,
   // a key's shard = splitmix64(key) % shards: key -> slot, sums kept in G.
@@ -431,6 +459,7 @@ template <class P, class O, class G> struct Table final : TableBase {
     }
     if (ns >= 2) s1.resize(s1.size() + d, from_f32<O>(0.0f));
     if (cfg.enable_optimizer && cfg.optimizer_kind == kOptAdam) steps.push_back(0);
+    scores.push_back(0);
     return row;
   }
 
@@ -545,16 +574,17 @@ template <class P, class O, class G> struct Table final : TableBase {
         P *p = params.data() + size_t(row) * d;
         switch (cfg.optimizer_kind) {
         case kOptSgd:
-          sgd_row<P>(p, gbuf.data(), cfg.lr, cfg.weight_decay, d, simd_cut);
+          sgd_row<P>(p, gbuf.data(), policy_lr(cfg, scores[row]), cfg.weight_decay, d, simd_cut);
           break;
         case kOptAdagrad:
-          adagrad_row<P, O>(p, gbuf.data(), s0.data() + size_t(row) * d, cfg.lr, cfg.eps,
+          adagrad_row<P, O>(p, gbuf.data(), s0.data() + size_t(row) * d, policy_lr(cfg, scores[row]), cfg.eps,
                             cfg.weight_decay, d);
           break;
         case kOptAdam: {
           uint32_t t = ++steps[row];
           adam_row<P, O>(p, gbuf.data(), s0.data() + size_t(row) * d, s1.data() + size_t(row) * d,
-                         cfg.lr, cfg.beta1, cfg.beta2, cfg.eps, bc1[t], bc2[t], cfg.weight_decay, d,
+                         policy_lr(cfg, scores[row]), cfg.beta1, cfg.beta2, cfg.eps, bc1[t], bc2[t],
+                         cfg.weight_decay, d,
                          simd_cut);
           break;
         }
@@ -611,6 +641,34 @@ template <class P, class O, class G> struct Table final : TableBase {
     }
   }
 
+  // ScorePolicyRuntime::on_access (score_policy.hpp:40-100) for every key a
+  // lookup finds, in batch order: LFU counts, LRU stamps with the store's clock.
+  void touch(const void *keys, size_t n, uint64_t *clock) override {
+    if (cfg.score_policy != 1 && cfg.score_policy != 2) return;
+    for (size_t i = 0; i < n; ++i) {
+      uint32_t row;
+      if (!map.find(key_at(cfg.key_dtype, keys, i), &row)) continue;
+      if (cfg.score_policy == 1) {
+        if (scores[row] != ~0ull) ++scores[row];
+      } else {
+        const uint64_t ts = (*clock)++;
+        if (scores[row] < ts) scores[row] = ts;
+      }
+    }
+  }
+  bool set_score(uint64_t key, uint64_t score) override {
+    uint32_t row;
+    if (!map.find(key, &row)) return false;
+    scores[row] = score;
+    return true;
+  }
+  bool get_score(uint64_t key, uint64_t *score) const override {
+    uint32_t row;
+    if (!map.find(key, &row)) return false;
+    *score = scores[row];
+    return true;
+  }
+
   // erase: hogwild_embedding_store.hpp:5011-5062 (absent keys are ignored).
   // Pending gradients stay keyed; optimizer_step resolves them then.
   void erase(const void *keys, size_t n) override {
@@ -659,6 +717,7 @@ struct Store {
   Config cfg;
   std::vector<TableBase *> tables;
   uint64_t dropped = 0;
+  uint64_t lru_clock = 1;  // the reference's clock starts at 1
   ~Store() { for (auto *t : tables) delete t; }
   TableBase *table(int64_t dim) {
     for (auto *t : tables) if (t->dim() == dim) return t;
@@ -726,11 +785,26 @@ void *or_store_create(const int64_t *dims, size_t ndims, int key_dtype, int valu
                       int optimizer_dtype, int gradient_dtype, float gradient_scale,
                       int enable_optimizer, int init_kind, float init_min, float init_max,
                       int optimizer_kind, float lr, float beta1, float beta2, float eps,
-                      float weight_decay, float initial_accumulator, int simd_width, int threads) {
+                      float weight_decay, float initial_accumulator, int simd_width, int threads,
+                      int score_policy, int lr_policy, float lr_min_ratio, uint64_t lr_max_score,
+                      const float *lut, size_t lut_len) {
   Store *s = new Store();
   s->cfg = Config{key_dtype, value_dtype, optimizer_dtype, gradient_dtype, gradient_scale,
                   enable_optimizer, init_kind, init_min, init_max, optimizer_kind, lr, beta1,
-                  beta2, eps, weight_decay, initial_accumulator, simd_width, threads};
+                  beta2, eps, weight_decay, initial_accumulator, simd_width, threads,
+                  score_policy, lr_policy, lr_min_ratio, lr_max_score, {}};
+  if (lr_policy == 4) {
+    // CosineFrequencyLrPolicy's table (dynamic_lr_policy.hpp:70-80)
+    s->cfg.lut.resize(size_t(lr_max_score) + 1);
+    const float pi = static_cast<float>(3.14159265358979323846);
+    for (uint64_t i = 0; i <= lr_max_score; ++i) {
+      const float ratio = static_cast<float>(i) / static_cast<float>(lr_max_score);
+      s->cfg.lut[size_t(i)] = (1.0f + std::cos(pi * ratio)) / 2.0f;
+    }
+  } else if (lr_policy == 5) {
+    s->cfg.lut.assign(lut, lut + lut_len);
+    s->cfg.lr_max_score = lut_len - 1;
+  }
   for (size_t i = 0; i < ndims; ++i) {
     bool dup = false;
     for (auto *t : s->tables) dup |= t->dim() == dims[i];
@@ -753,6 +827,7 @@ int or_lookup(void *h, const void *keys, size_t n, int64_t dim, void *out) {
   auto *t = s->table(dim);
   if (!t) return -2;
   t->lookup(keys, n, out, s->cfg.threads);
+  t->touch(keys, n, &s->lru_clock);
   return 0;
 }
 
@@ -786,6 +861,26 @@ uint64_t or_store_size(void *h, int64_t dim) {
 }
 
 uint64_t or_store_dropped(void *h) { return static_cast<Store *>(h)->dropped; }
+
+// assign_scores (hogwild_embedding_store.hpp:5202-5250): first table holding the key.
+void or_assign_scores(void *h, const void *keys, size_t n, const uint64_t *scores) {
+  Store *s = static_cast<Store *>(h);
+  for (size_t i = 0; i < n; ++i) {
+    const uint64_t key = key_at(s->cfg.key_dtype, keys, i);
+    for (auto *t : s->tables)
+      if (t->set_score(key, scores[i])) break;
+  }
+}
+
+void or_read_scores(void *h, const void *keys, size_t n, uint64_t *out) {
+  Store *s = static_cast<Store *>(h);
+  for (size_t i = 0; i < n; ++i) {
+    out[i] = 0;
+    const uint64_t key = key_at(s->cfg.key_dtype, keys, i);
+    for (auto *t : s->tables)
+      if (t->get_score(key, &out[i])) break;
+  }
+}
 
 void or_contains(void *h, const void *keys, size_t n, uint8_t *out) {
   Store *s = static_cast<Store *>(h);

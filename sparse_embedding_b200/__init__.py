@@ -33,6 +33,13 @@ from .store import (
     Adagrad,
     Adam,
     AutoStorage,
+    ConstantLrPolicy,
+    CosineFrequencyLrPolicy,
+    CustomLutLrPolicy,
+    InverseDecayLrPolicy,
+    LogDecayLrPolicy,
+    LrPolicy,
+    SqrtDecayLrPolicy,
     EmbeddingConfig,
     EmbeddingStore,
     Initializer,

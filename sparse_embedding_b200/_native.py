@@ -55,6 +55,12 @@ class StoreConfig(C.Structure):
         ("device", C.c_int32),
         ("simd_width", C.c_int32),
         ("internal_shards", C.c_int32),
+        ("score_policy", C.c_int32),
+        ("lr_policy", C.c_int32),
+        ("lr_min_ratio", C.c_float),
+        ("lr_max_score", C.c_uint64),
+        ("lr_lut", C.POINTER(C.c_float)),
+        ("lr_lut_len", C.c_size_t),
     ]
 
 
@@ -84,6 +90,8 @@ _SIGNATURES = {
     "se_assign_dim": [_vp, _vp, _sz, _i64, _vp, _vp],
     "se_erase": [_vp, _vp, _sz, _vp],
     "se_embedding_bag": [_vp, _vp, _sz, _vp, _sz, _i64, _vp, _i32, _vp],
+    "se_assign_scores": [_vp, _vp, _sz, _vp, _vp],
+    "se_read_scores": [_vp, _vp, _sz, _vp, _vp],
     "se_export_snapshot": [_vp, _i64, C.POINTER(_u64), _vp],
     "se_export_read": [_vp, _i64, _u64, _u64, _vp, _vp, _vp, _vp, _vp],
     "se_assign_opt_states": [_vp, _i64, _vp, _sz, _vp, _sz, _vp, _vp],

@@ -135,6 +135,7 @@ __device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const 
     }
   }
   if (L.nstate >= 2 && lane == 0) *reinterpret_cast<uint32_t *>(slab + L.step) = 0u;
+  if (L.score != 0u && lane == 0) *reinterpret_cast<unsigned long long *>(slab + L.score) = 0ull;  // a new row's score
 }
 
 // lookup_or_insert (hogwild_embedding_store.hpp:4925-4980 ->
@@ -363,7 +364,30 @@ struct OptSpec {
   float factor;        // gradient_scale / normalization_steps
   int raw;             // gradient used as stored (GradT == ParamT, factor 1)
   const uint32_t *poison;  // nonzero: the window holds a batch that failed validation
+  // dynamic learning rate (dynamic_lr_policy.hpp:32-124): the row's lr from its score
+  int lr_kind;             // enum se_lr_policy; SE_LR_CONSTANT: lr for every row
+  float lr_min_ratio;
+  unsigned long long lr_max_score;
+  const float *lr_lut;     // cosine multipliers [0, max_score], or the custom LUT
 };
+
+// Learning rate of a row with score `sc` (the reference's compute_lr, with
+// its compiled fused multiply-add in the cosine policy).
+__device__ __forceinline__ float row_lr(const OptSpec &o, unsigned long long sc) {
+  const float base = o.lr;
+  switch (o.lr_kind) {
+  case SE_LR_SQRT_DECAY: return sc == 0ull ? base : __fdiv_rn(base, __fsqrt_rn(__ull2float_rn(sc)));
+  case SE_LR_LOG_DECAY: return __fdiv_rn(base, log2f(__fadd_rn(2.0f, __ull2float_rn(sc))));
+  case SE_LR_INVERSE_DECAY: return sc == 0ull ? base : __fdiv_rn(base, __ull2float_rn(sc));
+  case SE_LR_COSINE_FREQUENCY: {
+    const float min_lr = __fmul_rn(base, o.lr_min_ratio);
+    if (sc >= o.lr_max_score) return min_lr;
+    return __fmaf_rn(__fsub_rn(base, min_lr), o.lr_lut[sc], min_lr);
+  }
+  case SE_LR_CUSTOM_LUT: return __fmul_rn(base, o.lr_lut[sc >= o.lr_max_score ? o.lr_max_score : sc]);
+  default: return base;
+  }
+}
 
 // Applies the optimizer to VEC elements [e, e+VEC) of one row, given the
 // reduced gradient in the gradient dtype's precision.
@@ -386,11 +410,15 @@ __device__ __forceinline__ void load_state(const Layout &L, const uint8_t *slab,
   if (o.kind == SE_OPT_ADAM) ldv<VEC>(slab + L.state1, L.odt, e, r.s1);
 }
 
-template <int VEC>
+// kDyn: the store has a dynamic learning-rate policy (the row's lr from its
+// score); a separate instantiation keeps the constant-lr kernels unchanged.
+template <int VEC, bool kDyn = false>
 __device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, const OptSpec &o, uint32_t t,
                                              uint32_t e, const float (&gsum)[VEC], RowState<VEC> &r) {
   float g[VEC];
   float (&p)[VEC] = r.p;
+  float lr = o.lr;
+  if constexpr (kDyn) lr = row_lr(o, *reinterpret_cast<const unsigned long long *>(slab + L.score));
   // GradientBatchView::assign (gradient_accumulator.hpp:38-53): g * scale / N -> ParamT.
 #pragma unroll
   for (int j = 0; j < VEC; ++j) g[j] = o.raw ? gsum[j] : round_to(L.pdt, __fmul_rn(gsum[j], o.factor));
@@ -398,7 +426,7 @@ __device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, con
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       const float gg = __fmaf_rn(o.wd, p[j], g[j]);
-      p[j] = __fmaf_rn(-o.lr, gg, p[j]);
+      p[j] = __fmaf_rn(-lr, gg, p[j]);
     }
   } else if (o.kind == SE_OPT_ADAGRAD) {
     float (&a)[VEC] = r.s0;
@@ -408,7 +436,7 @@ __device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, con
       if (o.wd > 0.0f) gg = __fmaf_rn(o.wd, p[j], gg);
       a[j] = __fmaf_rn(gg, gg, a[j]);
       const float denom = __fadd_rn(__fsqrt_rn(a[j]), o.eps);
-      p[j] = __fmaf_rn(-o.lr, __fdiv_rn(gg, denom), p[j]);
+      p[j] = __fmaf_rn(-lr, __fdiv_rn(gg, denom), p[j]);
     }
     stv<VEC>(slab + L.state0, L.odt, e, a);
   } else if (o.kind == SE_OPT_ADAM) {
@@ -430,8 +458,8 @@ __device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, con
       const float m_hat = __fmul_rn(mi, bc1);
       const float v_hat = __fmul_rn(vi, bc2);
       const float denom = __fadd_rn(__fsqrt_rn(v_hat), o.eps);
-      if (vec_body) p[j] = __fmaf_rn(-o.lr, __fdiv_rn(m_hat, denom), p[j]);
-      else p[j] = __fsub_rn(p[j], __fdiv_rn(__fmul_rn(o.lr, m_hat), denom));
+      if (vec_body) p[j] = __fmaf_rn(-lr, __fdiv_rn(m_hat, denom), p[j]);
+      else p[j] = __fsub_rn(p[j], __fdiv_rn(__fmul_rn(lr, m_hat), denom));
     }
     stv<VEC>(slab + L.state0, L.odt, e, ms);
     stv<VEC>(slab + L.state1, L.odt, e, vs);
@@ -439,12 +467,12 @@ __device__ __forceinline__ void apply_loaded(const Layout &L, uint8_t *slab, con
   stv<VEC>(slab, L.pdt, e, p);
 }
 
-template <int VEC>
+template <int VEC, bool kDyn = false>
 __device__ __forceinline__ void apply_chunk(const Layout &L, uint8_t *slab, const OptSpec &o,
                                             uint32_t t, uint32_t e, const float (&gsum)[VEC]) {
   RowState<VEC> r;
   load_state<VEC>(L, slab, o, e, r);
-  apply_loaded<VEC>(L, slab, o, t, e, gsum, r);
+  apply_loaded<VEC, kDyn>(L, slab, o, t, e, gsum, r);
 }
 
 // Adds the gradient rows spos[k0..k1) (in order) into acc, rounding to the
@@ -639,7 +667,7 @@ __device__ __forceinline__ uint32_t next_step(const Layout &L, uint8_t *slab) {
 // the row's parameters and state before the sum so both latencies overlap.
 constexpr int kApplySlots = 4;
 
-template <int LANES, int VEC, int SLOTS, int AHEAD>
+template <int LANES, int VEC, int SLOTS, int AHEAD, bool kDyn>
 __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, const OptSpec &o, int gdt,
                                               const void *pgrads, const GroupWs &w, uint32_t s, uint32_t cnt,
                                               uint32_t off, uint32_t row, uint32_t lane, unsigned mask,
@@ -680,8 +708,8 @@ __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, c
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc[j] = 0.0f;
     sum_rows<VEC, AHEAD>(pgrads, gdt, L.dim, ord, 0, cnt, e, acc);
-    if (e == e0) apply_loaded<VEC>(L, slab, o, step, e, acc, rs);
-    else apply_chunk<VEC>(L, slab, o, step, e, acc);
+    if (e == e0) apply_loaded<VEC, kDyn>(L, slab, o, step, e, acc, rs);
+    else apply_chunk<VEC, kDyn>(L, slab, o, step, e, acc);
   }
   __syncwarp(mask);
 }
@@ -691,7 +719,7 @@ __device__ __forceinline__ void group_segment(const Layout &L, uint8_t *slabs, c
 // become the block work items of k_group_hot. (Tried and slower: the long
 // segments in a concurrent kernel of their own, and half the lanes per
 // segment.)
-template <int LANES, int VEC>
+template <int LANES, int VEC, bool kDyn>
 __global__ void __launch_bounds__(256, 3)
 k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
               GroupWs w, const uint32_t *count_p) {
@@ -715,7 +743,7 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
       const uint32_t s = w.long_list[j];
       const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
       if (!poisoned)
-        group_segment<LANES, VEC, kApplySlots, 4>(L, slabs, o, gdt, pgrads, w, s, cnt, off, row, lane, mask,
+        group_segment<LANES, VEC, kApplySlots, 4, kDyn>(L, slabs, o, gdt, pgrads, w, s, cnt, off, row, lane, mask,
                                                   s_ord[gib]);
       if (lane == 0) {
         w.row_cnt[row] = 0u;
@@ -729,7 +757,7 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
     const uint32_t cnt = w.seg_cnt[s], off = w.seg_off[s], row = w.seg_row[s];
     if (cnt > w.short_max) continue;  // a long segment or one of k_group_hot's
     if (cnt > 0 && !poisoned)
-      group_segment<LANES, VEC, 1, 4>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
+      group_segment<LANES, VEC, 1, 4, kDyn>(L, slabs, o, gdt, pgrads, w, uint32_t(s), cnt, off, row, lane, mask,
                                       s_ord[gib]);
     if (lane == 0) {
       w.row_cnt[row] = 0u;
@@ -758,7 +786,7 @@ k_group_apply(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const v
 // summed serially (the reference's order); larger ones in runs of
 // 1024/LANES groups whose sums are added by a fixed pairwise tree. Everything
 // is fixed by the shapes, so results are deterministic.
-template <int LANES, int VEC>
+template <int LANES, int VEC, bool kDyn>
 __global__ void __launch_bounds__(kBlockThreads)
 k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const void *__restrict__ pgrads,
             GroupWs w, const uint32_t *count_p) {
@@ -874,7 +902,7 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
       }
       if (grp == 0 && e < L.dim) {
         if (nparts == 1) {
-          if (!poisoned) apply_chunk<VEC>(L, slab, o, s_step, e, acc);
+          if (!poisoned) apply_chunk<VEC, kDyn>(L, slab, o, s_step, e, acc);
         } else {
           float *dst = w.partials + size_t(first + q) * L.dim;
 #pragma unroll
@@ -904,7 +932,7 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
 #pragma unroll
             for (int j = 0; j < VEC; ++j) tot[j] = round_to(gdt, __fadd_rn(tot[j], __ldcg(src + j)));
           }
-          apply_chunk<VEC>(L, slab, o, s_step, e, tot);
+          apply_chunk<VEC, kDyn>(L, slab, o, s_step, e, tot);
         }
       }
     }
@@ -959,6 +987,7 @@ __device__ __forceinline__ void init_state(const Layout &L, uint8_t *slab, const
     }
   }
   if (L.nstate >= 2 && lane == 0) *reinterpret_cast<uint32_t *>(slab + L.step) = 0u;
+  if (L.score != 0u && lane == 0) *reinterpret_cast<unsigned long long *>(slab + L.score) = 0ull;
 }
 
 // validate_unique_mutation_batch (hogwild_embedding_store.hpp:5278-5305) on
@@ -1096,6 +1125,71 @@ k_requeue_count(Dir d, const unsigned long long *__restrict__ pkeys, uint32_t *_
     if (valid) prows[i] = row;
     count_entries(c, valid, row, i);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Scores (ScorePolicyRuntime::on_access, eviction/score_policy.hpp:40-100, as
+// forward_lookup applies it to every key it finds, hogwild_embedding_store.hpp:4479-4490)
+// ---------------------------------------------------------------------------
+
+// LFU: one more access for every position whose key is present.
+__global__ void __launch_bounds__(256)
+k_touch_lfu(Dir d, Layout L, uint8_t *__restrict__ slabs, const void *__restrict__ keys, int kdt, size_t n) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  if (row != kNoRow) atomicAdd(reinterpret_cast<unsigned long long *>(slabs + size_t(row) * L.stride + L.score), 1ull);
+}
+
+// LRU, first pass: rows and hit flags of the batch's positions.
+__global__ void __launch_bounds__(256)
+k_touch_find(Dir d, const void *__restrict__ keys, int kdt, size_t n, uint32_t *__restrict__ rows,
+             uint32_t *__restrict__ hits) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  rows[i] = row;
+  hits[i] = row != kNoRow ? 1u : 0u;
+}
+
+// LRU, second pass: the h-th hit of the batch (in position order) takes the
+// clock's value + h, and the row keeps the latest stamp; the clock advances
+// by the batch's hits, as one access at a time would advance it.
+__global__ void __launch_bounds__(256)
+k_touch_lru(Layout L, uint8_t *__restrict__ slabs, const uint32_t *__restrict__ rows, const uint32_t *__restrict__ hits,
+            const uint32_t *__restrict__ rank, size_t n, unsigned long long *clock) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const unsigned long long now = *clock;
+  if (hits[i])
+    atomicMax(reinterpret_cast<unsigned long long *>(slabs + size_t(rows[i]) * L.stride + L.score), now + rank[i]);
+  // the advanced clock goes to clock[1] (other blocks may still read
+  // clock[0]); the host moves it into clock[0] after the launch
+  if (i == n - 1) clock[1] = now + rank[i] + hits[i];
+}
+
+// assign_scores: the first table holding a key takes its score (`done` marks
+// keys already placed by an earlier table).
+__global__ void __launch_bounds__(256)
+k_assign_scores(Dir d, Layout L, uint8_t *__restrict__ slabs, const void *__restrict__ keys, int kdt, size_t n,
+                const unsigned long long *__restrict__ scores, uint8_t *__restrict__ done) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n || done[i]) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  if (row == kNoRow) return;
+  *reinterpret_cast<unsigned long long *>(slabs + size_t(row) * L.stride + L.score) = scores[i];
+  done[i] = 1;
+}
+
+__global__ void __launch_bounds__(256)
+k_read_scores(Dir d, Layout L, const uint8_t *__restrict__ slabs, const void *__restrict__ keys, int kdt, size_t n,
+              unsigned long long *__restrict__ out, uint8_t *__restrict__ done) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n || done[i]) return;
+  const uint32_t row = dir_find<false>(d, load_key(keys, kdt, i));
+  if (row == kNoRow) return;
+  out[i] = *reinterpret_cast<const unsigned long long *>(slabs + size_t(row) * L.stride + L.score);
+  done[i] = 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -1523,6 +1617,11 @@ struct StoreImpl {
   Scratch<unsigned long long> dup_set;  // assign's repeated-key check
   Scratch<uint32_t> dup_words;
   Scratch<uint8_t> stage_offs;             // embedding-bag offsets staged from the host
+  // scores and dynamic learning rates
+  float *lr_lut = nullptr;                 // cosine multipliers or the custom LUT, on the device
+  uint64_t lr_max = 0;                     // cosine max_score / custom LUT's last index
+  unsigned long long *lru_clock = nullptr; // [0] the LRU access clock, [1] its next value
+  Scratch<uint8_t> score_done;
   Scratch<uint32_t> bag_rows, bag_of_buf;  // rows of a bag batch's keys; bag of each key
   bool profiling = false;
   std::vector<ProfRec> prof;
@@ -1532,6 +1631,8 @@ struct StoreImpl {
     if (own) cudaStreamSynchronize(own);
     tables.clear();
     dfree(bc);
+    dfree(lr_lut);
+    dfree(lru_clock);
     if (status_host) cudaFreeHost(status_host);
     if (u64_host) cudaFreeHost(u64_host);
     for (auto &r : prof) {
@@ -1606,6 +1707,11 @@ struct StoreImpl {
     t.L.state1 = t.L.state0 + (nstate >= 1 ? up16(ob) : 0u);
     t.L.step = t.L.state1 + (nstate >= 2 ? up16(ob) : 0u);
     t.L.stride = t.L.step + (nstate >= 2 ? 16u : 0u);
+    t.L.score = 0u;
+    if (cfg.score_policy != SE_SCORE_NONE) {  // a u64 score after the optimizer state
+      t.L.score = t.L.stride;
+      t.L.stride += 16u;
+    }
     t.vec = dim % 4 == 0 ? 4 : 1;
     t.lanes = pick_lanes(uint64_t(dim) / uint64_t(t.vec));
     t.ctr = dalloc<uint32_t>(kCtrWords);
@@ -1827,6 +1933,7 @@ struct StoreImpl {
       if (al % 16 == 0) by_lanes(uint4{});
       else if (al % 4 == 0) by_lanes(uint32_t{});
       else by_lanes(uint16_t{});
+      if (cfg.score_policy == SE_SCORE_LFU || cfg.score_policy == SE_SCORE_LRU) touch_scores(t, dkeys, n, st);
     } else {
       ensure_rows(t, n, st);
       cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
@@ -2009,6 +2116,113 @@ struct StoreImpl {
       }
     }
     if (!is_device_ptr(keys)) cuda_check(cudaStreamSynchronize(st), "sync");
+  }
+
+  // ---- scores and dynamic learning rates -------------------------------------
+  // Store construction (bindings/module.cpp:144-158; dynamic_lr_policy.hpp:32-124).
+  void init_scores(se_store_config &c) {
+    if (c.score_policy < SE_SCORE_NONE || c.score_policy > SE_SCORE_MANUAL)
+      throw std::invalid_argument("unknown score policy");
+    if (c.lr_policy < SE_LR_CONSTANT || c.lr_policy > SE_LR_CUSTOM_LUT)
+      throw std::invalid_argument("unknown dynamic learning-rate policy");
+    if (c.lr_policy != SE_LR_CONSTANT && c.score_policy == SE_SCORE_NONE)
+      throw std::invalid_argument("dynamic learning-rate policy requires a score policy");
+    std::vector<float> lut;
+    if (c.lr_policy == SE_LR_COSINE_FREQUENCY) {
+      // CosineFrequencyLrPolicy's table: (1 + cos(pi * i / max_score)) / 2
+      if (!std::isfinite(c.lr_min_ratio) || c.lr_min_ratio < 0.0f || c.lr_min_ratio > 1.0f)
+        throw std::invalid_argument("min_lr_ratio must be finite and in [0, 1]");
+      if (c.lr_max_score == 0) throw std::invalid_argument("max_score must be greater than zero");
+      if (c.lr_max_score > (uint64_t(1) << 28)) throw std::invalid_argument("max_score above 2^28 is not supported");
+      lut.resize(size_t(c.lr_max_score) + 1);
+      const float pi = static_cast<float>(3.14159265358979323846);
+      for (uint64_t i = 0; i <= c.lr_max_score; ++i) {
+        const float ratio = static_cast<float>(i) / static_cast<float>(c.lr_max_score);
+        const float cos_val = std::cos(pi * ratio);
+        lut[size_t(i)] = (1.0f + cos_val) / 2.0f;
+      }
+      lr_max = c.lr_max_score;
+    } else if (c.lr_policy == SE_LR_CUSTOM_LUT) {
+      if (c.lr_lut == nullptr || c.lr_lut_len == 0) throw std::invalid_argument("lut must not be empty");
+      for (size_t i = 0; i < c.lr_lut_len; ++i)
+        if (!std::isfinite(c.lr_lut[i]) || c.lr_lut[i] < 0.0f)
+          throw std::invalid_argument("lut multipliers must be finite and non-negative");
+      lut.assign(c.lr_lut, c.lr_lut + c.lr_lut_len);
+      lr_max = c.lr_lut_len - 1;
+    }
+    c.lr_lut = nullptr;  // the caller's array is not kept
+    c.lr_lut_len = lut.size();
+    cfg.lr_lut = nullptr;
+    cfg.lr_lut_len = lut.size();
+    if (!lut.empty()) {
+      lr_lut = dalloc<float>(lut.size());
+      cuda_check(cudaMemcpy(lr_lut, lut.data(), lut.size() * 4, cudaMemcpyHostToDevice), "upload lut");
+    }
+    if (c.score_policy == SE_SCORE_LRU) {
+      const unsigned long long start[2] = {1ull, 1ull};  // the reference's clock starts at 1
+      lru_clock = dalloc<unsigned long long>(2);
+      cuda_check(cudaMemcpy(lru_clock, start, 16, cudaMemcpyHostToDevice), "init clock");
+    }
+  }
+
+  // on_access for every position of a lookup whose key is present.
+  void touch_scores(Table &t, const void *dkeys, size_t n, cudaStream_t st) {
+    if (cfg.score_policy == SE_SCORE_LFU) {
+      k_touch_lfu<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), t.L, t.slabs, dkeys, cfg.key_dtype, n);
+      launched("k_touch_lfu");
+    } else if (cfg.score_policy == SE_SCORE_LRU) {
+      uint32_t *rows = bag_rows.get(n), *hits = exp_flags.get(n), *rank = exp_at.get(n);
+      size_t tmp_bytes = 0;
+      cuda_check(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, hits, rank, int(n), st), "scan size");
+      uint8_t *tmp = exp_tmp.get(tmp_bytes);
+      k_touch_find<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.dir(), dkeys, cfg.key_dtype, n, rows, hits);
+      launched("k_touch_find");
+      cuda_check(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, hits, rank, int(n), st), "scan");
+      k_touch_lru<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t.L, t.slabs, rows, hits, rank, n, lru_clock);
+      launched("k_touch_lru");
+      cuda_check(cudaMemcpyAsync(lru_clock, lru_clock + 1, 8, cudaMemcpyDeviceToDevice, st), "clock");
+    }
+  }
+
+  // assign_scores (hogwild_embedding_store.hpp:5202-5250), without row lengths.
+  void assign_scores(const void *keys, size_t n, const uint64_t *scores, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (cfg.score_policy == SE_SCORE_NONE) throw Error(SE_ERR_RUNTIME, "assign_scores requires a score-enabled policy");
+    if (n == 0) return;
+    if (scores == nullptr) throw std::invalid_argument("assign_scores row counts differ");
+    cudaStream_t st = pick(sp);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const auto *dsc = static_cast<const unsigned long long *>(stage_in(stage_vals, scores, n * 8, st));
+    uint8_t *done = score_done.get(n);
+    cuda_check(cudaMemsetAsync(done, 0, n, st), "memset");
+    for (auto &t : tables) {
+      k_assign_scores<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t->dir(), t->L, t->slabs, dkeys, cfg.key_dtype,
+                                                                      n, dsc, done);
+      launched("k_assign_scores");
+    }
+    cuda_check(cudaStreamSynchronize(st), "sync");
+  }
+
+  void read_scores(const void *keys, size_t n, uint64_t *out, void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    if (cfg.score_policy == SE_SCORE_NONE) throw Error(SE_ERR_RUNTIME, "the store keeps no scores (score policy none)");
+    if (n == 0) return;
+    cudaStream_t st = pick(sp);
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
+    const bool host_out = !is_device_ptr(out);
+    auto *dout = reinterpret_cast<unsigned long long *>(host_out ? stage_vals.get(n * 8) : static_cast<void *>(out));
+    uint8_t *done = score_done.get(n);
+    cuda_check(cudaMemsetAsync(done, 0, n, st), "memset");
+    cuda_check(cudaMemsetAsync(dout, 0, n * 8, st), "memset");
+    for (auto &t : tables) {
+      k_read_scores<<<grid_for(n, 256, 0x7fffffffu), 256, 0, st>>>(t->dir(), t->L, t->slabs, dkeys, cfg.key_dtype, n,
+                                                                    dout, done);
+      launched("k_read_scores");
+    }
+    if (host_out) cuda_check(cudaMemcpyAsync(out, dout, n * 8, cudaMemcpyDeviceToHost, st), "copy out");
+    cuda_check(cudaStreamSynchronize(st), "sync");
   }
 
   // ---- checkpoint interop ------------------------------------------------------
@@ -2429,20 +2643,30 @@ struct StoreImpl {
     o.factor = cfg.gradient_scale / float(nsteps);
     o.raw = cfg.gradient_dtype == cfg.value_dtype && nsteps == 1 && cfg.gradient_scale == 1.0f;
     o.poison = t.ctr + kCtrPoison;
+    o.lr_kind = cfg.lr_policy;
+    o.lr_min_ratio = cfg.lr_min_ratio;
+    o.lr_max_score = lr_max;
+    o.lr_lut = lr_lut;
     const int gdt = cfg.gradient_dtype;
     auto go = [&](auto lanes_tag, auto vec_tag) {
       constexpr int LN = decltype(lanes_tag)::value;
       constexpr int VC = decltype(vec_tag)::value;
       // k_group_hot first (its blocks take whole SMs), k_group_apply beside it
-      {
-        Prof pr(this, "k_group_hot", st);
-        pdl(k_group_hot<LN, VC>, 128, kBlockThreads, 0, st, t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
-        launched("k_group_hot");
-      }
-      Prof pr(this, "k_group_apply", st);
-      pdl(k_group_apply<LN, VC>, grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st,
-          t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
-      launched("k_group_apply");
+      auto launch = [&](auto dyn_tag) {
+        constexpr bool DY = decltype(dyn_tag)::value;
+        {
+          Prof pr(this, "k_group_hot", st);
+          pdl(k_group_hot<LN, VC, DY>, 128, kBlockThreads, 0, st, t.L, t.slabs, o, gdt, t.pgrads, w,
+              t.ctr + kCtrPending);
+          launched("k_group_hot");
+        }
+        Prof pr(this, "k_group_apply", st);
+        pdl(k_group_apply<LN, VC, DY>, grid_for(size_t(P) * LN, 256, 148 * 8), 256, 0, st,
+            t.L, t.slabs, o, gdt, t.pgrads, w, t.ctr + kCtrPending);
+        launched("k_group_apply");
+      };
+      if (cfg.lr_policy != SE_LR_CONSTANT) launch(std::true_type{});
+      else launch(std::false_type{});
     };
     auto by_lanes = [&](auto vec_tag) {
       const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
@@ -2890,6 +3114,7 @@ int se_store_create(const se_store_config *config, se_store **out_store) {
     cuda_check(cudaStreamCreateWithFlags(&st.own, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaMallocHost(&st.status_host, 64), "cudaMallocHost");
     cuda_check(cudaMallocHost(&st.u64_host, 64), "cudaMallocHost");
+    st.init_scores(st.cfg);  // validates the score and lr policies; uploads the LUT
     for (size_t i = 0; i < c.num_dims; ++i) {
       bool dup = false;
       for (auto &t : st.tables) dup |= t->dim == c.dims[i];
@@ -2959,6 +3184,14 @@ int se_assign(se_store *store, const void *keys, size_t n, const void *values, s
     if (num_values != n * size_t(d)) throw std::invalid_argument("values size does not match row lengths");
     checked(store)->impl.assign(keys, n, d, values, stream);
   });
+}
+
+int se_assign_scores(se_store *store, const void *keys, size_t n, const uint64_t *scores, void *stream) {
+  return guarded([&] { checked(store)->impl.assign_scores(keys, n, scores, stream); });
+}
+
+int se_read_scores(se_store *store, const void *keys, size_t n, uint64_t *scores_out, void *stream) {
+  return guarded([&] { checked(store)->impl.read_scores(keys, n, scores_out, stream); });
 }
 
 int se_export_snapshot(se_store *store, int64_t dim, uint64_t *num_keys_out, void *stream) {

@@ -52,6 +52,7 @@ struct Layout {
   uint32_t step;
   uint32_t nstate;     // 0, 1 (Adagrad) or 2 (Adam)
   int32_t pdt, odt;    // value / optimizer dtypes (SE_FLOAT32 / SE_FLOAT16 / SE_BFLOAT16)
+  uint32_t score;      // offset of the row's u64 score; 0: the store keeps no scores
 };
 
 // Home bucket from the high bits of the SplitMix64 hash: the hash partitioner

@@ -153,14 +153,88 @@ class Optimizer:
     kind = "none"
 
 
+# ---------------------------------------------------------------------------
+# Dynamic learning-rate policies (optimizer/dynamic_lr_policy.hpp:32-124,
+# bindings/module.cpp:491-560): the row's learning rate from its score
+# ---------------------------------------------------------------------------
+
+
+class LrPolicy:
+    code = 0
+    requires_score = False
+    min_lr_ratio = 0.0
+    max_score = 0
+    lut: list = []
+
+
+class ConstantLrPolicy(LrPolicy):
+    """lr for every row."""
+
+
+class SqrtDecayLrPolicy(LrPolicy):
+    """lr / sqrt(score) (lr at score 0)."""
+
+    code = 1
+    requires_score = True
+
+
+class LogDecayLrPolicy(LrPolicy):
+    """lr / log2(2 + score)."""
+
+    code = 2
+    requires_score = True
+
+
+class InverseDecayLrPolicy(LrPolicy):
+    """lr / score (lr at score 0)."""
+
+    code = 3
+    requires_score = True
+
+
+class CosineFrequencyLrPolicy(LrPolicy):
+    """From lr at score 0 down to min_lr_ratio * lr at max_score along a half cosine."""
+
+    code = 4
+    requires_score = True
+
+    def __init__(self, min_lr_ratio: float = 0.1, max_score: int = 1024):
+        if not math.isfinite(min_lr_ratio) or min_lr_ratio < 0.0 or min_lr_ratio > 1.0:
+            raise ValueError("min_lr_ratio must be finite and in [0, 1]")
+        if int(max_score) == 0:
+            raise ValueError("max_score must be greater than zero")
+        self.min_lr_ratio = float(min_lr_ratio)
+        self.max_score = int(max_score)
+
+
+class CustomLutLrPolicy(LrPolicy):
+    """lr * lut[min(score, len(lut) - 1)]."""
+
+    code = 5
+    requires_score = True
+
+    def __init__(self, lut):
+        lut = [float(x) for x in lut]
+        if not lut:
+            raise ValueError("lut must not be empty")
+        if any(not math.isfinite(x) or x < 0.0 for x in lut):
+            raise ValueError("lut multipliers must be finite and non-negative")
+        self.lut = lut
+
+
+def _check_policy(policy):
+    if policy is not None and not isinstance(policy, LrPolicy):
+        raise TypeError("dynamic_lr_policy must be an LrPolicy")
+    return policy
+
+
 class Sgd(Optimizer):
     """SgdConfig (optimizer/optimizer_config.hpp:38-42): p -= lr * (g + wd * p)."""
 
     kind = "sgd"
 
     def __init__(self, lr: float = 1e-2, weight_decay: float = 0.0, dynamic_lr_policy=None):
-        if dynamic_lr_policy is not None:
-            raise NotImplementedError("dynamic learning-rate policies are not supported by the GPU store")
+        self.dynamic_lr_policy = _check_policy(dynamic_lr_policy)
         self.lr = float(lr)
         self.weight_decay = float(weight_decay)
 
@@ -173,8 +247,7 @@ class Adam(Optimizer):
 
     def __init__(self, lr: float = 1e-3, beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
                  weight_decay: float = 0.0, dynamic_lr_policy=None):
-        if dynamic_lr_policy is not None:
-            raise NotImplementedError("dynamic learning-rate policies are not supported by the GPU store")
+        self.dynamic_lr_policy = _check_policy(dynamic_lr_policy)
         self.lr = float(lr)
         self.beta1 = float(beta1)
         self.beta2 = float(beta2)
@@ -194,7 +267,8 @@ class Adagrad(Optimizer):
     kind = "adagrad"
 
     def __init__(self, lr: float = 1e-2, eps: float = 1e-8, weight_decay: float = 0.0,
-                 initial_accumulator_value: float = 0.1):
+                 initial_accumulator_value: float = 0.1, dynamic_lr_policy=None):
+        self.dynamic_lr_policy = _check_policy(dynamic_lr_policy)
         self.lr = float(lr)
         self.eps = float(eps)
         self.weight_decay = float(weight_decay)
@@ -235,8 +309,12 @@ class EmbeddingStore:
             opt = Adam()
         if not cfg.dims:
             raise ValueError("dims must not be empty")
-        if score_policy not in ("none", ""):
-            raise NotImplementedError("score policies (eviction scoring) are not supported by the GPU store")
+        # parse_store_score_policy (backend/hogwild/store_construction.cpp:9-19)
+        if score_policy not in ("none", "lfu", "lru", "manual"):
+            raise ValueError(f"unknown score policy: {score_policy}")
+        policy = getattr(opt, "dynamic_lr_policy", None) if cfg.enable_optimizer else None
+        if policy is not None and policy.requires_score and score_policy == "none":
+            raise ValueError("dynamic learning-rate policy requires a score policy")
         if not math.isfinite(cfg.gradient_scale) or cfg.gradient_scale <= 0.0:
             raise ValueError("gradient_scale must be finite and greater than zero")
         self._config = cfg
@@ -245,7 +323,7 @@ class EmbeddingStore:
         self._optimizer_dtype = optimizer_dtype
         self._gradient_dtype = gradient_dtype
         self._optimizer_enabled = cfg.enable_optimizer
-        self._score_policy = "none"
+        self._score_policy = score_policy
         self._thread_budget = cfg.thread_budget if cfg.thread_budget > 0 else max(1, os.cpu_count() or 1)
         self._device = _default_device() if cfg.device is None else int(cfg.device)
         self._operational = True
@@ -276,6 +354,16 @@ class EmbeddingStore:
         c.device = self._device
         c.simd_width = cfg.simd_width
         c.internal_shards = self._thread_budget
+        c.score_policy = {"none": 0, "lfu": 1, "lru": 2, "manual": 3}[score_policy]
+        lut = None
+        if policy is not None:
+            c.lr_policy = policy.code
+            c.lr_min_ratio = policy.min_lr_ratio
+            c.lr_max_score = policy.max_score
+            if policy.lut:
+                lut = (C.c_float * len(policy.lut))(*policy.lut)
+                c.lr_lut = C.cast(lut, C.POINTER(C.c_float))
+                c.lr_lut_len = len(policy.lut)
         self._optimizer = opt
         self._lib = N.lib()
         h = C.c_void_p()
@@ -427,6 +515,29 @@ class EmbeddingStore:
         stream = self._stream(g) or self._stream(k)
         N.check(self._lib.se_embedding_bag_backward(self._h, k.ptr, k.size, o.ptr, nb, int(g.shape[1]), g.ptr,
                                                     stream))
+
+    # ---- scores ---------------------------------------------------------------------
+
+    def assign_scores(self, keys, scores) -> None:
+        """Sets each key's score in the first table holding it; absent keys are
+        skipped (hogwild_embedding_store.hpp:5202-5250)."""
+        k = self._keys(keys)
+        sc = as_input(scores, "scores")
+        if sc.dtype != "uint64":
+            raise ValueError("scores must be uint64")
+        if sc.size != k.size:
+            raise ValueError("assign_scores row counts differ")
+        if (k.cuda_device is None) != (sc.cuda_device is None):
+            raise ValueError("keys and scores must be in the same memory space")
+        N.check(self._lib.se_assign_scores(self._h, k.ptr, k.size, sc.ptr, self._stream(k)))
+
+    def read_scores(self, keys):
+        """uint64 score of each key (0 when absent); host keys give a numpy array."""
+        k = self._keys(keys)
+        out = empty_like_space(k, (k.size,), "uint64")
+        if k.size:
+            N.check(self._lib.se_read_scores(self._h, k.ptr, k.size, data_ptr(out), self._stream(k)))
+        return out
 
     # ---- mutation API -----------------------------------------------------------
 

@@ -61,3 +61,21 @@ def test_config_errors():
     cfg = se.EmbeddingConfig(dims=[4], value_dtype=float, key_dtype=int)
     assert cfg.value_dtype == "float32" and cfg.key_dtype == "int64"
     assert math.isclose(se.Adagrad().initial_accumulator_value, 0.1)
+
+
+@pytest.mark.parametrize(
+    "factory",
+    [
+        lambda: se.CustomLutLrPolicy(lut=[]),
+        lambda: se.CustomLutLrPolicy(lut=[-0.1]),
+        lambda: se.CustomLutLrPolicy(lut=[math.nan]),
+        lambda: se.CosineFrequencyLrPolicy(min_lr_ratio=-0.1),
+        lambda: se.CosineFrequencyLrPolicy(min_lr_ratio=1.1),
+        lambda: se.CosineFrequencyLrPolicy(min_lr_ratio=math.nan),
+        lambda: se.CosineFrequencyLrPolicy(max_score=0),
+    ],
+)
+def test_invalid_lr_policy_configuration_is_rejected(factory):
+    """tests/test_dynamic_lr.py:117-131."""
+    with pytest.raises(ValueError):
+        factory()

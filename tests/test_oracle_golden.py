@@ -163,3 +163,45 @@ def test_unique_oracle_reference_cases():
         assert (np.diff(first) > 0).all()  # order of first appearance
         e = O.unique_first_occurrence(np.empty(0, dtype=dtype))
         assert all(x.size == 0 for x in e)
+
+
+@pytest.mark.parametrize(
+    ("policy", "kw", "score", "expected"),
+    [
+        ("constant", {}, 37, 1.0),
+        ("sqrt", {}, 0, 1.0),
+        ("sqrt", {}, 4, 0.5),
+        ("log", {}, 2, 0.5),
+        ("inverse", {}, 0, 1.0),
+        ("inverse", {}, 4, 0.25),
+        ("cosine", {"lr_min_ratio": 0.2, "lr_max_score": 4}, 0, 1.0),
+        ("cosine", {"lr_min_ratio": 0.2, "lr_max_score": 4}, 2, 0.6),
+        ("cosine", {"lr_min_ratio": 0.2, "lr_max_score": 4}, 4, 0.2),
+        ("cosine", {"lr_min_ratio": 0.2, "lr_max_score": 4}, 5, 0.2),
+        ("lut", {"lr_lut": [0.25, 0.5, 0.75]}, 0, 0.25),
+        ("lut", {"lr_lut": [0.25, 0.5, 0.75]}, 2, 0.75),
+        ("lut", {"lr_lut": [0.25, 0.5, 0.75]}, 3, 0.75),
+    ],
+)
+def test_oracle_lr_policies_reference_answers(policy, kw, score, expected):
+    """The reference's known answers for its policies (tests/test_dynamic_lr.py:35-52):
+    an SGD step of lr 1 on a zero row with gradient 1 moves it by -lr(score)."""
+    orc = O.OracleStore([16], key_dtype="int64", init="zeros", optimizer="sgd", lr=1.0, score_policy="manual",
+                        lr_policy=policy, **kw)
+    keys = np.array([7], dtype=np.int64)
+    orc.lookup_or_insert(keys, 16)
+    orc.assign_scores(keys, np.array([score], dtype=np.uint64))
+    orc.accumulate_gradients(keys, np.ones((1, 16), dtype=np.float32), 16)
+    orc.optimizer_step(1)
+    np.testing.assert_allclose(-orc.lookup(keys, 16), expected, atol=1e-6)
+
+
+def test_oracle_lfu_lru_scores():
+    """LFU counts every found position of a lookup; LRU stamps them with the
+    store's clock (from 1) in batch order; lookup_or_insert does not touch."""
+    for policy, expect in (("lfu", [3, 1, 0]), ("lru", [4, 2, 0])):
+        orc = O.OracleStore([4], key_dtype="int64", optimizer="sgd", score_policy=policy)
+        orc.lookup_or_insert(np.array([1, 2, 3], dtype=np.int64), 4)
+        orc.lookup(np.array([1, 2, 9, 1], dtype=np.int64), 4)   # 9 is absent
+        orc.lookup(np.array([1], dtype=np.int64), 4)
+        assert orc.read_scores(np.array([1, 2, 3], dtype=np.int64)).tolist() == expect
