@@ -65,6 +65,9 @@ def args_parse():
                    help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
     p.add_argument("--loopback", action="store_true",
                    help="N = 1: route the step through a one-rank peer-memory exchange (its kernels on one GPU)")
+    p.add_argument("--bag-only", type=int, default=0, metavar="SAMPLES",
+                   help="run only the DLRM-shaped embedding-bag step with this many samples per batch "
+                        "(a small case for profiling) and print its JSON")
     return p.parse_args()
 
 
@@ -663,7 +666,7 @@ def unique_bench(se, torch, num_keys):
                         "Zipf 1.05 + 5% new), device-resident", "batches": out}
 
 
-def dlrm_bag_bench(se, torch, peak):
+def dlrm_bag_bench(se, torch, peak, samples: int = 8192, capacity: int = 8_000_000):
     """DLRM-shaped embedding-bag step: 26 tables' pre-mixed u64 keys in one
     dim-128 fp32 store with Adam(1e-3); 8,192 samples x 26 tables x
     max(1, Poisson(20)) ids (~4.3M ids per step) drawn Zipf(1.2) over each
@@ -673,14 +676,17 @@ def dlrm_bag_bench(se, torch, peak):
     N(0, 1e-3) pooled gradients -> optimizer_step(1). Eager calls, CUDA events."""
     from sparse_embedding_b200.workloads import DlrmWorkload
 
-    wl = DlrmWorkload(max_rows=2_000_000)
+    wl = DlrmWorkload(max_rows=2_000_000, batch=samples)
     dim = wl.dim
-    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", initial_capacity=8_000_000),
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", initial_capacity=capacity),
                               optimizer_config=se.Adam(lr=1e-3))
     steps, warm = 4, 2
     batches = []
     for s in range(warm + steps):
-        k, o, g = wl.make_bags(s)
+        # the first warm-up batch is 10% larger, so the store's step buffers
+        # (sized by the largest window so far) are grown before the timed steps
+        src = DlrmWorkload(max_rows=2_000_000, batch=samples + samples // 10) if s == 0 else wl
+        k, o, g = src.make_bags(s)
         batches.append((torch.from_numpy(k.view(np.int64)).cuda().view(torch.uint64), torch.from_numpy(o).cuda(),
                         torch.from_numpy(g).cuda()))
     ids = [int(b[0].numel()) for b in batches[warm:]]
@@ -717,7 +723,7 @@ def dlrm_bag_bench(se, torch, peak):
     # each distinct row read once, a row number per id, the pooled rows written
     pool_bytes = sum(uniq) / len(uniq) * R + sum(ids) / len(ids) * 4 + nb * R
     pool_gbs = pool_bytes / (kern.get("k_bag_pool", float("nan")) / 1e6) / 1e9
-    out = {"workload": "DLRM-shaped bag step: 26 tables, 8,192 samples, ~4.3M ids/step, dim 128 fp32, Adam; "
+    out = {"workload": f"DLRM-shaped bag step: 26 tables, {samples:,} samples, dim 128 fp32, Adam; "
                        "rows per table 1e3..2e6 (scaled down from 4e7)",
            "ids_per_step": int(sum(ids) / len(ids)), "unique_ids_per_step": int(sum(uniq) / len(uniq)),
            "bags_per_step": nb, "us_per_step": round(el / steps * 1e6, 1),
@@ -842,6 +848,16 @@ def run_reference(args):
 
 def main():
     args = args_parse()
+    if args.bag_only > 0 and args.impl == "ours":
+        import torch
+
+        import sparse_embedding_b200 as se
+
+        peak, _ = measured_hbm()
+        # room for the rows in use plus one batch of keys (the insert bound)
+        cap = min(8_000_000, max(2_000_000, args.bag_only * 26 * 40))
+        print(json.dumps(dlrm_bag_bench(se, torch, peak, samples=args.bag_only, capacity=cap)), flush=True)
+        return
     if args.impl == "reference":
         out = run_reference(args)
     else:
