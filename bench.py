@@ -431,9 +431,35 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_el = max_over_ranks(time.perf_counter() - t0, world)
     e2e_value = world * BATCH * K / e2e_el
+
+    # The link's own bound: the same pinned copies, streams and buffers with
+    # no kernels between them (each step's rows read back from a device
+    # buffer of the same size).
+    rows_d = [torch.empty((BATCH, DIM), dtype=torch.float32, device="cuda") for _ in range(2)]
+
+    def copy_step(s):
+        b = s % 2
+        with torch.cuda.stream(s_in):
+            kd[b].copy_(kh[s], non_blocking=True)
+            gd[b].copy_(gh[s], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            out_h[b].copy_(rows_d[b], non_blocking=True)
+
+    copy_step(0)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for s in range(1, K + 1):
+        copy_step(s)
+    torch.cuda.synchronize()
+    copy_el = max_over_ranks(time.perf_counter() - t0, world)
     e2e = {"value": e2e_value, "unit": "keys/s", "h2d_bytes_per_step": BATCH * (KEY_BYTES + R) * world,
            "d2h_bytes_per_step": BATCH * R * world,
-           "pipeline": "H2D, compute and D2H on separate streams, double-buffered"}
+           "pipeline": "H2D, compute and D2H on separate streams, double-buffered",
+           "link_bound": {"value": world * BATCH * K / copy_el, "unit": "keys/s",
+                          "h2d_gbs_per_gpu": round(BATCH * (KEY_BYTES + R) * K / copy_el / 1e9, 1),
+                          "d2h_gbs_per_gpu": round(BATCH * R * K / copy_el / 1e9, 1),
+                          "note": "the same copies with no kernels: the PCIe ceiling of e2e"}}
 
     large = mut = uniq = bag = None
     if world == 1 and not args.no_forward:
