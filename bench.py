@@ -45,6 +45,13 @@ FWD_KEYS, FWD_DIM, FWD_BATCH, FWD_BATCHES = 1_000_000, 32, 4096, 400
 WIDE_KEYS, WIDE_DIM, WIDE_BATCH, WIDE_BATCHES = 200_000_000, 256, 262_144, 40
 KEY_BYTES, M_BYTES = 8, 16
 FALLBACK_HBM_GBS = 6650.0
+# Kernels of one train step (lookup_or_insert -> accumulate_gradients ->
+# optimizer_step), by accumulation mode.
+STEP_KERNELS = {
+    "ordered": ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc",
+                "k_group_place", "k_group_apply", "k_group_hot"],
+    "atomic": ["k_lookup_or_insert", "k_deferred", "k_acc_atomic", "k_acc_apply"],
+}
 # value = train-step keys/s; the forward-lookup figure rides in "forward_lookup".
 METRIC = "forward_lookup Mkeys/s & train-step keys/s at 1/2/4/8 B200; % of HBM peak"
 
@@ -65,6 +72,9 @@ def args_parse():
                    help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
     p.add_argument("--loopback", action="store_true",
                    help="N = 1: route the step through a one-rank peer-memory exchange (its kernels on one GPU)")
+    p.add_argument("--accumulation", choices=["atomic", "ordered"], default="ordered",
+                   help="how accumulate_gradients sums each key's rows: per-key fp32 sums with vector "
+                        "reductions (atomic) or kept rows summed in arrival order at the step (ordered)")
     p.add_argument("--bag-only", type=int, default=0, metavar="SAMPLES",
                    help="run only the DLRM-shaped embedding-bag step with this many samples per batch "
                         "(a small case for profiling) and print its JSON")
@@ -247,7 +257,8 @@ def run_ours(args):
     # captured: one batch from every rank.
     cap = int(len(mine) + (W + 4 * K + 8) * BATCH * 0.1 + (world + 1) * BATCH)
     store = se.EmbeddingStore(
-        se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap),
+        se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap,
+                           accumulation=args.accumulation),
         optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
     for chunk in np.array_split(mine, max(1, len(mine) // 1_000_000)):
         store.lookup_or_insert(torch.from_numpy(chunk).cuda(), DIM)
@@ -325,8 +336,7 @@ def run_ours(args):
     elapsed_prof, _, _ = timed_pass(W + K, True)
 
     # Per-kernel device time inside the timed region.
-    names = ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc",
-             "k_group_place", "k_group_apply", "k_group_hot"]
+    names = list(STEP_KERNELS[args.accumulation])
     if (world > 1 and args.transport == "p2p") or args.loopback:
         names += ["k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_rows", "k_ex_scatter_grads"]
     times = {}
@@ -336,20 +346,22 @@ def run_ours(args):
     peak, peak_kind = measured_hbm()
     R = DIM * 4
     n_new = int(round(BATCH * wl.new_fraction))
-    # Algorithmic bytes per launch:
+    # Algorithmic bytes per launch (what the step must move, per unit):
     #   lookup_or_insert: K + M + R (row read) + R (out write) per key, plus
     #                     R (param) + R (accumulator) initialised per new key;
-    #   accumulate:       K + R read and K + R appended per gradient row;
-    #   apply (k_group_apply + k_group_hot, one launch each per step):
-    #                     per unique key 2R (param r/w) + 2R (accumulator r/w),
-    #                     plus R per gradient row reduced.
+    #   accumulate:       K + R (key and gradient row read) per gradient row;
+    #   optimizer:        per unique key 2R (param read + write) + 2R (Adagrad
+    #                     accumulator read + write); the reduced gradient is
+    #                     on chip (ordered: registers) or in L2 (atomic sums).
     mean_u = sum(uniq) / len(uniq)
     rows_per_owner = BATCH  # weak scaling: each owner receives ~BATCH rows per step
+    acc_name, apply_members = (("k_acc_atomic", ["k_acc_apply"]) if args.accumulation == "atomic"
+                               else ("k_accumulate", ["k_group_apply", "k_group_hot"]))
     units = {
         "k_lookup_or_insert": (["k_lookup_or_insert" if "k_ex_owner" not in names else "k_ex_owner"],
                                rows_per_owner * (KEY_BYTES + M_BYTES + 2 * R) + n_new * 2 * R),
-        "k_accumulate": (["k_accumulate"], rows_per_owner * 2 * (KEY_BYTES + R)),
-        "k_group_apply+k_group_hot": (["k_group_apply", "k_group_hot"], mean_u * 4 * R + rows_per_owner * R),
+        acc_name: ([acc_name], rows_per_owner * (KEY_BYTES + R)),
+        "+".join(apply_members): (apply_members, mean_u * 4 * R),
     }
     kern = []
     total_ms = sum(t[0] for t in times.values())
@@ -483,6 +495,7 @@ def run_ours(args):
                                "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
                                "eps 1e-8, init_acc 0.1), hash partitioner",
                    "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
+                   "accumulation": args.accumulation,
                    "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none")),
                    "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
         "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
@@ -590,8 +603,7 @@ def large_batch_bench(store, torch, num_keys, peak):
         step(s)
     torch.cuda.synchronize()
     per_kernel = {}
-    for nm in ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc", "k_group_place",
-               "k_group_apply", "k_group_hot"]:
+    for nm in STEP_KERNELS["atomic" if store._config.accumulation == "atomic" else "ordered"]:
         ms, cnt = store.profile_read(nm)
         if cnt:
             per_kernel[nm] = round(ms / cnt * 1e3, 1)

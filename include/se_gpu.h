@@ -54,6 +54,17 @@ enum se_lr_policy {
   SE_LR_CONSTANT = 0, SE_LR_SQRT_DECAY = 1, SE_LR_LOG_DECAY = 2, SE_LR_INVERSE_DECAY = 3,
   SE_LR_COSINE_FREQUENCY = 4, SE_LR_CUSTOM_LUT = 5
 };
+/* How accumulate_gradients sums a key's gradient rows until optimizer_step.
+ * ORDERED: rows are kept and each key's rows are summed in arrival order
+ * from +0.0, rounding to the gradient dtype after each add - the reference's
+ * TransientArena order (sparse_embedding/src/arena/transient_arena.hpp:234-269),
+ * bit-exact for keys with at most 64 rows per window.
+ * ATOMIC: rows are added on arrival into fp32 per-key sums with vector
+ * reductions (a hash table keyed by key, like TransientArena::accumulate_hashed,
+ * transient_arena.hpp:119-145); the order of the adds varies, so updates
+ * match ORDERED within the rounding of a reassociated fp32 sum. Tables whose
+ * row exceeds 8,192 values use ORDERED. */
+enum se_accumulation_mode { SE_ACCUM_ORDERED = 0, SE_ACCUM_ATOMIC = 1 };
 /* Registered partitioners: sparse_embedding.{modulo,hash,fast_range}. */
 enum se_partitioner_kind { SE_PART_MODULO = 0, SE_PART_HASH = 1, SE_PART_FAST_RANGE = 2 };
 
@@ -87,6 +98,7 @@ typedef struct se_store_config {
   uint64_t lr_max_score;     /* cosine: score where the decay ends                 */
   const float *lr_lut;       /* custom LUT: multiplier per score (last one beyond) */
   size_t lr_lut_len;
+  int32_t accumulation;      /* enum se_accumulation_mode                          */
 } se_store_config;
 
 typedef struct se_store se_store;
@@ -227,6 +239,12 @@ int se_store_dropped_gradients(se_store *store, uint64_t *out_count);
  * key is absent. Host pointers. */
 int se_store_read_state(se_store *store, int64_t dim, uint64_t key, void *param_out,
                         void *state_out, uint32_t *step_out, int32_t *found);
+/* EmbeddingTableFacade::clear (hogwild_embedding_store.hpp:5107-5154; Python
+ * EmbeddingStore.clear, sparse_embedding/src/bindings/module.cpp:640):
+ * removes every key of every table and discards the gradients accumulated
+ * since the last optimizer_step; reserved capacity is kept. Waits for the
+ * stream. */
+int se_store_clear(se_store *store, void *stream);
 /* Waits for all work the store has queued. */
 int se_store_synchronize(se_store *store);
 /* CUDA-event timing of the store's kernels: enable, then read the summed

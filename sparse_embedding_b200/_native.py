@@ -27,6 +27,7 @@ VALUE_CODES = {"float32": 0, "float16": 1, "bfloat16": 2}
 OPT_CODES = {"none": 0, "sgd": 1, "adam": 2, "adagrad": 3}
 INIT_CODES = {"zeros": 0, "uniform": 1}
 PART_CODES = {"modulo": 0, "hash": 1, "fast_range": 2}
+ACCUM_CODES = {"ordered": 0, "atomic": 1}
 
 
 class StoreConfig(C.Structure):
@@ -61,6 +62,7 @@ class StoreConfig(C.Structure):
         ("lr_max_score", C.c_uint64),
         ("lr_lut", C.POINTER(C.c_float)),
         ("lr_lut_len", C.c_size_t),
+        ("accumulation", C.c_int32),
     ]
 
 
@@ -105,6 +107,7 @@ _SIGNATURES = {
     "se_store_dropped_gradients": [_vp, C.POINTER(_u64)],
     "se_store_read_state": [_vp, _i64, _u64, _vp, _vp, C.POINTER(_u32), C.POINTER(_i32)],
     "se_store_synchronize": [_vp],
+    "se_store_clear": [_vp, _vp],
     "se_store_profile_enable": [_vp, _i32],
     "se_store_profile_read": [_vp, C.c_char_p, C.POINTER(C.c_double), C.POINTER(_u64)],
     "se_partition": [_i32, _u32, _i32, _vp, _sz, _vp, _i32, _vp],

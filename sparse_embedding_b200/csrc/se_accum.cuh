@@ -1,0 +1,263 @@
+// Atomic accumulation mode of the B200 store.
+//
+// The ordered mode appends every gradient row and reduces each key's rows in
+// arrival order at optimizer_step (bit-exact with the reference's serial
+// sum). This mode instead sums gradients as they arrive into a hash table
+// keyed by key - the structure of TransientArena::accumulate_hashed
+// (arena/transient_arena.hpp:119-145: one accumulator slot per key, found by
+// hashing the key, each gradient row added into it) - with the additions
+// made concurrent:
+//
+//   k_acc_atomic  one block per tile of the batch: the tile's distinct keys
+//                 go into a shared-memory hash set, each gradient row is
+//                 added into its key's shared-memory sum, then each distinct
+//                 key finds (or claims) its slot of the table and adds the
+//                 tile's sum with 16-byte vector reductions
+//                 (red.global.add.v4.f32). Hot keys thus cost one reduction
+//                 per tile, not one per row.
+//   k_acc_apply   optimizer_step: one lane group per claimed slot resolves
+//                 the key in the directory (absent keys drop their rows, as
+//                 SlotStore::update_batch does,
+//                 hogwild_embedding_store.hpp:1942-1952), applies the
+//                 optimizer to the row with the slot's sum, and frees the
+//                 slot (sum zeroed, key cleared) for the next window.
+//
+// Sums are fp32 whatever the gradient dtype; the order of a key's additions
+// is not the arrival order, so updates equal the ordered mode's within the
+// rounding of a reassociated fp32 sum (1e-5 relative for fp32 tables).
+// Keys need not be present when their gradients arrive: they are resolved
+// at optimizer_step, like the reference's transient arena keyed by key.
+#pragma once
+
+#include "se_store_kernels.cuh"
+
+namespace se_gpu {
+
+// Hash table of one store table's gradient sums for the current window.
+struct AccTab {
+  unsigned long long *keys;  // [G] key of each slot, kEmptyKey when free
+  float *vals;               // [(G + 1) * dim] fp32 sums, zero when free; slot G holds the all-ones key
+  uint32_t *cnt;             // [G + 1] gradient rows summed into each slot
+  uint32_t *list;            // [G + 1] claimed slots in claim order
+  uint32_t *ctr;             // [0] claimed slots, [1] claim flag of slot G, [2] finished apply blocks
+  uint32_t mask;             // G - 1; G is a power of two
+  uint32_t dim;
+};
+
+constexpr uint32_t kAccThreads = 256;
+constexpr uint32_t kAccMaxTile = 256;        // rows per block of k_acc_atomic
+constexpr uint64_t kAccSmemBytes = 32768;    // shared-memory sums per block
+constexpr uint32_t kAccMaxDim = 8192;        // longest row of an atomic-mode table (one row per tile)
+
+// Slot of `key`, claiming a free one if the key has none; `claimed` tells
+// the caller to list the slot. Linear probing from the high bits of the
+// SplitMix64 hash (hash-partitioned GPUs share the low bits). kNoRow when
+// every slot is taken (the host sizes the table at twice the window's rows).
+__device__ __forceinline__ uint32_t acc_find_or_claim(const AccTab &a, uint64_t key, bool &claimed) {
+  claimed = false;
+  const uint32_t G = a.mask + 1u;
+  if (key == kEmptyKey) {
+    claimed = atomicCAS(a.ctr + 1, 0u, 1u) == 0u;
+    return G;
+  }
+  uint32_t s = uint32_t(__umul64hi(splitmix64(key), uint64_t(G)));
+  for (uint32_t probe = 0; probe < G; ++probe) {
+    const unsigned long long k = __ldcg(a.keys + s);
+    if (k == key) return s;
+    if (k == kEmptyKey) {
+      const unsigned long long old = atomicCAS(a.keys + s, kEmptyKey, key);
+      if (old == kEmptyKey) {
+        claimed = true;
+        return s;
+      }
+      if (old == key) return s;
+    }
+    s = (s + 1u) & a.mask;
+  }
+  return kNoRow;
+}
+
+// Adds four floats at a 16-byte aligned address of global memory with one
+// vector reduction (relaxed, device scope).
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// accumulate_gradients in atomic mode. Entries [blockIdx.x * tile, + tile)
+// of the batch (n_max rows, or *n_dev when the batch size is known only on
+// the device). Each gradient is validated and scaled on entry like
+// GradientAccumulator::accumulate_hashed (gradient_accumulator.hpp:88-128):
+// g / gradient_scale must be finite and within the gradient and parameter
+// dtypes (failures raise kStatusBadGradient in *bad_word), and the value
+// added is g (scale 1) or the scaled value rounded to the gradient dtype.
+// With kBag, entry i takes gradient row grad_row[i] (embedding-bag backward).
+// Dynamic shared memory: tile * dim floats.
+template <int VEC, bool kBag>
+__global__ void __launch_bounds__(kAccThreads)
+k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
+             const void *__restrict__ grads, int gdt, float scale, float maxv, uint32_t tile, uint32_t hbits,
+             uint32_t *bad_word, uint32_t *status, const uint32_t *__restrict__ grad_row) {
+  extern __shared__ float s_acc[];                    // [tile][dim] sums of the tile's distinct keys
+  __shared__ unsigned long long s_hkey[2 * kAccMaxTile];  // hash set of the tile's keys
+  __shared__ uint32_t s_hloc[2 * kAccMaxTile + 1];    // local index of each set slot; [H]: the all-ones key
+  __shared__ uint32_t s_ent[kAccMaxTile];             // set slot, then local index, of each entry
+  __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
+  __shared__ uint32_t s_lcnt[kAccMaxTile];            // entries of each local index
+  __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
+  __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
+  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base;
+  pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
+  const size_t n = n_dev ? min(size_t(*n_dev), n_max) : n_max;
+  const size_t i0 = size_t(blockIdx.x) * tile;
+  if (i0 >= n) return;  // whole block: past the end of a device-sized batch
+  const uint32_t m = uint32_t(min(size_t(tile), n - i0));
+  const uint32_t H = 1u << hbits;  // >= 2 * tile
+  const uint32_t dim = a.dim;
+  const uint32_t tid = threadIdx.x;
+  for (uint32_t h = tid; h < H; h += blockDim.x) s_hkey[h] = kEmptyKey;
+  for (uint32_t q = tid; q < tile; q += blockDim.x) s_lcnt[q] = 0u;
+  if (tid == 0) {
+    s_nloc = 0u;
+    s_spec = 0u;
+    s_nclaim = 0u;
+  }
+  __syncthreads();
+  // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
+  //    takes slot H)
+  for (uint32_t j = tid; j < m; j += blockDim.x) {
+    const uint64_t key = load_key(keys, kdt, i0 + j);
+    uint32_t h = H;
+    if (key == kEmptyKey) {
+      s_spec = 1u;
+    } else {
+      h = uint32_t(splitmix64(key) >> 32) & (H - 1u);
+      for (uint32_t probe = 0; probe < H; ++probe) {  // at most half full: ends at the key or a free slot
+        const unsigned long long old = atomicCAS(&s_hkey[h], kEmptyKey, key);
+        if (old == kEmptyKey || old == key) break;
+        h = (h + 1u) & (H - 1u);
+      }
+    }
+    s_ent[j] = h;
+  }
+  __syncthreads();
+  // 2. a local index per distinct key
+  for (uint32_t h = tid; h <= H; h += blockDim.x) {
+    const bool used = h < H ? s_hkey[h] != kEmptyKey : s_spec != 0u;
+    if (used) {
+      const uint32_t q = atomicAdd(&s_nloc, 1u);
+      s_hloc[h] = q;
+      s_lkey[q] = h < H ? s_hkey[h] : kEmptyKey;
+    }
+  }
+  __syncthreads();
+  const uint32_t nloc = s_nloc;
+  for (uint32_t j = tid; j < m; j += blockDim.x) {
+    const uint32_t q = s_hloc[s_ent[j]];
+    s_ent[j] = q;
+    atomicAdd(&s_lcnt[q], 1u);
+  }
+  for (uint32_t x = tid; x < nloc * dim; x += blockDim.x) s_acc[x] = 0.0f;
+  __syncthreads();
+  // 3. gradient rows into the shared sums (ILP loads ahead of the adds)
+  const uint32_t units = dim / VEC;
+  const uint32_t chunks = m * units;
+  bool bad = false;
+  constexpr int kIlp = 4;
+  for (uint32_t c0 = tid; c0 < chunks; c0 += blockDim.x * kIlp) {
+    float g[kIlp][VEC];
+    uint32_t dst[kIlp];
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      const uint32_t c = c0 + uint32_t(k) * blockDim.x;
+      if (c >= chunks) continue;
+      const uint32_t j = c / units;
+      const uint32_t e = (c - j * units) * VEC;
+      const size_t src = kBag ? size_t(grad_row[i0 + j]) : i0 + j;
+      ldv<VEC>(grads, gdt, src * dim + e, g[k]);
+      dst[k] = s_ent[j] * dim + e;
+    }
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      const uint32_t c = c0 + uint32_t(k) * blockDim.x;
+      if (c >= chunks) continue;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        const float s = __fdiv_rn(g[k][v], scale);
+        bad |= !(fabsf(s) <= maxv);
+        const float x = scale != 1.0f ? round_to(gdt, s) : g[k][v];
+        atomicAdd(&s_acc[dst[k] + v], x);
+      }
+    }
+  }
+  if (bad) raise_status(bad_word, kStatusBadGradient);
+  // 4. each distinct key's slot in the table
+  for (uint32_t q = tid; q < nloc; q += blockDim.x) {
+    bool claimed = false;
+    const uint32_t slot = acc_find_or_claim(a, s_lkey[q], claimed);
+    s_gslot[q] = slot;
+    s_crank[q] = claimed ? atomicAdd(&s_nclaim, 1u) : kNoRow;
+    if (slot == kNoRow) raise_status(status, kStatusTableFull);
+    else atomicAdd(a.cnt + slot, s_lcnt[q]);
+  }
+  __syncthreads();
+  if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);
+  __syncthreads();
+  for (uint32_t q = tid; q < nloc; q += blockDim.x)
+    if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = s_gslot[q];
+  // 5. the tile's sums into the table
+  const uint32_t lchunks = nloc * units;
+  for (uint32_t c = tid; c < lchunks; c += blockDim.x) {
+    const uint32_t q = c / units;
+    const uint32_t e = (c - q * units) * VEC;
+    const uint32_t slot = s_gslot[q];
+    if (slot == kNoRow) continue;
+    float *dst = a.vals + size_t(slot) * dim + e;
+    const float *src = s_acc + q * dim + e;
+    if constexpr (VEC == 4) red_add_v4(dst, src[0], src[1], src[2], src[3]);
+    else atomicAdd(dst, src[0]);
+  }
+}
+
+// Validation of a host batch before anything is added (the reference raises
+// before accumulating, gradient_accumulator.hpp:88-104).
+template <int VEC>
+__global__ void __launch_bounds__(256)
+k_acc_check(const void *__restrict__ grads, int gdt, size_t elems, float scale, float maxv, uint32_t *bad_word) {
+  pdl_wait();
+  pdl_trigger();
+  bool bad = false;
+  const size_t chunks = elems / VEC;
+  for (size_t c = size_t(blockIdx.x) * blockDim.x + threadIdx.x; c < chunks; c += size_t(gridDim.x) * blockDim.x) {
+    float g[VEC];
+    ldv<VEC>(grads, gdt, c * VEC, g);
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) bad |= !(fabsf(__fdiv_rn(g[v], scale)) <= maxv);
+  }
+  if (bad) raise_status(bad_word, kStatusBadGradient);
+}
+
+// Moves every claimed slot into a larger table (the window outgrew the old
+// one between accumulate calls). One thread per listed slot.
+__global__ void __launch_bounds__(256) k_acc_move(AccTab from, AccTab to, uint32_t *status) {
+  const uint32_t G = from.mask + 1u;
+  const uint32_t n = min(*from.ctr, G + 1u);
+  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < n; g += gridDim.x * blockDim.x) {
+    const uint32_t slot = from.list[g];
+    const uint64_t key = slot == G ? kEmptyKey : from.keys[slot];
+    bool claimed = false;
+    const uint32_t ns = acc_find_or_claim(to, key, claimed);
+    if (ns == kNoRow) {
+      raise_status(status, kStatusTableFull);
+      continue;
+    }
+    to.list[atomicAdd(to.ctr, 1u)] = ns;
+    to.cnt[ns] = from.cnt[slot];
+    const float *s = from.vals + size_t(slot) * from.dim;
+    float *d = to.vals + size_t(ns) * to.dim;
+    for (uint32_t e = 0; e < from.dim; ++e) d[e] = s[e];
+  }
+}
+
+}  // namespace se_gpu

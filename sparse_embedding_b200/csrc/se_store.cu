@@ -23,6 +23,7 @@
 #include "se_common.cuh"
 #include "se_host.hpp"
 #include "se_store_kernels.cuh"
+#include "se_accum.cuh"
 
 namespace se_gpu {
 
@@ -944,6 +945,73 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
   }
 }
 
+// optimizer_step in atomic mode (the sums of se_accum.cuh): one group of
+// LANES lanes per claimed slot. The slot's key is resolved in the directory
+// now, as SlotStore::update_batch re-resolves keys at step time
+// (hogwild_embedding_store.hpp:2735-2901); an absent key drops its rows and
+// counts them (1942-1952). The sum is scaled to ParamT and applied like the
+// ordered mode's reduced gradient (apply_chunk). Every slot is then freed
+// for the next window: sum zeroed, count and key cleared; the last block
+// resets the claim counters.
+template <int LANES, int VEC, bool kDyn>
+__global__ void __launch_bounds__(256)
+k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o, int apply,
+            unsigned long long *dropped) {
+  pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
+  const uint32_t G = a.mask + 1u;
+  const uint32_t nslots = min(__ldcg(a.ctr), G + 1u);
+  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
+  const uint32_t lane = uint32_t(t % LANES);
+  const unsigned mask = group_mask<LANES>();
+  const bool run = apply && *o.poison == 0u;
+  for (size_t g = t / LANES; g < nslots; g += groups) {
+    const uint32_t slot = __ldcg(a.list + g);
+    float *acc = a.vals + size_t(slot) * L.dim;
+    uint32_t row = kNoRow;
+    if (lane == 0 && apply) row = dir_find<false>(d, slot == G ? kEmptyKey : uint64_t(__ldcg(a.keys + slot)));
+    row = __shfl_sync(mask, row, 0, LANES);
+    if (apply && row == kNoRow) {
+      if (lane == 0) atomicAdd(dropped, (unsigned long long)__ldcg(a.cnt + slot));
+    } else if (run) {
+      uint8_t *slab = slabs + size_t(row) * L.stride;
+      uint32_t step = 0;
+      if (o.kind == SE_OPT_ADAM) {
+        if (lane == 0) step = next_step(L, slab);
+        step = __shfl_sync(mask, step, 0, LANES);
+      }
+      for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+        float gs[VEC];
+        if constexpr (VEC == 4) {
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(acc + e));
+          gs[0] = v.x; gs[1] = v.y; gs[2] = v.z; gs[3] = v.w;
+        } else {
+          gs[0] = __ldcg(acc + e);
+        }
+        // the sum is fp32; the ordered mode's is rounded to the gradient
+        // dtype after every add
+        apply_chunk<VEC, kDyn>(L, slab, o, step, e, gs);
+      }
+    }
+    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+      if constexpr (VEC == 4) *reinterpret_cast<float4 *>(acc + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+      else acc[e] = 0.0f;
+    }
+    if (lane == 0) {
+      a.cnt[slot] = 0u;
+      if (slot != G) a.keys[slot] = kEmptyKey;
+    }
+  }
+  // every block has read the claim counter: the last one resets it
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(a.ctr + 2, 1u) == gridDim.x - 1) {
+    a.ctr[0] = 0u;
+    a.ctr[1] = 0u;
+    a.ctr[2] = 0u;
+  }
+}
+
 // Rebuild into a larger directory.
 __global__ void k_rehash(const Bucket *__restrict__ old_b, uint64_t old_n, Dir nd, uint32_t *status) {
   const uint64_t slot = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -1570,6 +1638,16 @@ struct Table {
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
   uint64_t seg_fill_zeroed = 0;  // entries of g_seg_fill known to be zero
+  // atomic accumulation mode (se_accum.cuh): per-key fp32 sums of the window
+  bool atomic = false;
+  uint32_t acc_tile = 0, acc_hbits = 0;  // rows per block of k_acc_atomic, its hash-set bits
+  uint64_t acc_slots = 0;                // G (0: not allocated yet)
+  unsigned long long *acc_keys = nullptr;
+  float *acc_vals = nullptr;
+  uint32_t *acc_cnt = nullptr, *acc_list = nullptr, *acc_ctr = nullptr;
+  AccTab acc_tab() const {
+    return AccTab{acc_keys, acc_vals, acc_cnt, acc_list, acc_ctr, uint32_t(acc_slots - 1), uint32_t(dim)};
+  }
 
   Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
   RowAlloc alloc() const {
@@ -1588,6 +1666,11 @@ struct Table {
     dfree(free_rows);
     dfree(seg_row);
     dfree(unres);
+    dfree(acc_keys);
+    dfree(acc_vals);
+    dfree(acc_cnt);
+    dfree(acc_list);
+    dfree(acc_ctr);
   }
   CountWs count_ws() const {
     return CountWs{row_cnt, row_seg, seg_row, ctr + kCtrGroup, unres, ctr + kCtrUnres};
@@ -1714,6 +1797,15 @@ struct StoreImpl {
     }
     t.vec = dim % 4 == 0 ? 4 : 1;
     t.lanes = pick_lanes(uint64_t(dim) / uint64_t(t.vec));
+    // atomic mode: k_acc_atomic keeps a tile's sums in 32 KB of shared memory
+    t.atomic = cfg.accumulation == SE_ACCUM_ATOMIC && dim <= int64_t(kAccMaxDim);
+    if (t.atomic) {
+      uint32_t tile = 1;
+      while (tile < kAccMaxTile && uint64_t(tile) * 2 * uint64_t(dim) * 4 <= kAccSmemBytes) tile <<= 1;
+      t.acc_tile = tile;
+      t.acc_hbits = 1;
+      while ((1u << t.acc_hbits) < 2 * tile) ++t.acc_hbits;
+    }
     t.ctr = dalloc<uint32_t>(kCtrWords);
     cuda_check(cudaMemset(t.ctr, 0, kCtrWords * 4), "memset counters");
     cuda_check(cudaMemset(t.ctr + kCtrSpecialRow, 0xff, 4), "memset special");
@@ -1862,6 +1954,45 @@ struct StoreImpl {
     t.seg_row = nsr;
     t.unres = nu;
     t.pcap = ncap;
+  }
+
+  // Atomic mode: room in the sum table for `extra` more gradient rows of the
+  // window (at most half the slots in use). A larger table takes the claimed
+  // slots over (k_acc_move); under stream capture nothing can grow.
+  void ensure_acc(Table &t, uint64_t extra, cudaStream_t st) {
+    const uint64_t need = 2 * (t.pcount + extra);
+    if (need <= t.acc_slots) return;
+    if (capturing(st))
+      throw Error(SE_ERR_RUNTIME, "gradient window captured in a CUDA graph outgrows its sum table; run one "
+                                  "step of the same size before capturing");
+    if (need > (1ull << 31)) throw Error(SE_ERR_RUNTIME, "more than 2^30 gradient rows in one window");
+    const uint64_t G = next_pow2(std::max<uint64_t>(need, 1024));
+    auto *nk = dalloc<unsigned long long>(G);
+    auto *nv = dalloc<float>(size_t(G + 1) * size_t(t.dim));
+    auto *nc = dalloc<uint32_t>(G + 1);
+    auto *nl = dalloc<uint32_t>(G + 1);
+    auto *nctr = dalloc<uint32_t>(4);
+    cuda_check(cudaMemsetAsync(nk, 0xff, G * 8, st), "memset sums");
+    cuda_check(cudaMemsetAsync(nv, 0, size_t(G + 1) * size_t(t.dim) * 4, st), "memset sums");
+    cuda_check(cudaMemsetAsync(nc, 0, (G + 1) * 4, st), "memset sums");
+    cuda_check(cudaMemsetAsync(nctr, 0, 16, st), "memset sums");
+    const AccTab to{nk, nv, nc, nl, nctr, uint32_t(G - 1), uint32_t(t.dim)};
+    if (t.acc_slots) {
+      k_acc_move<<<grid_for(t.acc_slots + 1, 256, 148 * 8), 256, 0, st>>>(t.acc_tab(), to, t.ctr + kCtrStatus);
+      launched("k_acc_move");
+    }
+    cuda_check(cudaStreamSynchronize(st), "sync");
+    dfree(t.acc_keys);
+    dfree(t.acc_vals);
+    dfree(t.acc_cnt);
+    dfree(t.acc_list);
+    dfree(t.acc_ctr);
+    t.acc_keys = nk;
+    t.acc_vals = nv;
+    t.acc_cnt = nc;
+    t.acc_list = nl;
+    t.acc_ctr = nctr;
+    t.acc_slots = G;
   }
 
   void ensure_bc(uint64_t steps) {
@@ -2459,6 +2590,10 @@ struct StoreImpl {
     Table &t = table(dim);
     if (n == 0) return;
     cudaStream_t st = pick(sp);
+    if (t.atomic) {
+      accumulate_atomic(t, keys, n, n_dev, grads, st, kdt, grad_row, grad_rows);
+      return;
+    }
     ensure_pending(t, n, st);
     const size_t gb = value_bytes(cfg.gradient_dtype);
     if (kdt < 0) kdt = cfg.key_dtype;
@@ -2519,6 +2654,118 @@ struct StoreImpl {
     t.pcount += n;  // upper bound of the rows pending on the device
   }
 
+  // accumulate_gradients in atomic mode: the rows are added into the
+  // window's per-key sums (k_acc_atomic). Host inputs are validated first and
+  // the call raises before anything is added; device inputs are validated on
+  // the device and a failing batch poisons the window (see accumulate_locked).
+  void accumulate_atomic(Table &t, const void *keys, size_t n, const uint32_t *n_dev, const void *grads,
+                         cudaStream_t st, int kdt, const uint32_t *grad_row, size_t grad_rows) {
+    ensure_acc(t, n, st);
+    const size_t gb = value_bytes(cfg.gradient_dtype);
+    if (kdt < 0) kdt = cfg.key_dtype;
+    const int64_t dim = t.dim;
+    const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(kdt), st);
+    const size_t grad_elems = (grad_row ? grad_rows : n) * size_t(dim);
+    const void *dgrads = stage_in(stage_vals, grads, grad_elems * gb, st);
+    const float maxv = std::min(host_dtype_max(cfg.gradient_dtype), host_dtype_max(cfg.value_dtype));
+    const bool vec4 = dim % 4 == 0 && uintptr_t(dgrads) % (cfg.gradient_dtype == SE_FLOAT32 ? 16 : 8) == 0;
+    const bool device_inputs = dkeys == keys && dgrads == grads;
+    uint32_t *status_word = t.ctr + (device_inputs ? kCtrPoison : kCtrGradStatus);
+    if (!device_inputs) {
+      cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+      {
+        Prof pr(this, "k_acc_check", st);
+        if (vec4) pdl(k_acc_check<4>, grid_for(grad_elems / 4, 256, 148 * 8), 256, 0, st, dgrads,
+                      cfg.gradient_dtype, grad_elems, cfg.gradient_scale, maxv, status_word);
+        else pdl(k_acc_check<1>, grid_for(grad_elems, 256, 148 * 8), 256, 0, st, dgrads, cfg.gradient_dtype,
+                 grad_elems, cfg.gradient_scale, maxv, status_word);
+        launched("k_acc_check");
+      }
+      cuda_check(cudaMemcpyAsync(status_host, status_word, 4, cudaMemcpyDeviceToHost, st), "status");
+      cuda_check(cudaStreamSynchronize(st), "sync");
+      if (status_host[0] & kStatusBadGradient) {
+        cuda_check(cudaMemsetAsync(status_word, 0, 4, st), "status clear");
+        cuda_check(cudaStreamSynchronize(st), "sync");
+        throw std::overflow_error("gradient scale storage exceeds configured dtype");
+      }
+    }
+    {
+      Prof pr(this, "k_acc_atomic", st);
+      const unsigned grid = grid_for(n, t.acc_tile, 0x7fffffffu);
+      const size_t smem = size_t(t.acc_tile) * size_t(dim) * 4;
+      auto go = [&](auto kern) {
+        pdl(kern, grid, kAccThreads, smem, st, t.acc_tab(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
+            cfg.gradient_scale, maxv, t.acc_tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row);
+      };
+      if (grad_row) {
+        if (vec4) go(k_acc_atomic<4, true>);
+        else go(k_acc_atomic<1, true>);
+      } else {
+        if (vec4) go(k_acc_atomic<4, false>);
+        else go(k_acc_atomic<1, false>);
+      }
+      launched("k_acc_atomic");
+    }
+    if (!device_inputs) cuda_check(cudaStreamSynchronize(st), "sync");  // staging buffers are reused
+    t.pcount += n;  // upper bound of the window's distinct keys
+  }
+
+  // optimizer_step of an atomic-mode table (apply = 0: the window is only cleared).
+  void step_atomic(Table &t, size_t nsteps, bool apply, cudaStream_t st) {
+    OptSpec o = opt_spec(t, nsteps);
+    // the sums are fp32: used as they are only for fp32 parameters and factor 1
+    o.raw = cfg.value_dtype == SE_FLOAT32 && nsteps == 1 && cfg.gradient_scale == 1.0f;
+    auto *dropped = reinterpret_cast<unsigned long long *>(t.ctr + kCtrDropped);
+    const uint64_t slots = std::min<uint64_t>(t.pcount, t.acc_slots + 1);
+    auto go = [&](auto lanes_tag, auto vec_tag) {
+      constexpr int LN = decltype(lanes_tag)::value;
+      constexpr int VC = decltype(vec_tag)::value;
+      const unsigned grid = grid_for(slots * LN, 256, 148 * 16);
+      Prof pr(this, "k_acc_apply", st);
+      if (cfg.lr_policy != SE_LR_CONSTANT)
+        pdl(k_acc_apply<LN, VC, true>, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0,
+            dropped);
+      else
+        pdl(k_acc_apply<LN, VC, false>, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0,
+            dropped);
+      launched("k_acc_apply");
+    };
+    auto by_lanes = [&](auto vec_tag) {
+      const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
+      switch (ln) {
+      case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
+      case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
+      case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
+      default: go(std::integral_constant<int, 32>{}, vec_tag); break;
+      }
+    };
+    if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
+    else by_lanes(std::integral_constant<int, 1>{});
+  }
+
+  OptSpec opt_spec(const Table &t, size_t nsteps) const {
+    OptSpec o{};
+    o.kind = cfg.optimizer_kind;
+    o.lr = cfg.lr;
+    o.b1 = cfg.beta1;
+    o.b2 = cfg.beta2;
+    o.eps = cfg.eps;
+    o.wd = cfg.weight_decay;
+    o.omb1 = 1.0f - cfg.beta1;
+    o.omb2 = 1.0f - cfg.beta2;
+    const uint32_t wdt = uint32_t(cfg.simd_width > 0 ? cfg.simd_width : 1);
+    o.simd_cut = (uint32_t(t.dim) / wdt) * wdt;
+    o.bc = bc;
+    o.factor = cfg.gradient_scale / float(nsteps);
+    o.raw = cfg.gradient_dtype == cfg.value_dtype && nsteps == 1 && cfg.gradient_scale == 1.0f;
+    o.poison = t.ctr + kCtrPoison;
+    o.lr_kind = cfg.lr_policy;
+    o.lr_min_ratio = cfg.lr_min_ratio;
+    o.lr_max_score = lr_max;
+    o.lr_lut = lr_lut;
+    return o;
+  }
+
   void optimizer_step(size_t nsteps, void *sp) {
     std::lock_guard<std::mutex> lock(mu);
     DeviceGuard dg(device);
@@ -2530,7 +2777,9 @@ struct StoreImpl {
     for (auto &tp : tables) {
       Table &t = *tp;
       if (t.pcount == 0) continue;
-      if (apply) {
+      if (t.atomic) {
+        step_atomic(t, nsteps, apply, st);
+      } else if (apply) {
         step_table(t, nsteps, st);  // its last kernel clears the window's counters
       } else {
         cuda_check(cudaMemsetAsync(t.ctr + kCtrGroup, 0, 16, st), "memset group counters");
@@ -2622,25 +2871,7 @@ struct StoreImpl {
       pdl(k_group_place, g, 256, 0, st, t.ctr + kCtrPending, w);
       launched("k_group_place");
     }
-    OptSpec o{};
-    o.kind = cfg.optimizer_kind;
-    o.lr = cfg.lr;
-    o.b1 = cfg.beta1;
-    o.b2 = cfg.beta2;
-    o.eps = cfg.eps;
-    o.wd = cfg.weight_decay;
-    o.omb1 = 1.0f - cfg.beta1;
-    o.omb2 = 1.0f - cfg.beta2;
-    const uint32_t wdt = uint32_t(cfg.simd_width > 0 ? cfg.simd_width : 1);
-    o.simd_cut = (uint32_t(t.dim) / wdt) * wdt;
-    o.bc = bc;
-    o.factor = cfg.gradient_scale / float(nsteps);
-    o.raw = cfg.gradient_dtype == cfg.value_dtype && nsteps == 1 && cfg.gradient_scale == 1.0f;
-    o.poison = t.ctr + kCtrPoison;
-    o.lr_kind = cfg.lr_policy;
-    o.lr_min_ratio = cfg.lr_min_ratio;
-    o.lr_max_score = lr_max;
-    o.lr_lut = lr_lut;
+    const OptSpec o = opt_spec(t, nsteps);
     const int gdt = cfg.gradient_dtype;
     auto go = [&](auto lanes_tag, auto vec_tag) {
       constexpr int LN = decltype(lanes_tag)::value;
@@ -2673,6 +2904,37 @@ struct StoreImpl {
     };
     if (t.vec == 4) by_lanes(std::integral_constant<int, 4>{});
     else by_lanes(std::integral_constant<int, 1>{});
+  }
+
+  // clear (hogwild_embedding_store.hpp:5107-5154): every key of every table
+  // is removed, the arenas are reset and the gradients of the current window
+  // are discarded; capacity is kept. The store-wide LRU clock keeps running,
+  // as the reference's score policy does.
+  void clear(void *sp) {
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceGuard dg(device);
+    cudaStream_t st = pick(sp);
+    for (auto &tp : tables) {
+      Table &t = *tp;
+      cuda_check(cudaMemsetAsync(t.buckets, 0xff, t.nbuckets * sizeof(Bucket), st), "clear directory");
+      cuda_check(cudaMemsetAsync(t.ctr, 0, kCtrWords * 4, st), "clear counters");
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrSpecialRow, 0xff, 4, st), "clear special");
+      cuda_check(cudaMemsetAsync(t.row_cnt, 0, t.capacity * 4, st), "clear row counters");
+      if (t.acc_slots) {
+        cuda_check(cudaMemsetAsync(t.acc_keys, 0xff, t.acc_slots * 8, st), "clear sums");
+        cuda_check(cudaMemsetAsync(t.acc_vals, 0, size_t(t.acc_slots + 1) * size_t(t.dim) * 4, st), "clear sums");
+        cuda_check(cudaMemsetAsync(t.acc_cnt, 0, (t.acc_slots + 1) * 4, st), "clear sums");
+        cuda_check(cudaMemsetAsync(t.acc_ctr, 0, 16, st), "clear sums");
+      }
+      t.pcount = 0;
+      t.rows_bound = 0;
+      t.bound_stale = false;
+      t.tombs = 0;
+      t.erased = false;
+      t.exp_count = 0;
+      t.exp_taken = false;
+    }
+    cuda_check(cudaStreamSynchronize(st), "sync");
   }
 
   void read_state(int64_t dim, uint64_t key, void *param_out, void *state_out, uint32_t *step_out,
@@ -3100,6 +3362,8 @@ int se_store_create(const se_store_config *config, se_store **out_store) {
       if (dt < SE_FLOAT32 || dt > SE_BFLOAT16) throw std::invalid_argument("unsupported value dtype");
     if (!std::isfinite(c.gradient_scale) || c.gradient_scale <= 0.0f)
       throw std::invalid_argument("gradient_scale must be finite and greater than zero");
+    if (c.accumulation != SE_ACCUM_ORDERED && c.accumulation != SE_ACCUM_ATOMIC)
+      throw std::invalid_argument("accumulation must be 'ordered' or 'atomic'");
     auto s = std::make_unique<se_store>();
     StoreImpl &st = s->impl;
     st.cfg = c;
@@ -3326,6 +3590,10 @@ int se_store_dropped_gradients(se_store *store, uint64_t *out) {
 int se_store_read_state(se_store *store, int64_t dim, uint64_t key, void *param_out, void *state_out,
                         uint32_t *step_out, int32_t *found) {
   return guarded([&] { checked(store)->impl.read_state(dim, key, param_out, state_out, step_out, found); });
+}
+
+int se_store_clear(se_store *store, void *stream) {
+  return guarded([&] { checked(store)->impl.clear(stream); });
 }
 
 int se_store_synchronize(se_store *store) {

@@ -110,6 +110,7 @@ class EmbeddingConfig:
         device: int | None = None,
         initial_capacity: int = 0,
         simd_width: int = 16,
+        accumulation: str = "ordered",
     ):
         self.dims = [int(d) for d in dims]
         self.thread_budget = int(thread_budget)
@@ -124,6 +125,11 @@ class EmbeddingConfig:
         self.device = device
         self.initial_capacity = int(initial_capacity)
         self.simd_width = int(simd_width)
+        # How gradients are summed until optimizer_step (GPU store only):
+        # "ordered" keeps every row and sums each key's rows in arrival order
+        # (the reference's order); "atomic" adds them into per-key fp32 sums as
+        # they arrive (vector reductions; the order of the adds varies).
+        self.accumulation = str(accumulation)
 
 
 class Initializer:
@@ -317,6 +323,9 @@ class EmbeddingStore:
             raise ValueError("dynamic learning-rate policy requires a score policy")
         if not math.isfinite(cfg.gradient_scale) or cfg.gradient_scale <= 0.0:
             raise ValueError("gradient_scale must be finite and greater than zero")
+        accumulation = getattr(cfg, "accumulation", "ordered")
+        if accumulation not in N.ACCUM_CODES:
+            raise ValueError("accumulation must be 'ordered' or 'atomic'")
         self._config = cfg
         self._key_dtype = key_dtype
         self._value_dtype = value_dtype
@@ -355,6 +364,7 @@ class EmbeddingStore:
         c.simd_width = cfg.simd_width
         c.internal_shards = self._thread_budget
         c.score_policy = {"none": 0, "lfu": 1, "lru": 2, "manual": 3}[score_policy]
+        c.accumulation = N.ACCUM_CODES[accumulation]
         lut = None
         if policy is not None:
             c.lr_policy = policy.code
@@ -371,6 +381,9 @@ class EmbeddingStore:
         self._h = h
 
     def __del__(self):
+        pool = getattr(self, "_async_pool", None)
+        if pool is not None:
+            pool.shutdown(wait=True)
         h = getattr(self, "_h", None)
         if h is not None and h.value:
             try:
@@ -603,6 +616,81 @@ class EmbeddingStore:
             stream = self._current_stream()
         N.check(self._lib.se_optimizer_step(self._h, int(normalization_steps),
                                             C.c_void_p(stream) if stream else None))
+
+    def clear(self) -> None:
+        """Removes every key and discards the gradients accumulated since the
+        last optimizer_step (EmbeddingStoreWrapper::clear,
+        module_wrapper_methods.inl:212-216); reserved capacity is kept."""
+        self._check_operational()
+        stream = self._current_stream()
+        N.check(self._lib.se_store_clear(self._h, C.c_void_p(stream) if stream else None))
+
+    # ---- asyncio variants (module.cpp:648-684) --------------------------------
+    # Each returns an asyncio future of the running loop (the reference's
+    # create_asyncio_future, bindings/async_bridge.hpp:74-87). The call runs on
+    # the store's worker thread on the caller's CUDA stream; the future
+    # completes with the synchronous method's result once the device work of
+    # the call has finished, or with its exception. Argument checks that the
+    # reference makes before dispatching raise immediately.
+
+    def _async(self, fn, *args):
+        import asyncio
+        from concurrent.futures import ThreadPoolExecutor
+
+        loop = asyncio.get_running_loop()
+        if getattr(self, "_async_pool", None) is None:
+            self._async_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="se-async")
+        from ._tensors import _TORCH
+
+        stream = None
+        if _TORCH is not None and _TORCH.cuda.is_available() and _TORCH.cuda.is_initialized():
+            stream = _TORCH.cuda.current_stream(self._device)
+
+        def work():
+            if stream is None:
+                out = fn(*args)
+            else:
+                with _TORCH.cuda.stream(stream):
+                    out = fn(*args)
+            self.synchronize()  # the call's device work is done; deferred errors raise here
+            return out
+
+        return loop.run_in_executor(self._async_pool, work)
+
+    def async_lookup(self, keys, dim: int):
+        if int(dim) <= 0:
+            raise ValueError("dim must be > 0")
+        return self._async(self.lookup, keys, dim)
+
+    def async_lookup_or_insert(self, keys, dim: int):
+        if int(dim) <= 0:
+            raise ValueError("dim must be > 0")
+        return self._async(self.lookup_or_insert, keys, dim)
+
+    def async_assign(self, keys, values):
+        return self._async(self.assign, keys, values)
+
+    def async_accumulate_gradients(self, keys, grads):
+        if not self._optimizer_enabled:
+            raise RuntimeError("async_accumulate_gradients requires optimizer enabled")
+        return self._async(self.accumulate_gradients, keys, grads)
+
+    def async_optimizer_step(self, normalization_steps: int):
+        if not self._optimizer_enabled:
+            raise RuntimeError("async_optimizer_step requires optimizer enabled")
+        return self._async(self.optimizer_step, normalization_steps)
+
+    def async_contains(self, keys):
+        return self._async(self.contains, keys)
+
+    def async_erase(self, keys):
+        return self._async(self.erase, keys)
+
+    def async_clear(self):
+        return self._async(self.clear)
+
+    def async_assign_scores(self, keys, scores):
+        return self._async(self.assign_scores, keys, scores)
 
     def _current_stream(self) -> int | None:
         from ._tensors import _TORCH

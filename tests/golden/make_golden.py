@@ -1,6 +1,7 @@
 """Generates the golden fixtures in this folder from the reference itself.
 
-Run in a checkout that has the reference sources (default /root/reference) and
+Run in a checkout that has the reference sources (default: the checkout named
+"reference" beside this repository) and
 the reference shim built (`make -C oracle ref`, which compiles the reference's
 own ops/partitioner.hpp and simd/*_ops.hpp in place):
 
@@ -115,4 +116,4 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else str(HERE.parents[2] / "reference"))
