@@ -48,9 +48,9 @@ FALLBACK_HBM_GBS = 6650.0
 # Kernels of one train step (lookup_or_insert -> accumulate_gradients ->
 # optimizer_step), by accumulation mode.
 STEP_KERNELS = {
-    "ordered": ["k_lookup_or_insert", "k_deferred", "k_accumulate", "k_group_fix", "k_group_alloc",
+    "ordered": ["k_lookup_or_insert", "k_accumulate", "k_group_fix", "k_group_alloc",
                 "k_group_place", "k_group_apply", "k_group_hot"],
-    "atomic": ["k_lookup_or_insert", "k_deferred", "k_acc_atomic", "k_acc_apply"],
+    "atomic": ["k_lookup_or_insert", "k_acc_atomic", "k_acc_apply"],
 }
 # value = train-step keys/s; the forward-lookup figure rides in "forward_lookup".
 METRIC = "forward_lookup Mkeys/s & train-step keys/s at 1/2/4/8 B200; % of HBM peak"
@@ -491,13 +491,9 @@ def run_ours(args):
         "value": value, "unit": "keys/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "single-table train step: dim 64 fp32, 10M warmed int64 keys, 65,536-key "
-                               "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
-                               "eps 1e-8, init_acc 0.1), hash partitioner",
-                   "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
-                   "accumulation": args.accumulation,
-                   "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none")),
-                   "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"},
+        "config": train_config(args, world),
+        "execution": {"accumulation": args.accumulation,
+                      "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none"))},
         "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
                    else "eager API calls"),
         "profiled_pass_ms_per_step": elapsed_prof / K * 1e3,
@@ -854,14 +850,42 @@ def cpu_train(num_keys: int, steps: int, seconds: float, threads: int, warmup: i
     return BATCH * done / el, done
 
 
+def cpu_info(threads: int) -> dict:
+    """The host CPU the baseline ran on: model name, widest vector ISA it
+    offers, logical CPUs available to this process, threads used."""
+    model, flags = "unknown", set()
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name") and model == "unknown":
+                model = line.split(":", 1)[1].strip()
+            elif line.startswith("flags") and not flags:
+                flags = set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    isa = "AVX-512" if "avx512f" in flags else ("AVX2" if "avx2" in flags else "SSE")
+    return {"cpu_model": model, "cpu_isa": isa, "logical_cpus": len(os.sched_getaffinity(0)),
+            "threads_used": threads,
+            "code": "oracle port of the reference store flow, g++ -O2 -march=x86-64-v3 (AVX2 level), "
+                    "-ffp-contract=off; the reference's own compiled kernels pin its results in the tests"}
+
+
 def cpu_baseline(seconds: float):
     from oracle import oracle as O
 
     threads = O.cpu_count()
     value, done = cpu_train(NUM_KEYS, 50, seconds, threads)
-    return {"value": value, "unit": "keys/s", "cores": threads, "kind": "port",
+    return {"value": value, "unit": "keys/s", "cores": threads, "kind": "port", **cpu_info(threads),
             "sample": f"{done} train steps of 65,536 keys on the 10M-key dim-64 Adagrad table (oracle port, "
                       f"{threads} threads; insert-on-miss single-threaded as in the reference)"}
+
+
+def train_config(args, world: int) -> dict:
+    """The workload both arms run (the GPU arm adds its execution keys)."""
+    return {"workload": "single-table train step: dim 64 fp32, 10M warmed int64 keys, 65,536-key "
+                        "batches per GPU Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad(lr 0.01, "
+                        "eps 1e-8, init_acc 0.1), hash partitioner",
+            "num_keys": args.num_keys, "dim": DIM, "batch_per_gpu": BATCH, "parallelism": f"key-sharded x{world}",
+            "l2": "inputs larger than L2: 5.1 GB table, fresh batch each step"}
 
 
 def run_reference(args):
@@ -876,9 +900,8 @@ def run_reference(args):
     return {"impl": "reference", "metric": METRIC, "value": value, "unit": "keys/s", "n_gpus": args.gpus, "steps": done,
             "warmup": max(1, W), "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "single-table train step: dim 64 fp32, 10M warmed int64 keys, 65,536-key "
-                                   "batches Zipf(1.05) + 5% new keys, grads N(0,1e-3), Adagrad", "num_keys": args.num_keys},
-            "cpu_baseline": {"value": value, "unit": "keys/s", "cores": threads, "kind": "port",
+            "config": train_config(args, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "keys/s", "cores": threads, "kind": "port", **cpu_info(threads),
                              "sample": f"{done} steps of 65,536 keys (oracle port of the reference store flow; "
                                        "the reference store itself does not build here)"},
             "e2e": {"value": value, "unit": "keys/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

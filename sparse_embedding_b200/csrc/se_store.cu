@@ -139,89 +139,129 @@ __device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const 
   if (L.score != 0u && lane == 0) *reinterpret_cast<unsigned long long *>(slab + L.score) = 0ull;  // a new row's score
 }
 
+// Where lookup_or_insert leaves the batch's keys and rows for an
+// accumulate_gradients of the same keys that follows (ordered mode): the
+// accumulate takes row i from here when keys[i] equals keys[i] of the
+// lookup, instead of probing the directory again. *n is the batch size of
+// the last lookup_or_insert (0: nothing cached; an erase clears it).
+struct FwdCache {
+  unsigned long long *keys;  // null: nothing is cached by this launch
+  uint32_t *rows;
+  uint32_t *n;               // null: the cache is not kept at all (atomic mode)
+  uint32_t cap;              // entries keys / rows hold
+};
+
+// The last block of k_lookup_or_insert: copies the published rows of the
+// positions whose key another group of the launch claimed (row bytes as
+// 32-bit words, or 16-bit for odd half-precision rows; they are few), then
+// resets the launch's counters. Out of line, so the main path keeps its
+// register budget.
+__device__ __noinline__ void finish_deferred(const Layout &L, const uint8_t *slabs, size_t n, void *out,
+                                             uint32_t *def_count, const uint32_t *def_pos,
+                                             const unsigned long long *def_word, uint32_t *status, uint32_t *done,
+                                             const FwdCache &fc) {
+  __threadfence();
+  const size_t row_bytes = size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
+  const bool cache = fc.keys != nullptr && n <= fc.cap;
+  const uint32_t count = __ldcg(def_count);
+  const bool words = row_bytes % 4 == 0;
+  const uint32_t units = uint32_t(words ? row_bytes / 4 : row_bytes / 2);
+  for (uint32_t j = threadIdx.x / 32; j < count; j += blockDim.x / 32) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const size_t pos = __ldcg(def_pos + j);
+    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(__ldcg(def_word + j)));
+    uint8_t *dst = static_cast<uint8_t *>(out) + pos * row_bytes;
+    if (cache && lane == 0) fc.rows[pos] = row;
+    if (row == kNoRow && lane == 0) raise_status(status, kStatusTableFull);
+    const uint8_t *src = slabs + size_t(row) * L.stride;
+    for (uint32_t u = lane; u < units; u += 32) {
+      if (words) reinterpret_cast<uint32_t *>(dst)[u] = row == kNoRow ? 0u : __ldcg(reinterpret_cast<const uint32_t *>(src) + u);
+      else reinterpret_cast<uint16_t *>(dst)[u] = row == kNoRow ? uint16_t(0) : reinterpret_cast<const uint16_t *>(src)[u];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *def_count = 0u;  // for the next launch
+    *done = 0u;
+    if (fc.n) *fc.n = cache ? uint32_t(n) : 0u;
+  }
+}
+
 // lookup_or_insert (hogwild_embedding_store.hpp:4925-4980 ->
 // SlotStore::find_or_insert_batch 3057-3353). One claimant per absent key
 // initialises and publishes its row; other positions of the same key found
-// the claim before the row was published and are finished by k_deferred.
+// the claim before the row was published, are listed, and are finished by
+// the launch's last block once every claimant has published.
 template <int LANES, int VEC>
 __global__ void __launch_bounds__(256)
 k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init, const void *__restrict__ keys, int kdt,
                    size_t n, void *__restrict__ out, uint32_t *def_count, uint32_t *def_pos,
-                   unsigned long long *def_word, uint32_t *status) {
+                   unsigned long long *def_word, uint32_t *status, uint32_t *done, FwdCache fc) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t i = t / LANES;
   const uint32_t lane = uint32_t(t % LANES);
-  if (i >= n) return;
   const unsigned mask = group_mask<LANES>();
-  const uint64_t key = load_key(keys, kdt, i);
-  int kind = kFound;
-  uint32_t row = kNoRow;
-  uint32_t *word = nullptr;
-  if (lane == 0) {
-    const InsertResult r = dir_find_or_insert(d, key);
-    kind = r.kind;
-    word = r.row_word;
-    // found: published, claimed in this launch (3), or erased and revived here
-    if (kind == kFound) kind = resolve_found(word, &row);
-    else if (kind == kFull) raise_status(status, kStatusTableFull);
-  }
-  const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
-  if (lane == 0 && kind == kInserted) {
-    row = taken;
-    if (row >= ra.capacity) {
-      raise_status(status, kStatusTableFull);
-      kind = kFull;
-    }
-  }
-  kind = __shfl_sync(mask, kind, 0, LANES);
-  row = __shfl_sync(mask, row, 0, LANES);
-  void *out_row = static_cast<uint8_t *>(out) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
-  if (kind == kFound) {
-    const uint8_t *slab = slabs + size_t(row) * L.stride;
-    copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
-  } else if (kind == kInserted) {
-    uint8_t *slab = slabs + size_t(row) * L.stride;
-    init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
-    __threadfence();  // every lane's slab writes are visible device-wide ...
-    __syncwarp(mask);
-    if (lane == 0) atomicExch(word, row);  // ... before the row is published
-  } else if (kind == 3) {
+  const size_t row_bytes = size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
+  const bool cache = fc.keys != nullptr && n <= fc.cap;
+  if (i < n) {
+    const uint64_t key = load_key(keys, kdt, i);
+    int kind = kFound;
+    uint32_t row = kNoRow;
+    uint32_t *word = nullptr;
     if (lane == 0) {
-      const uint32_t j = atomicAdd(def_count, 1u);
-      def_pos[j] = uint32_t(i);
-      def_word[j] = reinterpret_cast<unsigned long long>(word);
+      const InsertResult r = dir_find_or_insert(d, key);
+      kind = r.kind;
+      word = r.row_word;
+      // found: published, claimed in this launch (3), or erased and revived here
+      if (kind == kFound) kind = resolve_found(word, &row);
+      else if (kind == kFull) raise_status(status, kStatusTableFull);
     }
-  } else {
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
-  }
-}
-
-// Positions whose key was claimed by another group in the same launch.
-template <int LANES, int VEC>
-__global__ void __launch_bounds__(256)
-k_deferred(Layout L, const uint8_t *__restrict__ slabs, const uint32_t *def_count,
-           const uint32_t *def_pos, const unsigned long long *def_word, void *__restrict__ out,
-           uint32_t *status) {
-  pdl_wait();
-  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
-  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
-  const uint32_t lane = uint32_t(t % LANES);
-  const uint32_t count = *def_count;
-  for (size_t j = t / LANES; j < count; j += groups) {
-    const size_t i = def_pos[j];
-    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
-    void *out_row = static_cast<uint8_t *>(out) + i * size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
-    if (row == kNoRow) {
-      if (lane == 0) raise_status(status, kStatusTableFull);
+    const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
+    if (lane == 0 && kind == kInserted) {
+      row = taken;
+      if (row >= ra.capacity) {
+        raise_status(status, kStatusTableFull);
+        kind = kFull;
+      }
+    }
+    kind = __shfl_sync(mask, kind, 0, LANES);
+    row = __shfl_sync(mask, row, 0, LANES);
+    void *out_row = static_cast<uint8_t *>(out) + i * row_bytes;
+    if (cache && lane == 0) {
+      fc.keys[i] = key;
+      fc.rows[i] = (kind == kFound || kind == kInserted) ? row : kNoRow;  // deferred: filled below
+    }
+    if (kind == kFound) {
+      const uint8_t *slab = slabs + size_t(row) * L.stride;
+      copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
+    } else if (kind == kInserted) {
+      uint8_t *slab = slabs + size_t(row) * L.stride;
+      init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
+      __threadfence();  // every lane's slab writes are visible device-wide ...
+      __syncwarp(mask);
+      if (lane == 0) atomicExch(word, row);  // ... before the row is published
+    } else if (kind == 3) {
+      if (lane == 0) {
+        const uint32_t j = atomicAdd(def_count, 1u);
+        def_pos[j] = uint32_t(i);
+        def_word[j] = reinterpret_cast<unsigned long long>(word);
+      }
+    } else {
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
-      continue;
     }
-    const uint8_t *slab = slabs + size_t(row) * L.stride;
-    copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
   }
+  // The last block to finish serves the positions whose key another group
+  // claimed: every claimant has published its row (fence, then the count).
+  __shared__ bool s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) finish_deferred(L, slabs, n, out, def_count, def_pos, def_word, status, done, fc);
 }
 
 // Per-row counting of the pending entries for optimizer_step's grouping,
@@ -283,7 +323,7 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,
              void *__restrict__ pgrads_base, size_t pcap, uint32_t *pending, uint32_t *done, uint32_t *status,
              uint32_t *err, CountWs cw, int count_rows, const uint32_t *__restrict__ known_rows,
-             const uint32_t *__restrict__ grad_row) {
+             const uint32_t *__restrict__ grad_row, FwdCache fc) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t stride = size_t(gridDim.x) * blockDim.x;
@@ -301,6 +341,8 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
   }
   unsigned long long *pkeys = pkeys_base + base;
   uint32_t *prows = prows_base + base;
+  // rows the last lookup_or_insert resolved for the same keys at the same positions
+  const size_t cached = fc.n ? min(size_t(__ldcg(fc.n)), size_t(fc.cap)) : 0;
   void *pgrads = static_cast<uint8_t *>(pgrads_base) + size_t(base) * dim * (gdt == SE_FLOAT32 ? 4 : 2);
   // Keys and their rows (the directory probe overlaps the gradient copy; a
   // key absent now is probed again by optimizer_step). With count_rows the
@@ -312,8 +354,15 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
     if (valid) {
       const uint64_t key = load_key(keys, kdt, i);
       pkeys[i] = key;
-      // rows an exchange's owner kernel already resolved for these keys
-      row = known_rows ? known_rows[i] : dir_find<false>(d, key);
+      // rows an exchange's owner kernel already resolved for these keys, or
+      // the last lookup_or_insert of the same keys; else a probe
+      if (known_rows) {
+        row = known_rows[i];
+      } else {
+        row = kNoRow;
+        if (i < cached && __ldcg(fc.keys + i) == key) row = __ldcg(fc.rows + i);
+        if (row == kNoRow) row = dir_find<false>(d, key);
+      }
       prows[i] = row;
     }
     if (count_rows) count_entries(cw, valid, row, base + uint32_t(i));
@@ -953,10 +1002,14 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
 // ordered mode's reduced gradient (apply_chunk). Every slot is then freed
 // for the next window: sum zeroed, count and key cleared; the last block
 // resets the claim counters.
-template <int LANES, int VEC, bool kDyn>
+// OPT: the optimizer kind, fixed at compile time so the registers of the
+// loads in flight are those of one optimizer's state.
+template <int LANES, int VEC, bool kDyn, int OPT>
 __global__ void __launch_bounds__(256)
-k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o, int apply,
+k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in, int apply,
             unsigned long long *dropped) {
+  OptSpec o = o_in;
+  o.kind = OPT;
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const uint32_t G = a.mask + 1u;
@@ -981,17 +1034,31 @@ k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o, i
         if (lane == 0) step = next_step(L, slab);
         step = __shfl_sync(mask, step, 0, LANES);
       }
-      for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
-        float gs[VEC];
-        if constexpr (VEC == 4) {
-          const float4 v = __ldcg(reinterpret_cast<const float4 *>(acc + e));
-          gs[0] = v.x; gs[1] = v.y; gs[2] = v.z; gs[3] = v.w;
-        } else {
-          gs[0] = __ldcg(acc + e);
+      // kChunks chunks per lane and pass: every load of the pass (sum,
+      // parameters, state) is in flight before the first update
+      constexpr int kChunks = 4;
+      for (uint32_t e0 = lane * VEC; e0 < L.dim; e0 += LANES * VEC * kChunks) {
+        float gs[kChunks][VEC];
+        RowState<VEC> rs[kChunks];
+#pragma unroll
+        for (int k = 0; k < kChunks; ++k) {
+          const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
+          if (e >= L.dim) continue;
+          if constexpr (VEC == 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(acc + e));
+            gs[k][0] = v.x; gs[k][1] = v.y; gs[k][2] = v.z; gs[k][3] = v.w;
+          } else {
+            gs[k][0] = __ldcg(acc + e);
+          }
+          load_state<VEC>(L, slab, o, e, rs[k]);
         }
         // the sum is fp32; the ordered mode's is rounded to the gradient
         // dtype after every add
-        apply_chunk<VEC, kDyn>(L, slab, o, step, e, gs);
+#pragma unroll
+        for (int k = 0; k < kChunks; ++k) {
+          const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
+          if (e < L.dim) apply_loaded<VEC, kDyn>(L, slab, o, step, e, gs[k], rs[k]);
+        }
       }
     }
     for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
@@ -1594,7 +1661,10 @@ enum Ctr : int {
   kCtrUnres = 16,      // pending entries whose key was absent when appended (cleared after each step)
   kCtrStepDone = 17,   // blocks of the running k_group_hot that have finished
   kCtrFreeTop = 18,    // int: rows of erased keys on the free stack (may read below zero; see take_row)
-  kCtrWords = 20,
+  kCtrFwdDone = 19,    // blocks of the running k_lookup_or_insert that have finished
+  kCtrFwdN = 20,       // keys cached by the last lookup_or_insert (FwdCache::n)
+  kCtrFwdDeferred = 21,  // k_lookup_or_insert's deferred positions (zero between launches)
+  kCtrWords = 24,
 };
 
 struct Table {
@@ -1638,6 +1708,9 @@ struct Table {
   Scratch<float> g_partials;
   Scratch<unsigned long long> def_word;
   uint64_t seg_fill_zeroed = 0;  // entries of g_seg_fill known to be zero
+  // keys and rows of the last lookup_or_insert, for the accumulate that follows (ordered mode)
+  Scratch<unsigned long long> fwd_keys;
+  Scratch<uint32_t> fwd_rows;
   // atomic accumulation mode (se_accum.cuh): per-key fp32 sums of the window
   bool atomic = false;
   uint32_t acc_tile = 0, acc_hbits = 0;  // rows per block of k_acc_atomic, its hash-set bits
@@ -2067,26 +2140,33 @@ struct StoreImpl {
       if (cfg.score_policy == SE_SCORE_LFU || cfg.score_policy == SE_SCORE_LRU) touch_scores(t, dkeys, n, st);
     } else {
       ensure_rows(t, n, st);
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
-      uint32_t *dpos = t.def_pos.get(n);
-      unsigned long long *dword = t.def_word.get(n);
+      const bool under_capture = capturing(st);
+      uint32_t *dpos = under_capture ? t.def_pos.ptr : t.def_pos.get(n);
+      unsigned long long *dword = under_capture ? t.def_word.ptr : t.def_word.get(n);
+      if (under_capture && (t.def_pos.cap < n || t.def_word.cap < n))
+        throw Error(SE_ERR_RUNTIME, "lookup_or_insert captured in a CUDA graph needs a batch of the same size "
+                                    "run once before capturing");
+      // ordered mode: keys and rows stay cached for the accumulate of the same keys
+      FwdCache fc{nullptr, nullptr, nullptr, 0};
+      if (!t.atomic) {
+        fc.n = t.ctr + kCtrFwdN;
+        if (!under_capture || (t.fwd_keys.cap >= n && t.fwd_rows.cap >= n)) {
+          fc.keys = t.fwd_keys.get(n);
+          fc.rows = t.fwd_rows.get(n);
+          fc.cap = uint32_t(std::min<size_t>(std::min(t.fwd_keys.cap, t.fwd_rows.cap), 0xffffffffu));
+        }
+      }
       InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
                     cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
       const bool vec4 = t.vec == 4 && (uintptr_t(dout) % 16 == 0);
       auto go = [&](auto lanes_tag, auto vec_tag) {
         constexpr int LN = decltype(lanes_tag)::value;
         constexpr int VC = decltype(vec_tag)::value;
-        {
-          Prof pr(this, "k_lookup_or_insert", st);
-          pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
-              t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n,
-              dout, t.ctr + kCtrDeferred, dpos, dword, t.ctr + kCtrStatus);
-          launched("k_lookup_or_insert");
-        }
-        Prof pr(this, "k_deferred", st);
-        pdl(k_deferred<LN, VC>, grid_for(n * LN, 256, 148 * 4), 256, 0, st,
-            t.L, t.slabs, t.ctr + kCtrDeferred, dpos, dword, dout, t.ctr + kCtrStatus);
-        launched("k_deferred");
+        Prof pr(this, "k_lookup_or_insert", st);
+        pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
+            t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n,
+            dout, t.ctr + kCtrFwdDeferred, dpos, dword, t.ctr + kCtrStatus, t.ctr + kCtrFwdDone, fc);
+        launched("k_lookup_or_insert");
       };
       auto by_lanes = [&](auto vec_tag) {
         const uint32_t ln = gather_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim));
@@ -2236,7 +2316,11 @@ struct StoreImpl {
       }
       t.tombs += n;
       t.erased = true;
-      if (t.pcount > 0) {
+      // an erased key's row may be reused: rows cached by the last
+      // lookup_or_insert are no longer trusted
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrFwdN, 0, 4, st), "cache clear");
+      // ordered mode: pending rows are counted again (atomic mode resolves keys at the step)
+      if (t.pcount > 0 && !t.atomic) {
         const unsigned grid = grid_for(t.pcount, 256, 148 * 8);
         k_requeue_clear<<<grid, 256, 0, st>>>(t.prows, t.ctr + kCtrPending, uint32_t(t.pcap), t.capacity,
                                               t.count_ws());
@@ -2624,7 +2708,9 @@ struct StoreImpl {
       auto go = [&](auto kern) {
         pdl(kern, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype, uint32_t(dim),
             cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads, size_t(t.pcap), t.ctr + kCtrPending,
-            t.ctr + kCtrAccDone, status_word, t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows, grad_row);
+            t.ctr + kCtrAccDone, status_word, t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows, grad_row,
+            FwdCache{t.fwd_keys.ptr, t.fwd_rows.ptr, t.fwd_keys.ptr ? t.ctr + kCtrFwdN : nullptr,
+                     uint32_t(std::min<size_t>(std::min(t.fwd_keys.cap, t.fwd_rows.cap), 0xffffffffu))});
       };
       if (grad_row) {
         if (vec4) go(k_accumulate<4, true>);
@@ -2722,16 +2808,25 @@ struct StoreImpl {
       constexpr int VC = decltype(vec_tag)::value;
       const unsigned grid = grid_for(slots * LN, 256, 148 * 16);
       Prof pr(this, "k_acc_apply", st);
-      if (cfg.lr_policy != SE_LR_CONSTANT)
-        pdl(k_acc_apply<LN, VC, true>, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0,
-            dropped);
-      else
-        pdl(k_acc_apply<LN, VC, false>, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0,
-            dropped);
+      auto launch = [&](auto kern) {
+        pdl(kern, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0, dropped);
+      };
+      const bool dyn = cfg.lr_policy != SE_LR_CONSTANT;
+      if (o.kind == SE_OPT_ADAM) {
+        if (dyn) launch(k_acc_apply<LN, VC, true, SE_OPT_ADAM>);
+        else launch(k_acc_apply<LN, VC, false, SE_OPT_ADAM>);
+      } else if (o.kind == SE_OPT_ADAGRAD) {
+        if (dyn) launch(k_acc_apply<LN, VC, true, SE_OPT_ADAGRAD>);
+        else launch(k_acc_apply<LN, VC, false, SE_OPT_ADAGRAD>);
+      } else {  // SGD, or no optimizer (the window is only cleared)
+        if (dyn) launch(k_acc_apply<LN, VC, true, SE_OPT_SGD>);
+        else launch(k_acc_apply<LN, VC, false, SE_OPT_SGD>);
+      }
       launched("k_acc_apply");
     };
     auto by_lanes = [&](auto vec_tag) {
-      const uint32_t ln = decltype(vec_tag)::value == 4 ? t.lanes : pick_lanes(uint64_t(t.dim));
+      // few lanes per slot, each with several chunks in flight: one wave of groups
+      const uint32_t ln = gather_lanes(uint64_t(t.dim) / uint64_t(decltype(vec_tag)::value));
       switch (ln) {
       case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
       case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
