@@ -92,9 +92,35 @@ __device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, 
 // dtypes (failures raise kStatusBadGradient in *bad_word), and the value
 // added is g (scale 1) or the scaled value rounded to the gradient dtype.
 // With kBag, entry i takes gradient row grad_row[i] (embedding-bag backward).
-// Dynamic shared memory: tile * dim floats.
+// Dynamic shared memory: tile * dim floats; tile * dim <= kAccSmemBytes / 4,
+// so each thread holds at most kAccRegFloats gradient values.
+//
+// Latency: the tile's gradient rows are loaded into registers at the start,
+// while the keys are hashed, and each distinct key's table slot is found
+// while the rows are added into shared memory, so the block's chain is one
+// DRAM round trip, one L2 round trip (the slot), then fire-and-forget
+// reductions.
+constexpr uint32_t kAccRegFloats = uint32_t(kAccSmemBytes / 4 / kAccThreads);  // 32
+
+// Walks chunks c = c0, c0 + step, c0 + 2 step, ... of rows of `units`
+// chunks as (row, chunk in row) without a division per step.
+struct ChunkWalk {
+  uint32_t j, u;          // row and chunk of the current c
+  uint32_t dj, du, units;  // step = dj * units + du
+  __device__ __forceinline__ ChunkWalk(uint32_t c0, uint32_t step, uint32_t units_)
+      : j(c0 / units_), u(c0 % units_), dj(step / units_), du(step % units_), units(units_) {}
+  __device__ __forceinline__ void next() {
+    j += dj;
+    u += du;
+    if (u >= units) {
+      u -= units;
+      ++j;
+    }
+  }
+};
+
 template <int VEC, bool kBag>
-__global__ void __launch_bounds__(kAccThreads)
+__global__ void __launch_bounds__(kAccThreads, 4)  // 4 blocks per SM: a 65,536-row batch in one wave
 k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, float scale, float maxv, uint32_t tile, uint32_t hbits,
              uint32_t *bad_word, uint32_t *status, const uint32_t *__restrict__ grad_row) {
@@ -107,6 +133,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
   __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base;
+  constexpr int CH = int(kAccRegFloats) / VEC;        // gradient chunks per thread
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t n = n_dev ? min(size_t(*n_dev), n_max) : n_max;
@@ -116,6 +143,19 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   const uint32_t H = 1u << hbits;  // >= 2 * tile
   const uint32_t dim = a.dim;
   const uint32_t tid = threadIdx.x;
+  const uint32_t units = dim / VEC;
+  const uint32_t chunks = m * units;  // <= CH * blockDim.x
+  // 0. the tile's gradient rows into registers (chunk c = tid + k * blockDim.x)
+  float g[CH][VEC];
+  {
+    ChunkWalk w(tid, blockDim.x, units);
+#pragma unroll
+    for (int k = 0; k < CH; ++k, w.next()) {
+      if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
+      const size_t src = kBag ? size_t(grad_row[i0 + w.j]) : i0 + w.j;
+      ldv<VEC>(grads, gdt, src * dim + w.u * VEC, g[k]);
+    }
+  }
   for (uint32_t h = tid; h < H; h += blockDim.x) s_hkey[h] = kEmptyKey;
   for (uint32_t q = tid; q < tile; q += blockDim.x) s_lcnt[q] = 0u;
   if (tid == 0) {
@@ -141,6 +181,25 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     }
     s_ent[j] = h;
   }
+  // validation and entry scaling of the registers (overlaps the hashing);
+  // g / 1 == g needs no division (uniform branch)
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
+    if (scale == 1.0f) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) bad |= !(fabsf(g[k][v]) <= maxv);
+    } else {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        const float sc = __fdiv_rn(g[k][v], scale);
+        bad |= !(fabsf(sc) <= maxv);
+        g[k][v] = round_to(gdt, sc);
+      }
+    }
+  }
+  if (bad) raise_status(bad_word, kStatusBadGradient);
   __syncthreads();
   // 2. a local index per distinct key
   for (uint32_t h = tid; h <= H; h += blockDim.x) {
@@ -158,41 +217,15 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_ent[j] = q;
     atomicAdd(&s_lcnt[q], 1u);
   }
-  for (uint32_t x = tid; x < nloc * dim; x += blockDim.x) s_acc[x] = 0.0f;
-  __syncthreads();
-  // 3. gradient rows into the shared sums (ILP loads ahead of the adds)
-  const uint32_t units = dim / VEC;
-  const uint32_t chunks = m * units;
-  bool bad = false;
-  constexpr int kIlp = 4;
-  for (uint32_t c0 = tid; c0 < chunks; c0 += blockDim.x * kIlp) {
-    float g[kIlp][VEC];
-    uint32_t dst[kIlp];
-#pragma unroll
-    for (int k = 0; k < kIlp; ++k) {
-      const uint32_t c = c0 + uint32_t(k) * blockDim.x;
-      if (c >= chunks) continue;
-      const uint32_t j = c / units;
-      const uint32_t e = (c - j * units) * VEC;
-      const size_t src = kBag ? size_t(grad_row[i0 + j]) : i0 + j;
-      ldv<VEC>(grads, gdt, src * dim + e, g[k]);
-      dst[k] = s_ent[j] * dim + e;
-    }
-#pragma unroll
-    for (int k = 0; k < kIlp; ++k) {
-      const uint32_t c = c0 + uint32_t(k) * blockDim.x;
-      if (c >= chunks) continue;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float s = __fdiv_rn(g[k][v], scale);
-        bad |= !(fabsf(s) <= maxv);
-        const float x = scale != 1.0f ? round_to(gdt, s) : g[k][v];
-        atomicAdd(&s_acc[dst[k] + v], x);
-      }
-    }
+  if constexpr (VEC == 4) {  // rows are whole float4s
+    for (uint32_t x = tid; x < nloc * units; x += blockDim.x)
+      reinterpret_cast<float4 *>(s_acc)[x] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    for (uint32_t x = tid; x < nloc * dim; x += blockDim.x) s_acc[x] = 0.0f;
   }
-  if (bad) raise_status(bad_word, kStatusBadGradient);
-  // 4. each distinct key's slot in the table
+  __syncthreads();
+  // 3. each distinct key's slot in the table (its L2 round trips overlap the
+  //    shared-memory adds of step 4)
   for (uint32_t q = tid; q < nloc; q += blockDim.x) {
     bool claimed = false;
     const uint32_t slot = acc_find_or_claim(a, s_lkey[q], claimed);
@@ -201,6 +234,17 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     if (slot == kNoRow) raise_status(status, kStatusTableFull);
     else atomicAdd(a.cnt + slot, s_lcnt[q]);
   }
+  // 4. the gradient rows into the shared sums
+  {
+    ChunkWalk w(tid, blockDim.x, units);
+#pragma unroll
+    for (int k = 0; k < CH; ++k, w.next()) {
+      if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
+      float *dst = s_acc + s_ent[w.j] * dim + w.u * VEC;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) atomicAdd(dst + v, g[k][v]);
+    }
+  }
   __syncthreads();
   if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);
   __syncthreads();
@@ -208,13 +252,13 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = s_gslot[q];
   // 5. the tile's sums into the table
   const uint32_t lchunks = nloc * units;
-  for (uint32_t c = tid; c < lchunks; c += blockDim.x) {
-    const uint32_t q = c / units;
-    const uint32_t e = (c - q * units) * VEC;
-    const uint32_t slot = s_gslot[q];
+  ChunkWalk w(tid, blockDim.x, units);
+  for (uint32_t c = tid; c < lchunks; c += blockDim.x, w.next()) {
+    const uint32_t slot = s_gslot[w.j];
     if (slot == kNoRow) continue;
+    const uint32_t e = w.u * VEC;
     float *dst = a.vals + size_t(slot) * dim + e;
-    const float *src = s_acc + q * dim + e;
+    const float *src = s_acc + w.j * dim + e;
     if constexpr (VEC == 4) red_add_v4(dst, src[0], src[1], src[2], src[3]);
     else atomicAdd(dst, src[0]);
   }

@@ -54,7 +54,7 @@ k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row
   V *dst = out + i * row_units;
   if (row != kNoRow) {
     const V *src = reinterpret_cast<const V *>(slabs + size_t(row) * stride);
-    constexpr int kIlp = 4;  // loads in flight per lane
+    constexpr int kIlp = LANES == 2 ? 8 : 4;  // loads in flight per lane
     for (uint32_t u = lane; u < row_units; u += LANES * kIlp) {
       V v[kIlp];
 #pragma unroll
@@ -235,7 +235,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, In
     }
     if (kind == kFound) {
       const uint8_t *slab = slabs + size_t(row) * L.stride;
-      copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
+      copy_row<VEC, LANES == 2 ? 8 : 4>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
     } else if (kind == kInserted) {
       uint8_t *slab = slabs + size_t(row) * L.stride;
       init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
@@ -385,11 +385,15 @@ k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const 
 #pragma unroll
     for (int k = 0; k < kIlp; ++k) {
       if (c0 + k * stride >= chunks) continue;
+      if (scale == 1.0f) {  // g / 1 == g: no division (uniform branch)
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float s = __fdiv_rn(g[k][j], scale);
-        bad |= !(fabsf(s) <= maxv);
-        if (scale != 1.0f) g[k][j] = s;
+        for (int j = 0; j < VEC; ++j) bad |= !(fabsf(g[k][j]) <= maxv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          g[k][j] = __fdiv_rn(g[k][j], scale);
+          bad |= !(fabsf(g[k][j]) <= maxv);
+        }
       }
       stv<VEC>(pgrads, gdt, (c0 + k * stride) * VEC, g[k]);
     }
@@ -1605,6 +1609,16 @@ uint32_t gather_lanes(uint64_t units) {
   return l;
 }
 
+// Lanes per key of the forward kernels (k_lookup, k_lookup_or_insert): two
+// lanes per key while each lane's share stays <= 8 units, so a 65,536-key
+// batch of 256-byte rows is 131,072 threads - one wave of resident blocks -
+// and every lane keeps its 8 loads of the row in flight together.
+uint32_t forward_lanes(uint64_t units) {
+  uint32_t l = 2;
+  while (l < 32 && uint64_t(l) * 8 < units) l <<= 1;
+  return l;
+}
+
 uint32_t pick_lanes(uint64_t units) {
   uint32_t l = 4;
   while (l < 32 && l < units) l <<= 1;
@@ -2126,8 +2140,9 @@ struct StoreImpl {
       };
       auto by_lanes = [&](auto vtag) {
         using V = decltype(vtag);
-        const uint32_t ln = gather_lanes(row_bytes / sizeof(V));
+        const uint32_t ln = forward_lanes(row_bytes / sizeof(V));
         switch (ln) {
+        case 2: go(std::integral_constant<int, 2>{}, vtag); break;
         case 4: go(std::integral_constant<int, 4>{}, vtag); break;
         case 8: go(std::integral_constant<int, 8>{}, vtag); break;
         case 16: go(std::integral_constant<int, 16>{}, vtag); break;
@@ -2169,8 +2184,9 @@ struct StoreImpl {
         launched("k_lookup_or_insert");
       };
       auto by_lanes = [&](auto vec_tag) {
-        const uint32_t ln = gather_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim));
+        const uint32_t ln = forward_lanes(vec4 ? uint64_t(dim) / 4 : uint64_t(dim));
         switch (ln) {
+        case 2: go(std::integral_constant<int, 2>{}, vec_tag); break;
         case 4: go(std::integral_constant<int, 4>{}, vec_tag); break;
         case 8: go(std::integral_constant<int, 8>{}, vec_tag); break;
         case 16: go(std::integral_constant<int, 16>{}, vec_tag); break;
