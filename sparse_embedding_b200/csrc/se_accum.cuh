@@ -38,11 +38,30 @@ struct AccTab {
   unsigned long long *keys;  // [G] key of each slot, kEmptyKey when free
   float *vals;               // [(G + 1) * dim] fp32 sums, zero when free; slot G holds the all-ones key
   uint32_t *cnt;             // [G + 1] gradient rows summed into each slot
-  uint32_t *list;            // [G + 1] claimed slots in claim order
+  uint4 *list;               // [G + 1] claimed slots in claim order: (slot, row, erase epoch, 0)
   uint32_t *ctr;             // [0] claimed slots, [1] claim flag of slot G, [2] finished apply blocks
+  const uint32_t *epoch;     // the table's erase epoch (bumped by every erase)
   uint32_t mask;             // G - 1; G is a power of two
   uint32_t dim;
 };
+
+// Keys and rows the last lookup_or_insert resolved, by batch position (the
+// accumulate of the same batch finds its rows here instead of probing the
+// directory). *n is that batch's size; an erase clears it.
+struct FwdCache {
+  unsigned long long *keys;  // null: nothing is cached by this launch
+  uint32_t *rows;
+  uint32_t *n;               // null: the cache is not kept
+  uint32_t cap;              // entries keys / rows hold
+};
+
+// Row of key `key` at batch position pos from the cache, or kNoRow.
+__device__ __forceinline__ uint32_t cached_row(const FwdCache &fc, size_t pos, uint64_t key) {
+  if (fc.n == nullptr || fc.keys == nullptr) return kNoRow;
+  const size_t cached = min(size_t(__ldcg(fc.n)), size_t(fc.cap));
+  if (pos >= cached || __ldcg(fc.keys + pos) != key) return kNoRow;
+  return __ldcg(fc.rows + pos);
+}
 
 constexpr uint32_t kAccThreads = 256;
 constexpr uint32_t kAccMaxTile = 256;        // rows per block of k_acc_atomic
@@ -123,7 +142,7 @@ template <int VEC, bool kBag>
 __global__ void __launch_bounds__(kAccThreads, 4)  // 4 blocks per SM: a 65,536-row batch in one wave
 k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, float scale, float maxv, uint32_t tile, uint32_t hbits,
-             uint32_t *bad_word, uint32_t *status, const uint32_t *__restrict__ grad_row) {
+             uint32_t *bad_word, uint32_t *status, const uint32_t *__restrict__ grad_row, FwdCache fc) {
   extern __shared__ float s_acc[];                    // [tile][dim] sums of the tile's distinct keys
   __shared__ unsigned long long s_hkey[2 * kAccMaxTile];  // hash set of the tile's keys
   __shared__ uint32_t s_hloc[2 * kAccMaxTile + 1];    // local index of each set slot; [H]: the all-ones key
@@ -132,7 +151,9 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ uint32_t s_lcnt[kAccMaxTile];            // entries of each local index
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
-  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base;
+  __shared__ uint32_t s_hpos[2 * kAccMaxTile + 1];    // an entry of each set slot (its batch position - i0)
+  __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each claimed local key from the cache, or kNoRow
+  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch;
   constexpr int CH = int(kAccRegFloats) / VEC;        // gradient chunks per thread
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
@@ -162,6 +183,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_nloc = 0u;
     s_spec = 0u;
     s_nclaim = 0u;
+    s_epoch = __ldcg(a.epoch);
   }
   __syncthreads();
   // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
@@ -171,10 +193,12 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     uint32_t h = H;
     if (key == kEmptyKey) {
       s_spec = 1u;
+      s_hpos[H] = j;
     } else {
       h = uint32_t(splitmix64(key) >> 32) & (H - 1u);
       for (uint32_t probe = 0; probe < H; ++probe) {  // at most half full: ends at the key or a free slot
         const unsigned long long old = atomicCAS(&s_hkey[h], kEmptyKey, key);
+        if (old == kEmptyKey) s_hpos[h] = j;
         if (old == kEmptyKey || old == key) break;
         h = (h + 1u) & (H - 1u);
       }
@@ -208,6 +232,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
       const uint32_t q = atomicAdd(&s_nloc, 1u);
       s_hloc[h] = q;
       s_lkey[q] = h < H ? s_hkey[h] : kEmptyKey;
+      s_lrow[q] = s_hpos[h];  // the entry's tile position until step 3 turns it into a row
     }
   }
   __syncthreads();
@@ -228,9 +253,13 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   //    shared-memory adds of step 4)
   for (uint32_t q = tid; q < nloc; q += blockDim.x) {
     bool claimed = false;
-    const uint32_t slot = acc_find_or_claim(a, s_lkey[q], claimed);
+    const uint64_t key = s_lkey[q];
+    const uint32_t slot = acc_find_or_claim(a, key, claimed);
     s_gslot[q] = slot;
     s_crank[q] = claimed ? atomicAdd(&s_nclaim, 1u) : kNoRow;
+    // the claimant lists the key's row when lookup_or_insert left it cached,
+    // so optimizer_step need not probe the directory for it
+    if (claimed) s_lrow[q] = cached_row(fc, i0 + s_lrow[q], key);
     if (slot == kNoRow) raise_status(status, kStatusTableFull);
     else atomicAdd(a.cnt + slot, s_lcnt[q]);
   }
@@ -249,7 +278,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);
   __syncthreads();
   for (uint32_t q = tid; q < nloc; q += blockDim.x)
-    if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = s_gslot[q];
+    if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = make_uint4(s_gslot[q], s_lrow[q], s_epoch, 0u);
   // 5. the tile's sums into the table
   const uint32_t lchunks = nloc * units;
   ChunkWalk w(tid, blockDim.x, units);
@@ -288,7 +317,8 @@ __global__ void __launch_bounds__(256) k_acc_move(AccTab from, AccTab to, uint32
   const uint32_t G = from.mask + 1u;
   const uint32_t n = min(*from.ctr, G + 1u);
   for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < n; g += gridDim.x * blockDim.x) {
-    const uint32_t slot = from.list[g];
+    const uint4 ent = from.list[g];
+    const uint32_t slot = ent.x;
     const uint64_t key = slot == G ? kEmptyKey : from.keys[slot];
     bool claimed = false;
     const uint32_t ns = acc_find_or_claim(to, key, claimed);
@@ -296,7 +326,7 @@ __global__ void __launch_bounds__(256) k_acc_move(AccTab from, AccTab to, uint32
       raise_status(status, kStatusTableFull);
       continue;
     }
-    to.list[atomicAdd(to.ctr, 1u)] = ns;
+    to.list[atomicAdd(to.ctr, 1u)] = make_uint4(ns, ent.y, ent.z, 0u);
     to.cnt[ns] = from.cnt[slot];
     const float *s = from.vals + size_t(slot) * from.dim;
     float *d = to.vals + size_t(ns) * to.dim;

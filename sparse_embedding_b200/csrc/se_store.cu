@@ -139,18 +139,6 @@ __device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const 
   if (L.score != 0u && lane == 0) *reinterpret_cast<unsigned long long *>(slab + L.score) = 0ull;  // a new row's score
 }
 
-// Where lookup_or_insert leaves the batch's keys and rows for an
-// accumulate_gradients of the same keys that follows (ordered mode): the
-// accumulate takes row i from here when keys[i] equals keys[i] of the
-// lookup, instead of probing the directory again. *n is the batch size of
-// the last lookup_or_insert (0: nothing cached; an erase clears it).
-struct FwdCache {
-  unsigned long long *keys;  // null: nothing is cached by this launch
-  uint32_t *rows;
-  uint32_t *n;               // null: the cache is not kept at all (atomic mode)
-  uint32_t cap;              // entries keys / rows hold
-};
-
 // The last block of k_lookup_or_insert: copies the published rows of the
 // positions whose key another group of the launch claimed (row bytes as
 // 32-bit words, or 16-bit for odd half-precision rows; they are few), then
@@ -1009,7 +997,7 @@ k_group_hot(Layout L, uint8_t *__restrict__ slabs, OptSpec o, int gdt, const voi
 // OPT: the optimizer kind, fixed at compile time so the registers of the
 // loads in flight are those of one optimizer's state.
 template <int LANES, int VEC, bool kDyn, int OPT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)  // 3 blocks per SM: ~29K slots of 4 lanes in one wave
 k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in, int apply,
             unsigned long long *dropped) {
   OptSpec o = o_in;
@@ -1023,11 +1011,16 @@ k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in
   const uint32_t lane = uint32_t(t % LANES);
   const unsigned mask = group_mask<LANES>();
   const bool run = apply && *o.poison == 0u;
+  const uint32_t epoch = __ldcg(a.epoch);
   for (size_t g = t / LANES; g < nslots; g += groups) {
-    const uint32_t slot = __ldcg(a.list + g);
+    const uint4 ent = __ldcg(a.list + g);
+    const uint32_t slot = ent.x;
     float *acc = a.vals + size_t(slot) * L.dim;
-    uint32_t row = kNoRow;
-    if (lane == 0 && apply) row = dir_find<false>(d, slot == G ? kEmptyKey : uint64_t(__ldcg(a.keys + slot)));
+    // the row the accumulate listed (from lookup_or_insert) while no erase
+    // happened since; else the key is resolved in the directory now
+    uint32_t row = ent.z == epoch ? ent.y : kNoRow;
+    if (lane == 0 && apply && row == kNoRow)
+      row = dir_find<false>(d, slot == G ? kEmptyKey : uint64_t(__ldcg(a.keys + slot)));
     row = __shfl_sync(mask, row, 0, LANES);
     if (apply && row == kNoRow) {
       if (lane == 0) atomicAdd(dropped, (unsigned long long)__ldcg(a.cnt + slot));
@@ -1204,8 +1197,11 @@ k_assign(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec ini
 }
 
 // Rows popped past the bottom of the free stack leave it below zero.
-__global__ void k_free_clamp(int *free_top) {
+// Before an erase: clamps the free-stack top and bumps the table's erase
+// epoch (rows listed by the atomic accumulate before it are probed again).
+__global__ void k_free_clamp(int *free_top, uint32_t *erase_epoch) {
   if (*free_top < 0) *free_top = 0;
+  ++*erase_epoch;
 }
 
 // erase / erase_dimension (hogwild_embedding_store.hpp:5011-5106): the key's
@@ -1678,6 +1674,7 @@ enum Ctr : int {
   kCtrFwdDone = 19,    // blocks of the running k_lookup_or_insert that have finished
   kCtrFwdN = 20,       // keys cached by the last lookup_or_insert (FwdCache::n)
   kCtrFwdDeferred = 21,  // k_lookup_or_insert's deferred positions (zero between launches)
+  kCtrEraseEpoch = 22,   // erases so far (rows listed by the atomic accumulate carry it)
   kCtrWords = 24,
 };
 
@@ -1731,12 +1728,19 @@ struct Table {
   uint64_t acc_slots = 0;                // G (0: not allocated yet)
   unsigned long long *acc_keys = nullptr;
   float *acc_vals = nullptr;
-  uint32_t *acc_cnt = nullptr, *acc_list = nullptr, *acc_ctr = nullptr;
+  uint32_t *acc_cnt = nullptr, *acc_ctr = nullptr;
+  uint4 *acc_list = nullptr;
   AccTab acc_tab() const {
-    return AccTab{acc_keys, acc_vals, acc_cnt, acc_list, acc_ctr, uint32_t(acc_slots - 1), uint32_t(dim)};
+    return AccTab{acc_keys, acc_vals, acc_cnt, acc_list, acc_ctr, ctr + kCtrEraseEpoch, uint32_t(acc_slots - 1),
+                  uint32_t(dim)};
   }
 
   Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
+  // the keys and rows the last lookup_or_insert cached, for reading
+  FwdCache fwd_cache() const {
+    return FwdCache{fwd_keys.ptr, fwd_rows.ptr, fwd_keys.ptr ? ctr + kCtrFwdN : nullptr,
+                    uint32_t(std::min<size_t>(std::min(fwd_keys.cap, fwd_rows.cap), 0xffffffffu))};
+  }
   RowAlloc alloc() const {
     return RowAlloc{ctr + kCtrNextRow, erased ? reinterpret_cast<int *>(ctr + kCtrFreeTop) : nullptr, free_rows,
                     capacity};
@@ -2057,13 +2061,13 @@ struct StoreImpl {
     auto *nk = dalloc<unsigned long long>(G);
     auto *nv = dalloc<float>(size_t(G + 1) * size_t(t.dim));
     auto *nc = dalloc<uint32_t>(G + 1);
-    auto *nl = dalloc<uint32_t>(G + 1);
+    auto *nl = dalloc<uint4>(G + 1);
     auto *nctr = dalloc<uint32_t>(4);
     cuda_check(cudaMemsetAsync(nk, 0xff, G * 8, st), "memset sums");
     cuda_check(cudaMemsetAsync(nv, 0, size_t(G + 1) * size_t(t.dim) * 4, st), "memset sums");
     cuda_check(cudaMemsetAsync(nc, 0, (G + 1) * 4, st), "memset sums");
     cuda_check(cudaMemsetAsync(nctr, 0, 16, st), "memset sums");
-    const AccTab to{nk, nv, nc, nl, nctr, uint32_t(G - 1), uint32_t(t.dim)};
+    const AccTab to{nk, nv, nc, nl, nctr, t.ctr + kCtrEraseEpoch, uint32_t(G - 1), uint32_t(t.dim)};
     if (t.acc_slots) {
       k_acc_move<<<grid_for(t.acc_slots + 1, 256, 148 * 8), 256, 0, st>>>(t.acc_tab(), to, t.ctr + kCtrStatus);
       launched("k_acc_move");
@@ -2161,15 +2165,12 @@ struct StoreImpl {
       if (under_capture && (t.def_pos.cap < n || t.def_word.cap < n))
         throw Error(SE_ERR_RUNTIME, "lookup_or_insert captured in a CUDA graph needs a batch of the same size "
                                     "run once before capturing");
-      // ordered mode: keys and rows stay cached for the accumulate of the same keys
-      FwdCache fc{nullptr, nullptr, nullptr, 0};
-      if (!t.atomic) {
-        fc.n = t.ctr + kCtrFwdN;
-        if (!under_capture || (t.fwd_keys.cap >= n && t.fwd_rows.cap >= n)) {
-          fc.keys = t.fwd_keys.get(n);
-          fc.rows = t.fwd_rows.get(n);
-          fc.cap = uint32_t(std::min<size_t>(std::min(t.fwd_keys.cap, t.fwd_rows.cap), 0xffffffffu));
-        }
+      // keys and rows stay cached for the accumulate of the same keys
+      FwdCache fc{nullptr, nullptr, t.ctr + kCtrFwdN, 0};
+      if (!under_capture || (t.fwd_keys.cap >= n && t.fwd_rows.cap >= n)) {
+        fc.keys = t.fwd_keys.get(n);
+        fc.rows = t.fwd_rows.get(n);
+        fc.cap = uint32_t(std::min<size_t>(std::min(t.fwd_keys.cap, t.fwd_rows.cap), 0xffffffffu));
       }
       InitSpec init{cfg.init_kind, cfg.init_min, cfg.init_max - cfg.init_min,
                     cfg.optimizer_kind == SE_OPT_ADAGRAD ? cfg.initial_accumulator : 0.0f};
@@ -2322,7 +2323,7 @@ struct StoreImpl {
       Table &t = *tp;
       if (only != nullptr && only != &t) continue;
       int *free_top = reinterpret_cast<int *>(t.ctr + kCtrFreeTop);
-      k_free_clamp<<<1, 1, 0, st>>>(free_top);
+      k_free_clamp<<<1, 1, 0, st>>>(free_top, t.ctr + kCtrEraseEpoch);
       launched("k_free_clamp");
       {
         Prof pr(this, "k_erase", st);
@@ -2725,8 +2726,7 @@ struct StoreImpl {
         pdl(kern, grid, 256, 0, st, t.dir(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype, uint32_t(dim),
             cfg.gradient_scale, maxv, t.pkeys, t.prows, t.pgrads, size_t(t.pcap), t.ctr + kCtrPending,
             t.ctr + kCtrAccDone, status_word, t.ctr + kCtrStatus, cw, device_inputs ? 1 : 0, known_rows, grad_row,
-            FwdCache{t.fwd_keys.ptr, t.fwd_rows.ptr, t.fwd_keys.ptr ? t.ctr + kCtrFwdN : nullptr,
-                     uint32_t(std::min<size_t>(std::min(t.fwd_keys.cap, t.fwd_rows.cap), 0xffffffffu))});
+            t.fwd_cache());
       };
       if (grad_row) {
         if (vec4) go(k_accumulate<4, true>);
@@ -2797,7 +2797,8 @@ struct StoreImpl {
       const size_t smem = size_t(t.acc_tile) * size_t(dim) * 4;
       auto go = [&](auto kern) {
         pdl(kern, grid, kAccThreads, smem, st, t.acc_tab(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
-            cfg.gradient_scale, maxv, t.acc_tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row);
+            cfg.gradient_scale, maxv, t.acc_tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row,
+            t.fwd_cache());
       };
       if (grad_row) {
         if (vec4) go(k_acc_atomic<4, true>);
