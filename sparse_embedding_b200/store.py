@@ -295,6 +295,27 @@ def _default_device() -> int:
     return torch.cuda.current_device()
 
 
+def _float_list(arr) -> list:
+    """Values of a host array (float32, float16, or bfloat16 as a torch tensor) as Python floats."""
+    if arr is None:
+        return []
+    if hasattr(arr, "float") and hasattr(arr, "numpy"):  # torch bfloat16
+        arr = arr.float().numpy()
+    return np.asarray(arr, dtype=np.float32).reshape(-1).tolist()
+
+
+def _from_float_list(values, shape, dtype_name: str):
+    """Floats as an array of a store dtype (bfloat16 as a torch tensor)."""
+    a = np.asarray(values, dtype=np.float32).reshape(shape)
+    if dtype_name == "float16":
+        return a.astype(np.float16)
+    if dtype_name == "bfloat16":
+        from ._tensors import torch_mod
+
+        return torch_mod().from_numpy(a).to(torch_mod().bfloat16)
+    return a
+
+
 class EmbeddingStore:
     """GPU store with the reference EmbeddingStore's hot-path API
     (sparse_embedding/src/bindings/module.cpp:611-724)."""
@@ -815,11 +836,72 @@ class EmbeddingStore:
 
     # ---- conventions the GPU store does not provide --------------------------
 
-    def _not_here(self, what: str):
-        raise NotImplementedError(f"{what} is not provided by the GPU store")
-
     def export_page_images(self):
-        self._not_here("export_page_images (host checkpointing)")
+        """Page images of every table (EmbeddingStoreWrapper::export_page_images,
+        module_wrapper_methods.inl:254-290): a list of dicts with the
+        reference's fields. The GPU store has no host pages; page p of a
+        table holds entries [p * E, (p + 1) * E) of its export in directory
+        order, E = entries_per_page(); slot_ordinals are the entries' places
+        in the page and page_slot_stride_bytes is the reference's slot stride
+        for the row (row bytes rounded up to 64). values / optimizer_states
+        are float lists (row-major), steps the Adam steps (0 otherwise),
+        scores the keys' scores (0 without a score policy), seq_counts 0."""
+        from .checkpoint import export_batches
+
+        per_page = self.entries_per_page()
+        vb = 4 if self._value_dtype == "float32" else 2
+        pages = []
+        for dim, keys, values, states, steps in export_batches(self, batch_size=per_page,
+                                                               include_optimizer_state=True, include_steps=True):
+            scores = self.read_scores(keys) if self._score_policy != "none" else np.zeros(len(keys), np.uint64)
+            pages.append({
+                "embedding_dim": int(dim),
+                "physical_page_id": sum(1 for q in pages if q["embedding_dim"] == int(dim)),
+                "page_slot_stride_bytes": (int(dim) * vb + 63) // 64 * 64,
+                "slot_ordinals": list(range(len(keys))),
+                "keys": [int(k) & 0xFFFFFFFFFFFFFFFF for k in np.asarray(keys).tolist()],
+                "seq_counts": [0] * len(keys),
+                "scores": [int(x) for x in np.asarray(scores).tolist()],
+                "steps": [int(x) for x in np.asarray(steps).tolist()],
+                "values": _float_list(values),
+                "optimizer_states": _float_list(states),
+            })
+        return pages
 
     def import_page_images(self, pages):
-        self._not_here("import_page_images (host checkpointing)")
+        """Loads page images into this (empty) store (import_page_images,
+        hogwild_embedding_store.hpp:6512-6590): every page's keys get their
+        values, optimizer state, Adam steps and scores. Errors as the
+        reference: a dimension without a table, repeated page ids of a
+        dimension, or a store that already holds keys."""
+        from .checkpoint import assign_opt_state
+
+        self._check_operational()
+        dims = set(self._config.dims)
+        seen = set()
+        for page in pages:
+            d = int(page["embedding_dim"])
+            if d not in dims:
+                raise ValueError("page-image import dimension has no physical table")
+            if (d, int(page["physical_page_id"])) in seen:
+                raise ValueError("page-image import has duplicate page ids")
+            seen.add((d, int(page["physical_page_id"])))
+        if self.total_size() != 0:
+            raise RuntimeError("page-image import requires empty slots")
+        kdt = np.dtype(self._key_dtype)
+        ns = {"adam": 2, "adagrad": 1}.get(getattr(self._optimizer, "kind", "none"), 0) \
+            if self._optimizer_enabled else 0
+        for page in pages:
+            d = int(page["embedding_dim"])
+            n = len(page["keys"])
+            if n == 0:
+                continue
+            keys = np.asarray(page["keys"], dtype=np.uint64).view(np.int64).astype(kdt) if kdt.kind == "i" \
+                else np.asarray(page["keys"], dtype=np.uint64).astype(kdt)
+            values = _from_float_list(page["values"], (n, d), self._value_dtype)
+            self.assign(keys, values)
+            if ns:
+                states = _from_float_list(page["optimizer_states"], (n, ns * d), self._optimizer_dtype)
+                assign_opt_state(self, keys, states, d, steps=np.asarray(page["steps"], dtype=np.uint32))
+            if self._score_policy != "none" and any(page["scores"]):
+                self.assign_scores(keys, np.asarray(page["scores"], dtype=np.uint64))

@@ -123,3 +123,44 @@ def test_assign_opt_state_errors_leave_the_store_unchanged():
     sgd.lookup_or_insert(keys, 8)
     with pytest.raises(ValueError, match="payload size does not match"):
         ck.assign_opt_state(sgd, keys, np.ones((10, 8), dtype=np.float32), 8)
+
+
+@pytest.mark.parametrize("value_dtype,opt", [("float32", "adam"), ("bfloat16", "adagrad"), ("float32", "sgd")])
+def test_page_images_round_trip(value_dtype, opt):
+    """export_page_images -> import_page_images into an empty store of the
+    same configuration reproduces every key's row, optimizer state and Adam
+    step (page dicts with the reference's fields), and the copy trains on
+    identically; the reference's import errors are kept."""
+    gpu, _, present = trained(value_dtype=value_dtype, opt=opt)
+    pages = gpu.export_page_images()
+    assert pages and {"embedding_dim", "physical_page_id", "page_slot_stride_bytes", "slot_ordinals", "keys",
+                      "seq_counts", "scores", "steps", "values", "optimizer_states"} <= set(pages[0])
+    per_page = gpu.entries_per_page()
+    assert all(len(p["keys"]) <= per_page for p in pages)
+    assert sum(len(p["keys"]) for p in pages) == gpu.total_size()
+    fresh, _ = pair([16, 32], key_dtype="int64", value_dtype=value_dtype, opt=opt, lr=1e-2)
+    fresh.import_page_images(pages)
+    assert fresh.total_size() == gpu.total_size()
+    for d, keys in present.items():
+        np.testing.assert_array_equal(bits(fresh.lookup(keys, d)[0]), bits(gpu.lookup(keys, d)[0]))
+        for k in keys[:20]:
+            a, b = gpu.read_state(int(k), d), fresh.read_state(int(k), d)
+            assert a[0] and b[0] and a[3] == b[3]
+            np.testing.assert_array_equal(a[2], b[2])
+    rng = np.random.default_rng(5)
+    keys = rng.choice(present[16], size=3000)
+    g = (rng.standard_normal((len(keys), 16)) * 1e-2).astype(np.float32)
+    if value_dtype == "bfloat16":
+        g = torch.from_numpy(g).to(torch.bfloat16)
+    for s in (gpu, fresh):
+        s.accumulate_gradients(keys, g)
+        s.optimizer_step(1)
+    np.testing.assert_array_equal(bits(fresh.lookup(present[16], 16)[0]), bits(gpu.lookup(present[16], 16)[0]))
+    with pytest.raises(RuntimeError, match="requires empty slots"):
+        fresh.import_page_images(pages)
+    other, _ = pair([8], key_dtype="int64", value_dtype=value_dtype, opt=opt, lr=1e-2)
+    with pytest.raises(ValueError, match="no physical table"):
+        other.import_page_images(pages)
+    empty, _ = pair([16, 32], key_dtype="int64", value_dtype=value_dtype, opt=opt, lr=1e-2)
+    with pytest.raises(ValueError, match="duplicate page ids"):
+        empty.import_page_images([pages[0], pages[0]])
