@@ -208,13 +208,17 @@ __global__ void k_ex_sync(ExView x, int kind, int total_word) {
 
 // Route counts of this rank's keys: per-tile histograms by owner. Launched
 // with max(tiles, 1) blocks of kExTile keys.
+// count_dev: when not null, the batch holds min(*count_dev, count) keys (the
+// sender's distinct keys, counted on the device).
 template <class K>
 __global__ void __launch_bounds__(kRouteThreads)
-k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts) {
+k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts,
+           const uint32_t *count_dev) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   extern __shared__ uint32_t hist[];  // [W]
   if (ex_failed(x)) return;
+  if (count_dev) count = min(count, size_t(*count_dev));
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) hist[p] = 0;
   __syncthreads();
   const size_t i = size_t(blockIdx.x) * kRouteThreads + threadIdx.x;
@@ -278,9 +282,10 @@ template <class K, bool kGrads, class U>
 __global__ void __launch_bounds__(kRouteThreads)
 k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, const uint32_t *__restrict__ tile_offsets,
              const uint32_t *__restrict__ counts_local, const uint8_t *__restrict__ grads,
-             uint32_t *__restrict__ key_pid, uint32_t *__restrict__ key_slot) {
+             uint32_t *__restrict__ key_pid, uint32_t *__restrict__ key_slot, const uint32_t *count_dev) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
+  if (count_dev) count = min(count, size_t(*count_dev));
   extern __shared__ uint32_t sm[];
   uint32_t *warp_base = sm;                   // [kRouteWarps][W]
   uint32_t *remote = sm + kRouteWarps * s.n;  // [W] slot base on each owner minus the local prefix
@@ -534,6 +539,156 @@ k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t
 #pragma unroll
       for (int k = 0; k < kIlp; ++k)
         if (dst[k]) dst[k][c] = v[k];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Sender-side dedupe. A Zipf batch repeats its hot keys thousands of times;
+// routing each distinct key once per sender keeps the owners' work and the
+// NVLink traffic at the distinct keys, and the forward expands the rows
+// locally. The gradient batch routed like such a forward is summed per
+// distinct key on the sender first (pre-reduction: the order of the adds
+// changes, so results match the plain route within fp32 reassociation).
+// ---------------------------------------------------------------------------
+
+struct DedupeWs {
+  unsigned long long *set_keys;  // [D] hash set of the batch's keys, kEmptyKey when free
+  uint32_t *set_idx;             // [D + 1] distinct-key index of each set slot; [D]: the all-ones key
+  uint32_t *pos_slot;            // [M] set slot of each batch position
+  uint32_t *uslot;               // [M] set slot of each distinct key
+  uint32_t *inverse;             // [M] distinct-key index of each batch position
+  uint32_t *ctr;                 // [0] distinct keys, [1] claim flag of the all-ones key, [2] blocks done
+  uint32_t mask;                 // D - 1
+};
+
+// Distinct keys of the batch, claim order: ukeys[idx] is the idx-th claimed
+// key (same dtype as the batch), pos_slot[i] the set slot of position i.
+// Bounded probing; the set holds at least twice the batch.
+template <class K>
+__global__ void __launch_bounds__(256)
+k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__restrict__ ukeys) {
+  pdl_wait();
+  pdl_trigger();
+  if (ex_failed(x)) return;
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint32_t D = w.mask + 1u;
+  bool claimed = false;
+  uint32_t slot = kNoRow;
+  K k{};
+  if (i < n) {
+    k = keys[i];
+    const uint64_t key = key_u64(k);
+    if (key == kEmptyKey) {
+      slot = D;
+      claimed = atomicCAS(w.ctr + 1, 0u, 1u) == 0u;
+    } else {
+      uint32_t h = uint32_t(__umul64hi(splitmix64(key), uint64_t(D)));
+      for (uint32_t probe = 0; probe < D; ++probe) {
+        const unsigned long long old = atomicCAS(w.set_keys + h, kEmptyKey, key);
+        if (old == kEmptyKey || old == key) {
+          claimed = old == kEmptyKey;
+          slot = h;
+          break;
+        }
+        h = (h + 1u) & w.mask;
+      }
+    }
+    w.pos_slot[i] = slot;
+  }
+  // one counter atomic per warp for its claims
+  const uint32_t lane = threadIdx.x & 31u;
+  const unsigned claims = __ballot_sync(0xffffffffu, claimed);
+  if (claims == 0u) return;
+  uint32_t base = 0;
+  if (lane == uint32_t(__ffs(claims) - 1)) base = atomicAdd(w.ctr, uint32_t(__popc(claims)));
+  base = __shfl_sync(0xffffffffu, base, __ffs(claims) - 1);
+  if (claimed) {
+    const uint32_t idx = base + __popc(claims & ((1u << lane) - 1u));
+    w.set_idx[slot] = idx;
+    w.uslot[idx] = slot;
+    ukeys[idx] = k;
+  }
+}
+
+// inverse[i]: the distinct-key index of position i.
+__global__ void __launch_bounds__(256) k_ex_dedupe_inverse(ExView x, size_t n, DedupeWs w) {
+  pdl_wait();
+  pdl_trigger();
+  if (ex_failed(x)) return;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t slot = w.pos_slot[i];
+    w.inverse[i] = slot == kNoRow ? 0u : __ldcg(w.set_idx + slot);
+  }
+}
+
+// Requester of a deduplicated forward: waits for the rows of every owner
+// (stream order), then out[i] = row buffer[inverse[i]] in units U; also
+// empties the dedupe set for the next call (the last block resets its
+// counters once every block has read them).
+template <class U>
+__global__ void __launch_bounds__(256)
+k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, DedupeWs w) {
+  pdl_wait();
+  pdl_trigger();
+  const bool failed = ex_failed(x);
+  const U *src = reinterpret_cast<const U *>(x.rows(x.me));
+  const size_t total = n * units;
+  const size_t stride = size_t(gridDim.x) * blockDim.x;
+  const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (!failed) {
+    for (size_t c = tid; c < total; c += stride) {
+      const size_t i = c / units, u = c - i * units;
+      const uint32_t idx = __ldcg(w.inverse + i);
+      out[c] = __ldcg(src + size_t(min(idx, x.M - 1u)) * units + u);
+    }
+  }
+  const uint32_t nd = min(__ldcg(w.ctr), x.M);
+  for (size_t j = tid; j < nd; j += stride) {
+    const uint32_t slot = __ldcg(w.uslot + j);
+    if (slot <= w.mask) w.set_keys[slot] = kEmptyKey;
+  }
+  __shared__ bool s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(w.ctr + 2, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    w.ctr[0] = 0u;
+    w.ctr[1] = 0u;
+    w.ctr[2] = 0u;
+  }
+}
+
+// Pre-reduced gradient rows of a deduplicated forward's keys: distinct key
+// u's fp32 sum (pre[u], `dim` floats) goes to slot key_slot[u] of owner
+// key_pid[u]'s gradient inbox, in the gradient dtype; the sum is zeroed for
+// the next call. One warp per row.
+__global__ void __launch_bounds__(256)
+k_ex_scatter_prerows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot,
+                     const uint32_t *count_dev, size_t n_max, float *__restrict__ pre, uint32_t dim, int gdt) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint8_t *inbox_of[kExMaxRanks];
+  if (ex_failed(x)) return;
+  for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) inbox_of[p] = x.ingrads(p);
+  __syncthreads();
+  const size_t nd = min(size_t(*count_dev), n_max);
+  const uint32_t inbox = x.W * x.M;
+  const uint32_t lane = threadIdx.x & 31u;
+  const size_t warps = (size_t(gridDim.x) * blockDim.x) >> 5;
+  for (size_t u = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < nd; u += warps) {
+    const uint32_t slot = key_slot[u];
+    float *src = pre + u * dim;
+    uint8_t *dst = slot < inbox ? inbox_of[key_pid[u]] + size_t(slot) * x.grad_bytes : nullptr;
+    for (uint32_t e = lane; e < dim; e += 32) {
+      const float v = src[e];
+      src[e] = 0.0f;
+      if (dst == nullptr) continue;
+      if (gdt == SE_FLOAT32) reinterpret_cast<float *>(dst)[e] = v;
+      else reinterpret_cast<uint16_t *>(dst)[e] = uint16_t(f_to_bits(gdt, v));
     }
   }
 }

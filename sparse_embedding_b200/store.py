@@ -841,14 +841,14 @@ class EmbeddingStore:
         module_wrapper_methods.inl:254-290): a list of dicts with the
         reference's fields. The GPU store has no host pages; page p of a
         table holds entries [p * E, (p + 1) * E) of its export in directory
-        order, E = entries_per_page(); slot_ordinals are the entries' places
+        order, E = entries_per_page; slot_ordinals are the entries' places
         in the page and page_slot_stride_bytes is the reference's slot stride
         for the row (row bytes rounded up to 64). values / optimizer_states
         are float lists (row-major), steps the Adam steps (0 otherwise),
         scores the keys' scores (0 without a score policy), seq_counts 0."""
         from .checkpoint import export_batches
 
-        per_page = self.entries_per_page()
+        per_page = self.entries_per_page
         vb = 4 if self._value_dtype == "float32" else 2
         pages = []
         for dim, keys, values, states, steps in export_batches(self, batch_size=per_page,

@@ -135,7 +135,7 @@ def test_page_images_round_trip(value_dtype, opt):
     pages = gpu.export_page_images()
     assert pages and {"embedding_dim", "physical_page_id", "page_slot_stride_bytes", "slot_ordinals", "keys",
                       "seq_counts", "scores", "steps", "values", "optimizer_states"} <= set(pages[0])
-    per_page = gpu.entries_per_page()
+    per_page = gpu.entries_per_page
     assert all(len(p["keys"]) <= per_page for p in pages)
     assert sum(len(p["keys"]) for p in pages) == gpu.total_size()
     fresh, _ = pair([16, 32], key_dtype="int64", value_dtype=value_dtype, opt=opt, lr=1e-2)
