@@ -360,6 +360,15 @@ int se_exchange_accumulate(se_exchange *ex, const void *keys, size_t n, const vo
 int se_exchange_accumulate_routed(se_exchange *ex, const void *grads, size_t n, void *stream);
 /* Synchronises `stream`; raises a timed-out wait, then the owner table's errors. */
 int se_exchange_check(se_exchange *ex, void *stream);
+/* Sender-side dedupe (no reference counterpart): with enable != 0, each
+ * se_exchange_lookup routes every distinct key of the rank's batch once and
+ * expands the returned rows to the batch's positions (rows are identical to
+ * the plain route), and se_exchange_accumulate_routed sums each distinct
+ * key's gradient rows on the sender (fp32) before sending one row per key
+ * (the order of the adds changes: updates match the plain route within
+ * fp32 reassociation). Every rank of the exchange must make the same
+ * choice; rows of at most 8,192 values. */
+int se_exchange_set_dedupe(se_exchange *ex, int32_t enable);
 /* Frees this rank's end. Call only after every rank finished its last
  * exchange call (peers store into this arena). */
 int se_exchange_destroy(se_exchange *ex);

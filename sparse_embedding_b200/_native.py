@@ -124,6 +124,7 @@ _SIGNATURES = {
     "se_exchange_accumulate": [_vp, _vp, _sz, _vp, _vp],
     "se_exchange_accumulate_routed": [_vp, _vp, _sz, _vp],
     "se_exchange_check": [_vp, _vp],
+    "se_exchange_set_dedupe": [_vp, _i32],
     "se_exchange_destroy": [_vp],
 }
 _RESTYPES = {"se_last_error": C.c_char_p, "se_version": C.c_char_p, "se_kernel_launch_count": _u64}

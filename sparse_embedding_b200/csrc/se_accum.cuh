@@ -138,7 +138,11 @@ struct ChunkWalk {
   }
 };
 
-template <int VEC, bool kBag>
+// With kDirect the "keys" are row indices of a dense fp32 sum array
+// (a.vals, [rows][dim]): each distinct index adds its tile sum into its own
+// row, with no slot claims, counts or list (a sender's gradient
+// pre-reduction by distinct key of an exchange).
+template <int VEC, bool kBag, bool kDirect = false>
 __global__ void __launch_bounds__(kAccThreads, 4)  // 4 blocks per SM: a 65,536-row batch in one wave
 k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, float scale, float maxv, uint32_t tile, uint32_t hbits,
@@ -183,7 +187,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_nloc = 0u;
     s_spec = 0u;
     s_nclaim = 0u;
-    s_epoch = __ldcg(a.epoch);
+    s_epoch = a.epoch ? __ldcg(a.epoch) : 0u;
   }
   __syncthreads();
   // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
@@ -254,6 +258,11 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   for (uint32_t q = tid; q < nloc; q += blockDim.x) {
     bool claimed = false;
     const uint64_t key = s_lkey[q];
+    if constexpr (kDirect) {
+      s_gslot[q] = uint32_t(key);
+      s_crank[q] = kNoRow;
+      continue;
+    }
     const uint32_t slot = acc_find_or_claim(a, key, claimed);
     s_gslot[q] = slot;
     s_crank[q] = claimed ? atomicAdd(&s_nclaim, 1u) : kNoRow;

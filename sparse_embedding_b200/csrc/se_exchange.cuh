@@ -425,9 +425,9 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec i
     }
     // the row for a gradient batch routed like this forward (deferred keys: below)
     if (lane == 0 && kind != 3) x.inrow()[i] = (kind == kFound || kind == kInserted) ? row : kNoRow;
-    if (kind == kFound) {
+    if (kind == kFound) {  // L1 may serve the row (see copy_units)
       const uint8_t *slab = slabs + size_t(row) * L.stride;
-      copy_row<VEC>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
+      copy_row<VEC, 4, true>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
     } else if (kind == kInserted) {
       uint8_t *slab = slabs + size_t(row) * L.stride;
       init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
@@ -552,13 +552,20 @@ k_ex_scatter_rows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t
 // changes, so results match the plain route within fp32 reassociation).
 // ---------------------------------------------------------------------------
 
+// The counters of a deduplicated forward alternate between two sets by the
+// forward's parity: forward c counts its distinct keys in count[c % 2],
+// which the gradient batch routed like it still reads, and forward c's last
+// kernel resets the other set (forward c - 1's, dead by then) for c + 1.
 struct DedupeWs {
   unsigned long long *set_keys;  // [D] hash set of the batch's keys, kEmptyKey when free
   uint32_t *set_idx;             // [D + 1] distinct-key index of each set slot; [D]: the all-ones key
   uint32_t *pos_slot;            // [M] set slot of each batch position
   uint32_t *uslot;               // [M] set slot of each distinct key
   uint32_t *inverse;             // [M] distinct-key index of each batch position
-  uint32_t *ctr;                 // [0] distinct keys, [1] claim flag of the all-ones key, [2] blocks done
+  uint32_t *count;               // this forward's distinct keys
+  uint32_t *spec;                // this forward's claim flag of the all-ones key
+  uint32_t *other_count, *other_spec;  // the previous forward's, reset by this one
+  uint32_t *done;                // blocks of k_ex_rows_out_dedupe that finished
   uint32_t mask;                 // D - 1
 };
 
@@ -581,7 +588,7 @@ k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__res
     const uint64_t key = key_u64(k);
     if (key == kEmptyKey) {
       slot = D;
-      claimed = atomicCAS(w.ctr + 1, 0u, 1u) == 0u;
+      claimed = atomicCAS(w.spec, 0u, 1u) == 0u;
     } else {
       uint32_t h = uint32_t(__umul64hi(splitmix64(key), uint64_t(D)));
       for (uint32_t probe = 0; probe < D; ++probe) {
@@ -601,7 +608,7 @@ k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__res
   const unsigned claims = __ballot_sync(0xffffffffu, claimed);
   if (claims == 0u) return;
   uint32_t base = 0;
-  if (lane == uint32_t(__ffs(claims) - 1)) base = atomicAdd(w.ctr, uint32_t(__popc(claims)));
+  if (lane == uint32_t(__ffs(claims) - 1)) base = atomicAdd(w.count, uint32_t(__popc(claims)));
   base = __shfl_sync(0xffffffffu, base, __ffs(claims) - 1);
   if (claimed) {
     const uint32_t idx = base + __popc(claims & ((1u << lane) - 1u));
@@ -624,8 +631,8 @@ __global__ void __launch_bounds__(256) k_ex_dedupe_inverse(ExView x, size_t n, D
 
 // Requester of a deduplicated forward: waits for the rows of every owner
 // (stream order), then out[i] = row buffer[inverse[i]] in units U; also
-// empties the dedupe set for the next call (the last block resets its
-// counters once every block has read them).
+// empties the dedupe set for the next forward, and its last block resets
+// the previous forward's counters.
 template <class U>
 __global__ void __launch_bounds__(256)
 k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, DedupeWs w) {
@@ -643,22 +650,19 @@ k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, De
       out[c] = __ldcg(src + size_t(min(idx, x.M - 1u)) * units + u);
     }
   }
-  const uint32_t nd = min(__ldcg(w.ctr), x.M);
+  const uint32_t nd = min(__ldcg(w.count), x.M);
   for (size_t j = tid; j < nd; j += stride) {
     const uint32_t slot = __ldcg(w.uslot + j);
     if (slot <= w.mask) w.set_keys[slot] = kEmptyKey;
   }
   __shared__ bool s_last;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    s_last = atomicAdd(w.ctr + 2, 1u) == gridDim.x - 1;
-  }
+  if (threadIdx.x == 0) s_last = atomicAdd(w.done, 1u) == gridDim.x - 1;
   __syncthreads();
   if (s_last && threadIdx.x == 0) {
-    w.ctr[0] = 0u;
-    w.ctr[1] = 0u;
-    w.ctr[2] = 0u;
+    *w.other_count = 0u;
+    *w.other_spec = 0u;
+    *w.done = 0u;
   }
 }
 

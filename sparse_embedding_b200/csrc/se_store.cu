@@ -78,11 +78,15 @@ __device__ __forceinline__ void zero_elems(void *dst, int dt, size_t e) {
 }
 
 // Copies elements e0, e0 + step, ... (< dim) of a row in VEC-element units,
-// raw bits. Loads go to L2 (ld.cg): in the insert kernels a row may have been
-// initialised by another SM during the same launch, so no L1 line may be
-// trusted. ILP loads are in flight before their stores: a few lanes per key then
-// keep a whole row's loads outstanding, and more keys fit in flight per SM.
-template <class U, int VEC, int ILP>
+// raw bits. ILP loads are in flight before their stores: a few lanes per key
+// then keep a whole row's loads outstanding, and more keys fit in flight per SM.
+// kCached: plain loads, which L1 may serve. A row found through the
+// directory in an insert kernel was published before it was found, and no
+// thread of the launch read its slab before its claimant initialised it (a
+// fresh or recycled row belongs to no key until then), so no L1 line of it
+// can be stale; hot keys' rows are then fetched from L2 once per SM instead
+// of once per position. Otherwise loads go to L2 (ld.cg).
+template <class U, int VEC, int ILP, bool kCached = false>
 __device__ __forceinline__ void copy_units(void *dst, const void *src, uint32_t dim, uint32_t e0, uint32_t step) {
   const U *s = static_cast<const U *>(src);
   U *d = static_cast<U *>(dst);
@@ -90,22 +94,22 @@ __device__ __forceinline__ void copy_units(void *dst, const void *src, uint32_t 
     U v[ILP];
 #pragma unroll
     for (int k = 0; k < ILP; ++k)
-      if (e + k * step < dim) v[k] = __ldcg(s + (e + k * step) / VEC);
+      if (e + k * step < dim) v[k] = kCached ? s[(e + k * step) / VEC] : __ldcg(s + (e + k * step) / VEC);
 #pragma unroll
     for (int k = 0; k < ILP; ++k)
       if (e + k * step < dim) d[(e + k * step) / VEC] = v[k];
   }
 }
 
-template <int VEC, int ILP = 4>
+template <int VEC, int ILP = 4, bool kCached = false>
 __device__ __forceinline__ void copy_row(void *dst, const void *src, int dt, uint32_t dim, uint32_t e0,
                                          uint32_t step) {
   if (dt == SE_FLOAT32) {
-    if constexpr (VEC == 4) copy_units<uint4, 4, ILP>(dst, src, dim, e0, step);
-    else copy_units<unsigned int, 1, ILP>(dst, src, dim, e0, step);
+    if constexpr (VEC == 4) copy_units<uint4, 4, ILP, kCached>(dst, src, dim, e0, step);
+    else copy_units<unsigned int, 1, ILP, kCached>(dst, src, dim, e0, step);
   } else {
-    if constexpr (VEC == 4) copy_units<uint2, 4, ILP>(dst, src, dim, e0, step);
-    else copy_units<unsigned short, 1, ILP>(dst, src, dim, e0, step);
+    if constexpr (VEC == 4) copy_units<uint2, 4, ILP, kCached>(dst, src, dim, e0, step);
+    else copy_units<unsigned short, 1, ILP, kCached>(dst, src, dim, e0, step);
   }
 }
 
@@ -223,7 +227,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, In
     }
     if (kind == kFound) {
       const uint8_t *slab = slabs + size_t(row) * L.stride;
-      copy_row<VEC, LANES == 2 ? 8 : 4>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
+      copy_row<VEC, LANES == 2 ? 8 : 4, true>(out_row, slab, L.pdt, L.dim, lane * VEC, LANES * VEC);
     } else if (kind == kInserted) {
       uint8_t *slab = slabs + size_t(row) * L.stride;
       init_slab<LANES, VEC>(L, slab, init, key, lane, out_row);
@@ -3110,10 +3114,20 @@ struct ExchangeImpl {
   uint32_t *route[2] = {nullptr, nullptr};
   uint32_t tiles_cap = 0;
   uint32_t *status_host = nullptr;  // pinned
-  // (owner, slot) of every key of the last forward, and its batch size
+  // (owner, slot) of every key of the last forward (of every distinct key
+  // when it was deduplicated), and its batch size
   uint32_t *key_pid = nullptr, *key_slot = nullptr;
   size_t last_fwd_n = 0;
   bool have_fwd = false;
+  // sender-side dedupe (se_exchange_set_dedupe): workspace, distinct keys of
+  // the batch (key dtype), fp32 per-key gradient sums of the routed backward
+  bool dedupe = false, fwd_deduped = false;
+  uint32_t parity = 0;
+  unsigned long long *dd_set = nullptr;
+  uint32_t *dd_idx = nullptr, *dd_pos_slot = nullptr, *dd_uslot = nullptr, *dd_inverse = nullptr, *dd_ctr = nullptr;
+  uint8_t *dd_ukeys = nullptr;
+  float *dd_pre = nullptr;
+  uint64_t dd_slots = 0;
 
   ~ExchangeImpl() {
     DeviceGuard dg(device);
@@ -3126,7 +3140,43 @@ struct ExchangeImpl {
     dfree(route[1]);
     dfree(key_pid);
     dfree(key_slot);
+    dfree(dd_set);
+    dfree(dd_idx);
+    dfree(dd_pos_slot);
+    dfree(dd_uslot);
+    dfree(dd_inverse);
+    dfree(dd_ctr);
+    dfree(dd_ukeys);
+    dfree(dd_pre);
     if (status_host) cudaFreeHost(status_host);
+  }
+
+  // Sender-side dedupe of forwards (and pre-reduction of the gradient batch
+  // routed like them). Every rank of the exchange must make the same choice.
+  void set_dedupe(bool enable) {
+    DeviceGuard dg(device);
+    std::lock_guard<std::mutex> lock(store->mu);
+    if (enable && dd_set == nullptr) {
+      dd_slots = next_pow2(std::max<uint64_t>(2 * M, 64));
+      dd_set = dalloc<unsigned long long>(dd_slots);
+      dd_idx = dalloc<uint32_t>(dd_slots + 1);
+      dd_pos_slot = dalloc<uint32_t>(M);
+      dd_uslot = dalloc<uint32_t>(M);
+      dd_inverse = dalloc<uint32_t>(M);
+      dd_ctr = dalloc<uint32_t>(8);
+      dd_ukeys = dalloc<uint8_t>(M * 8);
+      dd_pre = dalloc<float>(M * size_t(dim));
+      cuda_check(cudaMemset(dd_set, 0xff, dd_slots * 8), "memset dedupe");
+      cuda_check(cudaMemset(dd_ctr, 0, 32), "memset dedupe");
+      cuda_check(cudaMemset(dd_pre, 0, M * size_t(dim) * 4), "memset dedupe");
+      cuda_check(cudaDeviceSynchronize(), "sync");
+    }
+    dedupe = enable;
+  }
+
+  DedupeWs dedupe_ws() const {
+    return DedupeWs{dd_set, dd_idx, dd_pos_slot, dd_uslot, dd_inverse, dd_ctr + parity, dd_ctr + 2 + parity,
+                    dd_ctr + (parity ^ 1u), dd_ctr + 2 + (parity ^ 1u), dd_ctr + 4, uint32_t(dd_slots - 1)};
   }
 
   void create(StoreImpl *s, int kind, uint32_t world, uint32_t rank, uint64_t max_keys, int64_t row_dim,
@@ -3234,12 +3284,14 @@ struct ExchangeImpl {
   // Route of this rank's keys (per-tile counts, offsets, per-owner counts),
   // published to every rank as `kind`; returns after every rank's counts
   // arrived (stream order).
+  // count_dev: the batch's size on the device (at most n), or null.
   template <class K>
-  const uint32_t *run_route(const K *keys, size_t n, int dir, int kind, cudaStream_t st) {
+  const uint32_t *run_route(const K *keys, size_t n, int dir, int kind, cudaStream_t st,
+                            const uint32_t *count_dev = nullptr) {
     const uint32_t tiles = std::max(uint32_t((n + kExTile - 1) / kExTile), 1u);
     uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
     uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
-    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, keys, n, tile_counts);
+    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, keys, n, tile_counts, count_dev);
     launched("k_ex_count");
     pdl(k_ex_sync_counts, 1, kRouteThreads, 0, st, view, kind, tiles, tile_counts, tile_offsets, counts);
     launched("k_ex_sync_counts");
@@ -3266,15 +3318,30 @@ struct ExchangeImpl {
     DeviceGuard dg(device);
     Table &t = store->table(dim);
     const uint32_t tiles = uint32_t((n + kExTile - 1) / kExTile);
+    const bool dd = dedupe && n > 0;
+    if (dd) parity ^= 1u;
+    const DedupeWs dws = dedupe_ws();
     dispatch_key(store->cfg.key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
-      const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st);
+      const uint32_t *count_dev = nullptr;
+      if (dd) {  // route each distinct key of the batch once
+        StoreImpl::Prof pr(store, "k_ex_dedupe", st);
+        pdl(k_ex_dedupe<K>, grid_for(n, 256, 0x7fffffffu), 256, 0, st, view, k, n, dws,
+            reinterpret_cast<K *>(dd_ukeys));
+        launched("k_ex_dedupe");
+        pdl(k_ex_dedupe_inverse, grid_for(n, 256, 148 * 8), 256, 0, st, view, n, dws);
+        launched("k_ex_dedupe_inverse");
+        k = reinterpret_cast<const K *>(dd_ukeys);
+        count_dev = dws.count;
+      }
+      const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st, count_dev);
       StoreImpl::Prof pr(store, "k_ex_scatter_keys", st);
       pdl(k_ex_scatter<K, false, uint4>, std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st,
-          spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot);
+          spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot, count_dev);
       launched("k_ex_scatter");
     });
+    fwd_deduped = dd;
     sync(kExKeys, st);
     // owner side: at most W * M keys arrive
     const uint64_t WM = uint64_t(W) * M;
@@ -3326,7 +3393,12 @@ struct ExchangeImpl {
       using U = decltype(utag);
       const size_t units = bytes / sizeof(U);
       StoreImpl::Prof pr(store, "k_ex_rows_out", st);
-      pdl(k_ex_rows_out<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), units);
+      if (dd) {  // expand the distinct keys' rows to the batch's positions
+        pdl(k_ex_rows_out_dedupe<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), n,
+            uint32_t(view.row_bytes / sizeof(U)), dws);
+      } else {
+        pdl(k_ex_rows_out<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), units);
+      }
       launched("k_ex_rows_out");
     };
     if (al % 16 == 0) copy_out(uint4{});
@@ -3349,7 +3421,7 @@ struct ExchangeImpl {
         StoreImpl::Prof pr(store, "k_ex_scatter_grads", st);
         pdl(k_ex_scatter<K, true, U>, std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st,
             spec, view, k, n, route[1] + size_t(tiles_cap) * W, counts, static_cast<const uint8_t *>(grads), nullptr,
-            nullptr);
+            nullptr, nullptr);
         launched("k_ex_scatter");
       };
       if (al % 16 == 0) scatter(uint4{});
@@ -3372,24 +3444,61 @@ struct ExchangeImpl {
     if (n && !is_device_ptr(grads)) throw std::invalid_argument("exchange takes device gradient rows");
     std::lock_guard<std::mutex> lock(store->mu);
     DeviceGuard dg(device);
-    const uintptr_t al = uintptr_t(grads) | uintptr_t(view.grad_bytes);
-    auto scatter = [&](auto utag) {
-      using U = decltype(utag);
-      const uint32_t units = view.grad_bytes / uint32_t(sizeof(U));
-      uint32_t team = 1;
-      while (team < 32 && team < units) team <<= 1;
-      StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
-      pdl(k_ex_scatter_rows<U>, grid_for(n * team, 256, 148 * 8), 256, 0, st,
-          view, key_pid, key_slot, n, static_cast<const U *>(grads), units, team);
-      launched("k_ex_scatter_rows");
-    };
-    if (al % 16 == 0) scatter(uint4{});
-    else if (al % 4 == 0) scatter(uint32_t{});
-    else scatter(uint16_t{});
+    if (fwd_deduped) {
+      prereduce_and_scatter(grads, n, st);
+    } else {
+      const uintptr_t al = uintptr_t(grads) | uintptr_t(view.grad_bytes);
+      auto scatter = [&](auto utag) {
+        using U = decltype(utag);
+        const uint32_t units = view.grad_bytes / uint32_t(sizeof(U));
+        uint32_t team = 1;
+        while (team < 32 && team < units) team <<= 1;
+        StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
+        pdl(k_ex_scatter_rows<U>, grid_for(n * team, 256, 148 * 8), 256, 0, st,
+            view, key_pid, key_slot, n, static_cast<const U *>(grads), units, team);
+        launched("k_ex_scatter_rows");
+      };
+      if (al % 16 == 0) scatter(uint4{});
+      else if (al % 4 == 0) scatter(uint32_t{});
+      else scatter(uint16_t{});
+    }
     sync(kExGrads, st, kExFwdTotal);
     const auto *total = reinterpret_cast<const uint32_t *>(arena + view.o_words) + kExTotal;
     store->accumulate_locked(arena + view.o_inkeys, size_t(W) * M, total, dim, arena + view.o_ingrads, st,
                              SE_KEY_UINT64, reinterpret_cast<const uint32_t *>(arena + view.o_inrow));
+  }
+
+  // Gradient batch of a deduplicated forward: the rows of each distinct key
+  // are summed on this rank in fp32 (k_acc_atomic over dense rows indexed by
+  // the forward's inverse), then each sum goes to the owner's inbox slot of
+  // that key.
+  void prereduce_and_scatter(const void *grads, size_t n, cudaStream_t st) {
+    if (dim > int64_t(kAccMaxDim))
+      throw std::invalid_argument("dedupe needs rows of at most 8,192 values");
+    const DedupeWs dws = dedupe_ws();
+    const int gdt = store->cfg.gradient_dtype;
+    uint32_t tile = 1;
+    while (tile < kAccMaxTile && uint64_t(tile) * 2 * uint64_t(dim) * 4 <= kAccSmemBytes) tile <<= 1;
+    uint32_t hbits = 1;
+    while ((1u << hbits) < 2 * tile) ++hbits;
+    const AccTab dense{nullptr, dd_pre, nullptr, nullptr, nullptr, nullptr, 0u, uint32_t(dim)};
+    const bool vec4 = dim % 4 == 0 && uintptr_t(grads) % (gdt == SE_FLOAT32 ? 16 : 8) == 0;
+    {
+      StoreImpl::Prof pr(store, "k_ex_prereduce", st);
+      auto go = [&](auto kern) {
+        pdl(kern, grid_for(n, tile, 0x7fffffffu), kAccThreads, size_t(tile) * size_t(dim) * 4, st, dense,
+            static_cast<const void *>(dws.inverse), int(SE_KEY_UINT32), n, static_cast<const uint32_t *>(nullptr),
+            grads, gdt, 1.0f, INFINITY, tile, hbits, dd_ctr + 6, dd_ctr + 7, static_cast<const uint32_t *>(nullptr),
+            FwdCache{nullptr, nullptr, nullptr, 0u});
+      };
+      if (vec4) go(k_acc_atomic<4, false, true>);
+      else go(k_acc_atomic<1, false, true>);
+      launched("k_acc_atomic");
+    }
+    StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
+    pdl(k_ex_scatter_prerows, grid_for(n * 32, 256, 148 * 8), 256, 0, st, view, key_pid, key_slot, dws.count, size_t(M),
+        dd_pre, uint32_t(dim), gdt);
+    launched("k_ex_scatter_prerows");
   }
 
   // Waits for the stream; raises a timed-out wait, then the owner's table errors.
@@ -3829,6 +3938,13 @@ int se_exchange_accumulate_routed(se_exchange *ex, const void *grads, size_t n, 
   return guarded([&] {
     if (!ex) throw std::invalid_argument("exchange handle is null");
     ex->impl.backward_routed(grads, n, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int se_exchange_set_dedupe(se_exchange *ex, int32_t enable) {
+  return guarded([&] {
+    if (!ex) throw std::invalid_argument("exchange handle is null");
+    ex->impl.set_dedupe(enable != 0);
   });
 }
 

@@ -62,13 +62,21 @@ __device__ __forceinline__ uint64_t home_bucket(uint64_t h, uint64_t nbuckets) {
   return __umul64hi(h, nbuckets);
 }
 
-template <bool kCoherent>
+// Bucket loads: kLoadL2 bypasses L1 (ld.cg; words other SMs may be
+// writing), kLoadReadOnly takes the read-only path (ld.global.nc; no writes
+// during the launch), kLoadCached is a plain load that L1 may serve (stale
+// views are allowed: every decision on an empty slot is checked by a CAS).
+enum BucketLoad : int { kLoadL2 = 1, kLoadReadOnly = 0, kLoadCached = 2 };
+
+template <int kMode>
 __device__ __forceinline__ void load_bucket(const Bucket *b, uint64_t (&k)[kBucketSlots],
                                             uint32_t (&r)[kBucketSlots]) {
   const uint4 *p = reinterpret_cast<const uint4 *>(b);
   uint4 a0, a1, a2, a3;
-  if constexpr (kCoherent) {
+  if constexpr (kMode == kLoadL2) {
     a0 = __ldcg(p); a1 = __ldcg(p + 1); a2 = __ldcg(p + 2); a3 = __ldcg(p + 3);
+  } else if constexpr (kMode == kLoadCached) {
+    a0 = p[0]; a1 = p[1]; a2 = p[2]; a3 = p[3];
   } else {
     a0 = __ldg(p); a1 = __ldg(p + 1); a2 = __ldg(p + 2); a3 = __ldg(p + 3);
   }
@@ -92,7 +100,7 @@ __device__ __forceinline__ uint32_t dir_find(const Dir &d, uint64_t key) {
   for (uint64_t probe = 0; probe < d.nbuckets; ++probe) {
     uint64_t k[kBucketSlots];
     uint32_t r[kBucketSlots];
-    load_bucket<kCoherent>(d.buckets + b, k, r);
+    load_bucket<kCoherent ? kLoadL2 : kLoadReadOnly>(d.buckets + b, k, r);
     bool empty = false;
 #pragma unroll
     for (int s = 0; s < kBucketSlots; ++s) {
@@ -126,7 +134,7 @@ __device__ __forceinline__ InsertResult dir_find_or_insert(const Dir &d, uint64_
     Bucket *bk = d.buckets + b;
     uint64_t k[kBucketSlots];
     uint32_t r[kBucketSlots];
-    load_bucket<true>(bk, k, r);
+    load_bucket<kLoadCached>(bk, k, r);  // hot buckets from L1; claims are checked by the CAS
 #pragma unroll
     for (int s = 0; s < kBucketSlots; ++s) {
       if (k[s] == key) return {&bk->rows[s], kFound};
@@ -159,7 +167,7 @@ __device__ __forceinline__ uint32_t *dir_slot(const Dir &d, uint64_t key) {
   for (uint64_t probe = 0; probe < d.nbuckets; ++probe) {
     uint64_t k[kBucketSlots];
     uint32_t r[kBucketSlots];
-    load_bucket<true>(d.buckets + b, k, r);
+    load_bucket<kLoadL2>(d.buckets + b, k, r);
     bool empty = false;
 #pragma unroll
     for (int s = 0; s < kBucketSlots; ++s) {

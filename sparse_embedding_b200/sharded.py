@@ -93,7 +93,7 @@ class PeerExchange:
     HANDLE_BYTES = 64  # a CUDA IPC memory handle
 
     def __init__(self, store, partitioner_name: str, dim: int, max_keys_per_rank: int, group=None,
-                 timeout_ms: int = 10_000):
+                 timeout_ms: int = 10_000, dedupe: bool = False):
         import torch.distributed as dist
 
         self.dist, self.group = dist, group
@@ -110,6 +110,9 @@ class PeerExchange:
         N.check(self._lib.se_exchange_create(store._h, N.PART_CODES[kind], self.world, self.rank, self.max_keys,
                                              self.dim, int(timeout_ms), C.byref(h)))
         self._h = h
+        # every distinct key of a batch is routed once; the routed gradients
+        # are summed per key on the sender (fp32) before they are sent
+        N.check(self._lib.se_exchange_set_dedupe(h, int(bool(dedupe))))
         if not self.distributed:
             N.check(self._lib.se_exchange_connect_local((C.c_void_p * 1)(h.value), 1))
             return
@@ -170,7 +173,8 @@ class ShardedEmbeddingStore:
     """Data-parallel batches over key-sharded stores, one per rank."""
 
     def __init__(self, local_store, partitioner_name: str = "sparse_embedding.hash", group=None, router=None,
-                 transport: str = "collective", max_keys_per_rank: int | None = None, timeout_ms: int = 10_000):
+                 transport: str = "collective", max_keys_per_rank: int | None = None, timeout_ms: int = 10_000,
+                 dedupe: bool = False):
         import torch.distributed as dist
 
         if transport not in ("collective", "p2p"):
@@ -189,6 +193,10 @@ class ShardedEmbeddingStore:
         self.transport = transport
         self.max_keys_per_rank = max_keys_per_rank
         self.timeout_ms = timeout_ms
+        # p2p: route each distinct key of a batch once per sender and sum its
+        # gradient rows on the sender (rows unchanged; updates within fp32
+        # reassociation of the plain route)
+        self.dedupe = bool(dedupe)
         self._exchanges: dict[int, PeerExchange] = {}
         self.router = router if router is not None else (
             GpuRouter(partitioner_name, self.world) if transport == "collective" else None)
@@ -200,7 +208,7 @@ class ShardedEmbeddingStore:
         ex = self._exchanges.get(dim)
         if ex is None:
             ex = PeerExchange(self.store, self.partitioner_name, dim, self.max_keys_per_rank, self.group,
-                              self.timeout_ms)
+                              self.timeout_ms, dedupe=self.dedupe)
             self._exchanges[dim] = ex
         return ex
 

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, port, kind, transport, steps, q, accumulation="ordered"):
+def _worker(rank, port, kind, transport, steps, q, accumulation="ordered", dedupe=False):
     import datetime
 
     import torch.distributed as dist
@@ -41,7 +41,7 @@ def _worker(rank, port, kind, transport, steps, q, accumulation="ordered"):
                                                      accumulation=accumulation),
                                   optimizer_config=se.Adagrad(lr=0.01, eps=1e-8, initial_accumulator_value=0.1))
         sharded = ShardedEmbeddingStore(store, f"sparse_embedding.{kind}", transport=transport,
-                                        max_keys_per_rank=1024, timeout_ms=20_000)
+                                        max_keys_per_rank=1024, timeout_ms=20_000, dedupe=dedupe)
         mine, pool = batches(rank, steps)
         rows_seen = []
         for s, (keys, grads) in enumerate(mine):
@@ -60,13 +60,15 @@ def _worker(rank, port, kind, transport, steps, q, accumulation="ordered"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["collective", "p2p"])
+@pytest.mark.parametrize("transport", ["collective", "p2p", "p2p-dedupe"])
 @pytest.mark.parametrize("kind", ["hash", "fast_range"])
 @pytest.mark.parametrize("accumulation", ["ordered", "atomic"])
 def test_sharded_two_gpus_match_single_store(kind, transport, accumulation):
-    """Ordered accumulation: bit for bit. Atomic accumulation (per-key fp32
-    sums, order of the adds varies): the first step's rows bit for bit, the
-    rest within 1e-5 relative (atol 1e-5 of the values' 0.05 scale)."""
+    """Ordered accumulation over the plain routes: bit for bit. Atomic
+    accumulation (per-key fp32 sums, order of the adds varies) or sender-side
+    dedupe (gradients pre-summed per key on the sender): the first step's
+    rows bit for bit, the rest within 1e-5 relative (atol 1e-5 of the
+    values' 0.05 scale)."""
     if torch.cuda.device_count() < WORLD:
         pytest.skip("needs 2 GPUs")
     from oracle import oracle as O
@@ -75,7 +77,9 @@ def test_sharded_two_gpus_match_single_store(kind, transport, accumulation):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, kind, transport, steps, q, accumulation))
+    dedupe = transport == "p2p-dedupe"
+    procs = [ctx.Process(target=_worker, args=(r, port, kind, "p2p" if dedupe else transport, steps, q,
+                                               accumulation, dedupe))
              for r in range(WORLD)]
     for p in procs:
         p.start()
@@ -86,7 +90,7 @@ def test_sharded_two_gpus_match_single_store(kind, transport, accumulation):
     single = O.OracleStore([DIM], key_dtype="int64", optimizer="adagrad", lr=0.01, eps=1e-8, initial_accumulator=0.1)
     per_rank = [batches(r, steps)[0] for r in range(WORLD)]
     pool = batches(0, steps)[1]
-    exact = accumulation == "ordered"
+    exact = accumulation == "ordered" and not dedupe
     for s in range(steps):
         for r in range(WORLD):
             want = single.lookup_or_insert(per_rank[r][s][0], DIM)
