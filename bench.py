@@ -72,6 +72,8 @@ def args_parse():
                    help="N > 1: peer-memory exchange kernels, or NCCL all-to-all (eager)")
     p.add_argument("--loopback", action="store_true",
                    help="N = 1: route the step through a one-rank peer-memory exchange (its kernels on one GPU)")
+    p.add_argument("--no-dedupe", action="store_true",
+                   help="N > 1, p2p: route every position's key (no sender-side dedupe and pre-reduction)")
     p.add_argument("--accumulation", choices=["atomic", "ordered"], default="ordered",
                    help="how accumulate_gradients sums each key's rows: per-key fp32 sums with vector "
                         "reductions (atomic) or kept rows summed in arrival order at the step (ordered)")
@@ -268,7 +270,7 @@ def run_ours(args):
         from sparse_embedding_b200.sharded import ShardedEmbeddingStore
 
         api = ShardedEmbeddingStore(store, "sparse_embedding.hash", transport=args.transport,
-                                    max_keys_per_rank=BATCH)
+                                    max_keys_per_rank=BATCH, dedupe=not args.no_dedupe)
 
     keys_np, _ = wl.make_batches(W + 2 * K, start_step=0)
     keys_d = torch.from_numpy(keys_np).cuda()
@@ -338,7 +340,8 @@ def run_ours(args):
     # Per-kernel device time inside the timed region.
     names = list(STEP_KERNELS[args.accumulation])
     if (world > 1 and args.transport == "p2p") or args.loopback:
-        names += ["k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_scatter_rows", "k_ex_scatter_grads"]
+        names += ["k_ex_dedupe", "k_ex_scatter_keys", "k_ex_owner", "k_ex_rows_out", "k_ex_prereduce",
+                  "k_ex_scatter_rows", "k_ex_scatter_grads"]
     times = {}
     for nm in names:
         ms, cnt = store.profile_read(nm)
@@ -485,6 +488,18 @@ def run_ours(args):
         fwd = forward_bench(se, torch, N)
         if args.wide_keys > 0:
             wide = forward_wide_bench(se, torch, N, args.wide_keys)
+    if world > 1 and not args.no_forward and args.wide_keys > 0 and args.transport == "p2p":
+        if api is not store:  # the train step's exchange is done
+            api.close()
+            api = store
+        wide = forward_wide_sharded_bench(se, torch, world, rank, local, args.wide_keys)
+    capacity = None
+    if world >= 8 and not args.no_forward and args.transport == "p2p":
+        # the capacity table needs the device's memory: the train step's store goes first
+        del step, e2e_step, keys_d, grads_d
+        store = api = None
+        torch.cuda.empty_cache()
+        capacity = capacity_bench(se, torch, world, rank, local)
 
     result = {
         "metric": METRIC,
@@ -497,7 +512,8 @@ def run_ours(args):
         "dtype": "f32", "data": "synthetic",
         "config": train_config(args, world),
         "execution": {"accumulation": args.accumulation,
-                      "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none"))},
+                      "transport": (args.transport if world > 1 else ("p2p-loopback" if args.loopback else "none")),
+                      "dedupe": bool((world > 1 or args.loopback) and args.transport == "p2p" and not args.no_dedupe)},
         "timing": ("CUDA graph replay per step (captured from the public API calls)" if use_graphs
                    else "eager API calls"),
         "profiled_pass_ms_per_step": elapsed_prof / K * 1e3,
@@ -511,7 +527,13 @@ def run_ours(args):
     if wide:
         result["forward_wide"] = wide
         result["summary"]["forward_wide_mkeys_per_s"] = round(wide["value"], 1)
-        result["summary"]["forward_wide_frac_of_hbm"] = wide["frac"]
+        result["summary"]["forward_wide_frac_of_hbm"] = wide.get("frac", wide.get("hbm_frac"))
+        if "nvlink_frac" in wide:
+            result["summary"]["forward_wide_nvlink_frac"] = wide["nvlink_frac"]
+    if capacity:
+        result["capacity"] = capacity
+        if "value" in capacity:
+            result["summary"]["capacity_keys_per_s"] = capacity["value"]
     if large:
         result["train_step_large_batch"] = large
     if mut:
@@ -522,7 +544,7 @@ def run_ours(args):
         result["embedding_bag"] = bag
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=20.0)
-    if api is not store:
+    if api is not store and api is not None:
         api.close()
     if world > 1:
         import torch.distributed as dist
@@ -851,6 +873,150 @@ def forward_wide_bench(se, torch, N, num_keys):
             "value": WIDE_BATCH * WIDE_BATCHES / el / 1e6, "unit": "Mkeys/s",
             "us_per_call": el / WIDE_BATCHES * 1e6, "algorithmic_bytes_per_key": per_key,
             "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_gbs": peak}
+
+
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
+
+
+def forward_wide_sharded_bench(se, torch, world, rank, local, num_keys):
+    """The weight-only inference store sharded over the GPUs (hash
+    partitioner: rank r holds the int32 keys whose murmur fmix32 & (N-1) is
+    r, num_keys / N rows of dim 256 bf16 each), forward_lookup of 262,144-key
+    batches per GPU uniform over all keys, through the peer-memory exchange:
+    keys to their owners, rows back over NVLink (the row all-to-all). Weak
+    scaling; time = max over ranks. Per key: HBM 4 + 16 + 512 (owner's row
+    read) + 512 (row written), NVLink (4 + 512) x (N - 1) / N."""
+    from sparse_embedding_b200.sharded import ShardedEmbeddingStore
+    from sparse_embedding_b200.workloads import InferenceWorkload
+
+    owned = num_keys // world + num_keys // (world * 16) + 1_000_000
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[WIDE_DIM], key_dtype="int32", value_dtype="bfloat16",
+                                                 enable_optimizer=False, initial_capacity=owned, device=local))
+    part = se.HashPartitioner(num_shards=world)
+    chunk = 1 << 23
+    for s0 in range(0, num_keys, chunk):
+        keys = torch.arange(s0, min(s0 + chunk, num_keys), dtype=torch.int32, device="cuda")
+        mine = keys[part.filter(keys, rank)]
+        if mine.numel():
+            store.lookup_or_insert(mine, WIDE_DIM)
+    torch.cuda.synchronize()
+    api = ShardedEmbeddingStore(store, "sparse_embedding.hash", transport="p2p", max_keys_per_rank=WIDE_BATCH,
+                                dedupe=False)
+    wl = InferenceWorkload(num_keys=num_keys, dim=WIDE_DIM, batch=WIDE_BATCH, seed=0x1BF + rank)
+    batches = torch.from_numpy(wl.batches(WIDE_BATCHES)).cuda()
+    out = torch.empty((WIDE_BATCH, WIDE_DIM), dtype=torch.bfloat16, device="cuda")
+    ex = api.exchange(WIDE_DIM)
+    for i in range(3):
+        ex.lookup(batches[i], insert=False, out=out)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(WIDE_BATCHES):
+        ex.lookup(batches[i], insert=False, out=out)
+    b.record()
+    torch.cuda.synchronize()
+    el = max_over_ranks(a.elapsed_time(b) / 1e3, world)
+    api.check()
+    api.close()
+    del store
+    torch.cuda.empty_cache()
+    peak, _ = measured_hbm()
+    per_key = 4 + M_BYTES + 2 * WIDE_DIM * 2
+    link_per_key = (4 + WIDE_DIM * 2) * (world - 1) / world
+    keys_per_gpu_s = WIDE_BATCH * WIDE_BATCHES / el
+    hbm_gbs = per_key * keys_per_gpu_s / 1e9
+    link_gbs = link_per_key * keys_per_gpu_s / 1e9
+    return {"workload": f"weight-only dim 256 bf16, {num_keys:,} int32 keys hash-sharded over {world} GPUs, "
+                        f"{WIDE_BATCHES} batches x 262,144 keys per GPU uniform, rows returned over NVLink",
+            "value": world * keys_per_gpu_s / 1e6, "unit": "Mkeys/s (all GPUs)", "us_per_batch": el / WIDE_BATCHES * 1e6,
+            "hbm_gbs_per_gpu": round(hbm_gbs, 1), "hbm_frac": round(hbm_gbs / peak, 4),
+            "nvlink_gbs_per_gpu_per_direction": round(link_gbs, 1),
+            "nvlink_frac": round(link_gbs / NVLINK_PEER_GBS, 4),
+            "nvlink_peak_source": "measured peer copy 770 GB/s per direction per GPU",
+            "timing": "eager exchange calls, CUDA events, max over ranks"}
+
+
+def capacity_bench(se, torch, world, rank, local, total_keys: int = 1_500_000_000, steps: int = 10, warmup: int = 3):
+    """The capacity configuration: one table of 1.5e9 uint64 keys
+    splitmix64(i), dim 64 fp32 with Adam m / v state and a u32 step per row
+    (784 B per row: ~147 GB per B200 at 8 GPUs), modulo partitioner; each
+    rank generates its keys on the device and inserts the ones it owns
+    (after checking its free memory); then full train steps of 262,144 keys
+    per GPU (99 % Zipf(1.05) over all keys + 1 % new keys, grads N(0, 1e-3),
+    Adam) through the peer-memory exchange with sender-side dedupe and atomic
+    accumulation. Runs only where every rank has the memory (8 B200s);
+    otherwise reports why it was skipped. Time = max over ranks."""
+    import torch.distributed as dist
+
+    from sparse_embedding_b200.sharded import ShardedEmbeddingStore
+    from sparse_embedding_b200.workloads import CapacityWorkload
+
+    dim, stride = 64, 784
+    own = total_keys // world
+    cap = int(own * 1.02) + 8 * 262_144
+    dir_bytes = 64 * (1 << (int(cap / 3.5) + 1).bit_length())
+    need = cap * stride + dir_bytes + cap * 12 + (6 << 30)  # slabs, directory, row arrays, work buffers
+    free, _ = torch.cuda.mem_get_info()
+    ok = torch.tensor([1 if free > need else 0], dtype=torch.int32, device="cuda")
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()):
+        return {"skipped": f"needs ~{need / 1e9:.0f} GB per GPU over {world} GPUs; {free / 1e9:.0f} GB free "
+                           f"on rank {rank}"}
+    wl = CapacityWorkload(num_keys=total_keys, dim=dim, rank=rank)
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", device=local, initial_capacity=cap,
+                                                 accumulation="atomic"),
+                              optimizer_config=se.Adam(lr=1e-3))
+    part = se.ModuloPartitioner(num_shards=world)
+    t0 = time.perf_counter()
+    chunk = 1 << 26
+    for s0 in range(0, total_keys, chunk):
+        keys = wl.device_keys(s0, min(chunk, total_keys - s0), torch)
+        mine = keys[part.filter(keys, rank)]
+        if mine.numel():
+            store.lookup_or_insert(mine, dim)
+        del keys, mine
+    torch.cuda.synchronize()
+    warm_s = max_over_ranks(time.perf_counter() - t0, world)
+    held = store.total_size()
+    api = ShardedEmbeddingStore(store, "sparse_embedding.modulo", transport="p2p", max_keys_per_rank=wl.batch,
+                                dedupe=True)
+
+    def one(step):
+        k, g = wl.device_batch(step, torch)
+        torch.cuda.synchronize()
+        return k, g
+
+    for s in range(warmup):
+        k, g = one(s)
+        api.lookup_or_insert(k, dim)
+        api.accumulate_gradients(k, g)
+        api.optimizer_step(1)
+    batches = [one(warmup + s) for s in range(steps)]
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for k, g in batches:
+        api.lookup_or_insert(k, dim)
+        api.accumulate_gradients(k, g)
+        api.optimizer_step(1)
+    b.record()
+    torch.cuda.synchronize()
+    el = max_over_ranks(a.elapsed_time(b) / 1e3, world)
+    api.check()
+    api.close()
+    used = torch.cuda.mem_get_info()
+    del api, store, batches
+    torch.cuda.empty_cache()
+    return {"workload": f"{total_keys:,} uint64 keys splitmix64(i), dim 64 fp32 + Adam m/v + u32 step "
+                        f"({stride} B per row), modulo over {world} GPUs; 262,144-key batches per GPU, 99% "
+                        "Zipf(1.05) + 1% new, Adam, exchange with sender-side dedupe, atomic accumulation",
+            "value": world * wl.batch * steps / el, "unit": "keys/s (all GPUs)", "ms_per_step": el / steps * 1e3,
+            "keys_held_rank0": int(held), "device_bytes_in_use_rank0": int(used[1] - used[0]),
+            "warm_seconds": round(warm_s, 2), "timing": "eager API calls, CUDA events, max over ranks",
+            "zipf_sampler": "continuous inverse CDF, rank -> fmix64(rank) mod n (no stored permutation)"}
 
 
 # ---------------------------------------------------------------------------

@@ -111,20 +111,21 @@ __device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, 
 // dtypes (failures raise kStatusBadGradient in *bad_word), and the value
 // added is g (scale 1) or the scaled value rounded to the gradient dtype.
 // With kBag, entry i takes gradient row grad_row[i] (embedding-bag backward).
-// Dynamic shared memory: tile * dim floats; tile * dim <= kAccSmemBytes / 4,
-// so each thread holds at most kAccRegFloats gradient values.
 //
-// Latency: the tile's gradient rows are loaded into registers at the start,
-// while the keys are hashed, and each distinct key's table slot is found
-// while the rows are added into shared memory, so the block's chain is one
-// DRAM round trip, one L2 round trip (the slot), then fire-and-forget
-// reductions.
-constexpr uint32_t kAccRegFloats = uint32_t(kAccSmemBytes / 4 / kAccThreads);  // 32
+// The tile's gradient rows are staged in shared memory (dynamic, tile x row
+// bytes): one bulk copy through the TMA when the rows are contiguous and
+// 16-byte aligned (one per row for bag rows), else plain loads. Meanwhile
+// the keys are hashed; each distinct key gets a local index and a list of
+// its entries (shared-memory linked list), and finds or claims its table
+// slot. Then each (distinct key, 16-byte chunk) pair sums its entries'
+// chunks from shared memory and adds the sum to the table with one vector
+// reduction - no floating-point shared-memory atomics, conflict-free reads.
+constexpr uint32_t kCopySpinLimit = 1u << 26;  // polls of the bulk-copy barrier before giving up
 
 // Walks chunks c = c0, c0 + step, c0 + 2 step, ... of rows of `units`
 // chunks as (row, chunk in row) without a division per step.
 struct ChunkWalk {
-  uint32_t j, u;          // row and chunk of the current c
+  uint32_t j, u;           // row and chunk of the current c
   uint32_t dj, du, units;  // step = dj * units + du
   __device__ __forceinline__ ChunkWalk(uint32_t c0, uint32_t step, uint32_t units_)
       : j(c0 / units_), u(c0 % units_), dj(step / units_), du(step % units_), units(units_) {}
@@ -138,27 +139,24 @@ struct ChunkWalk {
   }
 };
 
-// With kDirect the "keys" are row indices of a dense fp32 sum array
-// (a.vals, [rows][dim]): each distinct index adds its tile sum into its own
-// row, with no slot claims, counts or list (a sender's gradient
-// pre-reduction by distinct key of an exchange).
 template <int VEC, bool kBag, bool kDirect = false>
 __global__ void __launch_bounds__(kAccThreads, 4)  // 4 blocks per SM: a 65,536-row batch in one wave
 k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, float scale, float maxv, uint32_t tile, uint32_t hbits,
              uint32_t *bad_word, uint32_t *status, const uint32_t *__restrict__ grad_row, FwdCache fc) {
-  extern __shared__ float s_acc[];                    // [tile][dim] sums of the tile's distinct keys
+  extern __shared__ __align__(16) uint8_t s_rows[];   // [tile][row bytes] the tile's gradient rows
   __shared__ unsigned long long s_hkey[2 * kAccMaxTile];  // hash set of the tile's keys
   __shared__ uint32_t s_hloc[2 * kAccMaxTile + 1];    // local index of each set slot; [H]: the all-ones key
-  __shared__ uint32_t s_ent[kAccMaxTile];             // set slot, then local index, of each entry
+  __shared__ uint32_t s_hpos[2 * kAccMaxTile + 1];    // an entry (tile position) of each set slot
+  __shared__ uint32_t s_ent[kAccMaxTile];             // set slot of each entry
+  __shared__ int32_t s_next[kAccMaxTile];             // next entry of the same key, -1 at the end
+  __shared__ int32_t s_head[kAccMaxTile];             // first entry of each local key
   __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
-  __shared__ uint32_t s_lcnt[kAccMaxTile];            // entries of each local index
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
-  __shared__ uint32_t s_hpos[2 * kAccMaxTile + 1];    // an entry of each set slot (its batch position - i0)
-  __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each claimed local key from the cache, or kNoRow
-  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch;
-  constexpr int CH = int(kAccRegFloats) / VEC;        // gradient chunks per thread
+  __shared__ uint32_t s_lrow[kAccMaxTile];            // tile position, then cached row, of each local key
+  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok;
+  __shared__ __align__(8) uint64_t s_bar;
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const size_t n = n_dev ? min(size_t(*n_dev), n_max) : n_max;
@@ -168,26 +166,37 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   const uint32_t H = 1u << hbits;  // >= 2 * tile
   const uint32_t dim = a.dim;
   const uint32_t tid = threadIdx.x;
+  const uint32_t gsize = gdt == SE_FLOAT32 ? 4u : 2u;
+  const uint32_t row_bytes = dim * gsize;
   const uint32_t units = dim / VEC;
-  const uint32_t chunks = m * units;  // <= CH * blockDim.x
-  // 0. the tile's gradient rows into registers (chunk c = tid + k * blockDim.x)
-  float g[CH][VEC];
-  {
-    ChunkWalk w(tid, blockDim.x, units);
-#pragma unroll
-    for (int k = 0; k < CH; ++k, w.next()) {
-      if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
-      const size_t src = kBag ? size_t(grad_row[i0 + w.j]) : i0 + w.j;
-      ldv<VEC>(grads, gdt, src * dim + w.u * VEC, g[k]);
+  // 0. stage the gradient rows
+  const uint8_t *gsrc = static_cast<const uint8_t *>(grads);
+  const bool tma = row_bytes % 16u == 0u && (reinterpret_cast<uintptr_t>(gsrc) & 15u) == 0u;
+  if (tma) {
+    if (tid == 0) {
+      mbar_init(&s_bar, 1);
+      mbar_arrive_expect_tx(&s_bar, m * row_bytes);
+      if (!kBag) bulk_copy_g2s(s_rows, gsrc + i0 * row_bytes, m * row_bytes, &s_bar);
+    }
+    __syncthreads();  // the barrier is initialised before any copy names it
+    if (kBag)
+      for (uint32_t j = tid; j < m; j += blockDim.x)
+        bulk_copy_g2s(s_rows + j * row_bytes, gsrc + size_t(grad_row[i0 + j]) * row_bytes, row_bytes, &s_bar);
+  } else {
+    for (uint32_t x = tid; x < m * (row_bytes / 2u); x += blockDim.x) {
+      const uint32_t j = x / (row_bytes / 2u), h = x - j * (row_bytes / 2u);
+      const size_t src = kBag ? size_t(grad_row[i0 + j]) : i0 + j;
+      reinterpret_cast<uint16_t *>(s_rows)[x] = reinterpret_cast<const uint16_t *>(gsrc + src * row_bytes)[h];
     }
   }
   for (uint32_t h = tid; h < H; h += blockDim.x) s_hkey[h] = kEmptyKey;
-  for (uint32_t q = tid; q < tile; q += blockDim.x) s_lcnt[q] = 0u;
+  for (uint32_t q = tid; q < tile; q += blockDim.x) s_head[q] = -1;
   if (tid == 0) {
     s_nloc = 0u;
     s_spec = 0u;
     s_nclaim = 0u;
     s_epoch = a.epoch ? __ldcg(a.epoch) : 0u;
+    s_copy_ok = 1u;
   }
   __syncthreads();
   // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
@@ -209,25 +218,6 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     }
     s_ent[j] = h;
   }
-  // validation and entry scaling of the registers (overlaps the hashing);
-  // g / 1 == g needs no division (uniform branch)
-  bool bad = false;
-#pragma unroll
-  for (int k = 0; k < CH; ++k) {
-    if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
-    if (scale == 1.0f) {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) bad |= !(fabsf(g[k][v]) <= maxv);
-    } else {
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        const float sc = __fdiv_rn(g[k][v], scale);
-        bad |= !(fabsf(sc) <= maxv);
-        g[k][v] = round_to(gdt, sc);
-      }
-    }
-  }
-  if (bad) raise_status(bad_word, kStatusBadGradient);
   __syncthreads();
   // 2. a local index per distinct key
   for (uint32_t h = tid; h <= H; h += blockDim.x) {
@@ -241,28 +231,20 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   }
   __syncthreads();
   const uint32_t nloc = s_nloc;
+  // 3. each entry joins its key's list; each distinct key finds (or claims)
+  //    its table slot (its L2 round trips overlap the lists and the copy)
   for (uint32_t j = tid; j < m; j += blockDim.x) {
     const uint32_t q = s_hloc[s_ent[j]];
-    s_ent[j] = q;
-    atomicAdd(&s_lcnt[q], 1u);
+    s_next[j] = atomicExch(&s_head[q], int32_t(j));
   }
-  if constexpr (VEC == 4) {  // rows are whole float4s
-    for (uint32_t x = tid; x < nloc * units; x += blockDim.x)
-      reinterpret_cast<float4 *>(s_acc)[x] = make_float4(0.f, 0.f, 0.f, 0.f);
-  } else {
-    for (uint32_t x = tid; x < nloc * dim; x += blockDim.x) s_acc[x] = 0.0f;
-  }
-  __syncthreads();
-  // 3. each distinct key's slot in the table (its L2 round trips overlap the
-  //    shared-memory adds of step 4)
   for (uint32_t q = tid; q < nloc; q += blockDim.x) {
-    bool claimed = false;
     const uint64_t key = s_lkey[q];
     if constexpr (kDirect) {
       s_gslot[q] = uint32_t(key);
       s_crank[q] = kNoRow;
       continue;
     }
+    bool claimed = false;
     const uint32_t slot = acc_find_or_claim(a, key, claimed);
     s_gslot[q] = slot;
     s_crank[q] = claimed ? atomicAdd(&s_nclaim, 1u) : kNoRow;
@@ -270,36 +252,65 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     // so optimizer_step need not probe the directory for it
     if (claimed) s_lrow[q] = cached_row(fc, i0 + s_lrow[q], key);
     if (slot == kNoRow) raise_status(status, kStatusTableFull);
-    else atomicAdd(a.cnt + slot, s_lcnt[q]);
-  }
-  // 4. the gradient rows into the shared sums
-  {
-    ChunkWalk w(tid, blockDim.x, units);
-#pragma unroll
-    for (int k = 0; k < CH; ++k, w.next()) {
-      if (tid + uint32_t(k) * blockDim.x >= chunks) continue;
-      float *dst = s_acc + s_ent[w.j] * dim + w.u * VEC;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) atomicAdd(dst + v, g[k][v]);
-    }
   }
   __syncthreads();
   if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);
+  if (tma) {  // every thread waits for the rows (bounded; the copy is local and completes)
+    uint32_t polls = 0;
+    while (!mbar_try_wait(&s_bar, 0u)) {
+      if (++polls > kCopySpinLimit) {
+        s_copy_ok = 0u;
+        break;
+      }
+    }
+  }
   __syncthreads();
+  if (tma && tid == 0) {
+    if (s_copy_ok) {
+      mbar_inval(&s_bar);
+    } else {
+      raise_status(status, kStatusCopyTimeout);
+      // wait (bounded) for the copy still in flight before the block's shared memory is released
+      for (uint32_t w = 0; w < kCopySpinLimit && !mbar_try_wait(&s_bar, 0u); ++w) __nanosleep(64);
+    }
+  }
+  if (!s_copy_ok) return;
   for (uint32_t q = tid; q < nloc; q += blockDim.x)
     if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = make_uint4(s_gslot[q], s_lrow[q], s_epoch, 0u);
-  // 5. the tile's sums into the table
-  const uint32_t lchunks = nloc * units;
+  // 4. per (distinct key, chunk): the sum of its entries' chunks, validated
+  //    and scaled on entry, added into the table
+  bool bad = false;
+  const uint32_t pairs = nloc * units;
   ChunkWalk w(tid, blockDim.x, units);
-  for (uint32_t c = tid; c < lchunks; c += blockDim.x, w.next()) {
-    const uint32_t slot = s_gslot[w.j];
+  for (uint32_t c = tid; c < pairs; c += blockDim.x, w.next()) {
+    const uint32_t q = w.j, e = w.u * VEC;
+    const uint32_t slot = s_gslot[q];
+    float acc[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[v] = 0.0f;
+    uint32_t count = 0;
+    for (int32_t j = s_head[q]; j >= 0; j = s_next[j], ++count) {
+      float g[VEC];
+      ldv<VEC>(s_rows + size_t(j) * row_bytes, gdt, e, g);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        if (scale == 1.0f) {  // g / 1 == g: no division (uniform branch)
+          bad |= !(fabsf(g[v]) <= maxv);
+        } else {
+          const float sc = __fdiv_rn(g[v], scale);
+          bad |= !(fabsf(sc) <= maxv);
+          g[v] = round_to(gdt, sc);
+        }
+        acc[v] = __fadd_rn(acc[v], g[v]);
+      }
+    }
     if (slot == kNoRow) continue;
-    const uint32_t e = w.u * VEC;
     float *dst = a.vals + size_t(slot) * dim + e;
-    const float *src = s_acc + w.j * dim + e;
-    if constexpr (VEC == 4) red_add_v4(dst, src[0], src[1], src[2], src[3]);
-    else atomicAdd(dst, src[0]);
+    if constexpr (VEC == 4) red_add_v4(dst, acc[0], acc[1], acc[2], acc[3]);
+    else atomicAdd(dst, acc[0]);
+    if (!kDirect && w.u == 0u) atomicAdd(a.cnt + slot, count);
   }
+  if (bad) raise_status(bad_word, kStatusBadGradient);
 }
 
 // Validation of a host batch before anything is added (the reference raises

@@ -78,6 +78,7 @@ enum StatusBits : uint32_t {
   kStatusBadGradient = 2u,     // gradient fails validate_input
   kStatusBadRow = 4u,          // row index outside the arena
   kStatusPendingOverflow = 8u, // device pending count beyond the host-sized buffers
+  kStatusCopyTimeout = 16u,    // a bulk copy into shared memory did not complete in time
 };
 
 // Programmatic dependent launch: wait for the previous kernel on the stream
@@ -86,6 +87,43 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // Lets the next kernel's blocks be scheduled as soon as this grid's blocks
 // have all started (they still wait in pdl_wait for this grid's results).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Bulk copies global -> shared memory through the tensor memory accelerator
+// (cp.async.bulk, 1-D; source and destination 16-byte aligned, size a
+// multiple of 16), completed on a shared-memory mbarrier. Local to the
+// calling CTA: no cluster multicast.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t arrivals) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(arrivals) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// One arrival that also announces `bytes` of bulk copies to come.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+               " selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(done)
+               : "r"(smem_u32(bar)), "r"(parity)
+               : "memory");
+  return done != 0u;
+}
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ void raise_status(uint32_t *status, uint32_t bits) {
   atomicOr(status, bits);

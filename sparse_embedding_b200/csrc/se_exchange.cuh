@@ -404,7 +404,7 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec i
         kind = r.kind;
         word = r.row_word;
         // found: published, claimed and not yet published (3), or erased and revived here
-        if (kind == kFound) kind = resolve_found(word, &row);
+        if (kind == kFound) kind = resolve_found(word, &row, r.seen);
         else if (kind == kFull) raise_status(status, kStatusTableFull);
       }
       // lanes of this warp still in the loop: keys i - t / LANES + [0, total)

@@ -148,13 +148,13 @@ __device__ __forceinline__ void init_slab(const Layout &L, uint8_t *slab, const 
 // 32-bit words, or 16-bit for odd half-precision rows; they are few), then
 // resets the launch's counters. Out of line, so the main path keeps its
 // register budget.
-__device__ __noinline__ void finish_deferred(const Layout &L, const uint8_t *slabs, size_t n, void *out,
-                                             uint32_t *def_count, const uint32_t *def_pos,
+// Arguments by value (scalars): a reference to a kernel parameter would make
+// every thread copy the parameter struct to its stack.
+__device__ __noinline__ void finish_deferred(uint32_t stride, size_t row_bytes, const uint8_t *slabs, size_t n,
+                                             void *out, uint32_t *def_count, const uint32_t *def_pos,
                                              const unsigned long long *def_word, uint32_t *status, uint32_t *done,
-                                             const FwdCache &fc) {
+                                             uint32_t *fc_rows, uint32_t *fc_n, bool cache) {
   __threadfence();
-  const size_t row_bytes = size_t(L.dim) * (L.pdt == SE_FLOAT32 ? 4 : 2);
-  const bool cache = fc.keys != nullptr && n <= fc.cap;
   const uint32_t count = __ldcg(def_count);
   const bool words = row_bytes % 4 == 0;
   const uint32_t units = uint32_t(words ? row_bytes / 4 : row_bytes / 2);
@@ -163,9 +163,9 @@ __device__ __noinline__ void finish_deferred(const Layout &L, const uint8_t *sla
     const size_t pos = __ldcg(def_pos + j);
     const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(__ldcg(def_word + j)));
     uint8_t *dst = static_cast<uint8_t *>(out) + pos * row_bytes;
-    if (cache && lane == 0) fc.rows[pos] = row;
+    if (cache && lane == 0) fc_rows[pos] = row;
     if (row == kNoRow && lane == 0) raise_status(status, kStatusTableFull);
-    const uint8_t *src = slabs + size_t(row) * L.stride;
+    const uint8_t *src = slabs + size_t(row) * stride;
     for (uint32_t u = lane; u < units; u += 32) {
       if (words) reinterpret_cast<uint32_t *>(dst)[u] = row == kNoRow ? 0u : __ldcg(reinterpret_cast<const uint32_t *>(src) + u);
       else reinterpret_cast<uint16_t *>(dst)[u] = row == kNoRow ? uint16_t(0) : reinterpret_cast<const uint16_t *>(src)[u];
@@ -175,7 +175,7 @@ __device__ __noinline__ void finish_deferred(const Layout &L, const uint8_t *sla
   if (threadIdx.x == 0) {
     *def_count = 0u;  // for the next launch
     *done = 0u;
-    if (fc.n) *fc.n = cache ? uint32_t(n) : 0u;
+    if (fc_n) *fc_n = cache ? uint32_t(n) : 0u;
   }
 }
 
@@ -207,7 +207,7 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, In
       kind = r.kind;
       word = r.row_word;
       // found: published, claimed in this launch (3), or erased and revived here
-      if (kind == kFound) kind = resolve_found(word, &row);
+      if (kind == kFound) kind = resolve_found(word, &row, r.seen);
       else if (kind == kFull) raise_status(status, kStatusTableFull);
     }
     const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);
@@ -253,7 +253,9 @@ k_lookup_or_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, In
     s_last = atomicAdd(done, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (s_last) finish_deferred(L, slabs, n, out, def_count, def_pos, def_word, status, done, fc);
+  if (s_last)
+    finish_deferred(L.stride, row_bytes, slabs, n, out, def_count, def_pos, def_word, status, done, fc.rows, fc.n,
+                    cache);
 }
 
 // Per-row counting of the pending entries for optimizer_step's grouping,
@@ -1453,7 +1455,7 @@ k_bag_insert(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec
     const InsertResult r = dir_find_or_insert(d, key);
     kind = r.kind;
     word = r.row_word;
-    if (kind == kFound) kind = resolve_found(word, &row);
+    if (kind == kFound) kind = resolve_found(word, &row, r.seen);
     else if (kind == kFull) raise_status(status, kStatusTableFull);
   }
   const uint32_t taken = take_rows_warp(ra, live_lanes(t, n * LANES), lane == 0 && kind == kInserted);

@@ -118,6 +118,7 @@ enum InsertKind : int { kFound = 0, kInserted = 1, kFull = 2 };
 struct InsertResult {
   uint32_t *row_word;
   int kind;
+  uint32_t seen;  // found: the row word as the probe read it (kNoRow for a claim)
 };
 
 // Find-or-claim by one thread. A claim CASes the key into the first empty
@@ -126,7 +127,7 @@ struct InsertResult {
 __device__ __forceinline__ InsertResult dir_find_or_insert(const Dir &d, uint64_t key) {
   if (key == kEmptyKey) {
     const uint32_t old = atomicCAS(d.special, 0u, 1u);
-    return {d.special + 1, old == 0u ? kInserted : kFound};
+    return {d.special + 1, old == 0u ? kInserted : kFound, kNoRow};
   }
   const uint64_t mask = d.nbuckets - 1;
   uint64_t b = home_bucket(splitmix64(key), d.nbuckets);
@@ -137,22 +138,29 @@ __device__ __forceinline__ InsertResult dir_find_or_insert(const Dir &d, uint64_
     load_bucket<kLoadCached>(bk, k, r);  // hot buckets from L1; claims are checked by the CAS
 #pragma unroll
     for (int s = 0; s < kBucketSlots; ++s) {
-      if (k[s] == key) return {&bk->rows[s], kFound};
+      if (k[s] == key) return {&bk->rows[s], kFound, r[s]};
       if (k[s] == kEmptyKey) {
         const unsigned long long old = atomicCAS(&bk->keys[s], kEmptyKey, key);
-        if (old == kEmptyKey) return {&bk->rows[s], kInserted};
-        if (old == key) return {&bk->rows[s], kFound};
+        if (old == kEmptyKey) return {&bk->rows[s], kInserted, kNoRow};
+        if (old == key) return {&bk->rows[s], kFound, kNoRow};
       }
     }
     b = (b + 1) & mask;
   }
-  return {nullptr, kFull};
+  return {nullptr, kFull, kNoRow};
 }
 
 // A found key's row word: kInserted when it was a tombstone that this thread
 // claimed back (its row is then taken like a new key's), 3 when the row is
 // not published yet (claimed in this launch), else kFound with *row set.
-__device__ __forceinline__ int resolve_found(uint32_t *word, uint32_t *row) {
+// `seen` is the word as the probe read it: a published row there is final
+// (rows change only by erase, which no insert kernel runs beside), so the
+// word is read again only when the probe saw it unpublished or erased.
+__device__ __forceinline__ int resolve_found(uint32_t *word, uint32_t *row, uint32_t seen = kNoRow) {
+  if (seen < kDeadRow) {
+    *row = seen;
+    return kFound;
+  }
   *row = __ldcg(word);
   if (*row == kDeadRow) return atomicCAS(word, kDeadRow, kNoRow) == kDeadRow ? kInserted : 3;
   return *row == kNoRow ? 3 : kFound;

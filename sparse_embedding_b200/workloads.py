@@ -196,6 +196,61 @@ class CapacityWorkload:
         return keys, grads
 
 
+    # ---- on-device generation (the stated scale: no host copy of 1.5e9 keys) ----
+    # torch has no unsigned 64-bit arithmetic for these ops, so the keys are
+    # computed on int64 tensors holding the u64 bit patterns (multiplication
+    # wraps mod 2^64; right shifts are made logical by masking).
+
+    @staticmethod
+    def _lsr(z, k: int):
+        return (z >> k) & ((1 << (64 - k)) - 1)
+
+    @classmethod
+    def _fmix64_t(cls, z):
+        z = z ^ cls._lsr(z, 30)
+        z = z * _I64_C1
+        z = z ^ cls._lsr(z, 27)
+        z = z * _I64_C2
+        return z ^ cls._lsr(z, 31)
+
+    @classmethod
+    def splitmix64_t(cls, idx):
+        """splitmix64_sequence of an int64 index tensor, as int64 bit patterns."""
+        return cls._fmix64_t((idx + 1) * _I64_GOLDEN)
+
+    def device_keys(self, start: int, count: int, torch, device="cuda"):
+        """Keys splitmix64(i) for i in [start, start + count), uint64 on the device."""
+        i = torch.arange(start, start + count, dtype=torch.int64, device=device)
+        return self.splitmix64_t(i).view(torch.uint64)
+
+    def device_batch(self, step: int, torch, device="cuda"):
+        """One batch on the device: (1 - new_fraction) Zipf(alpha) draws over
+        the keys and new_fraction never-seen keys, uint64; gradients
+        N(0, sigma) fp32. The Zipf law at this scale is sampled by the
+        continuous inverse CDF, rank = ((n^(1-a) - 1) u + 1)^(1/(1-a)), and
+        a rank goes to item fmix64(rank) mod n, which scatters the hot ranks
+        over the key space without a stored permutation."""
+        gen = torch.Generator(device=device).manual_seed((self.seed << 20) ^ (step << 8) ^ self.rank)
+        n_new = int(round(self.batch * self.new_fraction))
+        n_old = self.batch - n_new
+        u = torch.rand(n_old, generator=gen, device=device, dtype=torch.float64)
+        a1 = 1.0 - self.alpha
+        r = (((float(self.num_keys) ** a1 - 1.0) * u + 1.0) ** (1.0 / a1)).floor().clamp_(1, self.num_keys)
+        rank = r.to(torch.int64) - 1
+        item = (self._fmix64_t(rank) & 0x7FFFFFFFFFFFFFFF) % self.num_keys
+        base = self.num_keys + (step * 1024 + self.rank) * n_new
+        new = torch.arange(base, base + n_new, dtype=torch.int64, device=device)
+        keys = self.splitmix64_t(torch.cat([item, new]))
+        keys = keys[torch.randperm(self.batch, generator=gen, device=device)]
+        grads = torch.randn((self.batch, self.dim), generator=gen, device=device) * self.sigma
+        return keys.view(torch.uint64), grads
+
+
+_I64_GOLDEN = int(np.int64(np.uint64(0x9E3779B97F4A7C15).view(np.int64)))
+_I64_C1 = int(np.uint64(0xBF58476D1CE4E5B9).view(np.int64))
+_I64_C2 = int(np.uint64(0x94D049BB133111EB).view(np.int64))
+
+
 @dataclass
 class InferenceWorkload:
     """Weight-only inference store: int32 keys 0 .. num_keys-1, dim 256
