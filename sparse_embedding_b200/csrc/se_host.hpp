@@ -6,6 +6,9 @@
 
 #include <atomic>
 #include <cstdint>
+#include <mutex>
+#include <set>
+#include <tuple>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -109,6 +112,24 @@ inline void pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "cudaLaunchKernelEx");
+}
+
+// Lets `kernel` take up to `bytes` of dynamic shared memory (beyond the
+// default 48 KB of static plus dynamic). The attribute is set once per
+// kernel, device and size (the first call; a graph capture then finds it set).
+template <class... KArgs>
+inline void allow_dynamic_smem(void (*kernel)(KArgs...), size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void *, int, size_t>> done;
+  int dev = 0;
+  cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), dev, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return;
+  cuda_check(cudaFuncSetAttribute(reinterpret_cast<const void *>(kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(bytes)),
+             "cudaFuncSetAttribute");
+  done.insert(key);
 }
 
 inline unsigned grid_for(size_t work_items, unsigned per_block, unsigned cap = 1u << 20) {

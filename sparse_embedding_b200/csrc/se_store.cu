@@ -2802,6 +2802,7 @@ struct StoreImpl {
       const unsigned grid = grid_for(n, t.acc_tile, 0x7fffffffu);
       const size_t smem = size_t(t.acc_tile) * size_t(dim) * 4;
       auto go = [&](auto kern) {
+        allow_dynamic_smem(kern, smem);
         pdl(kern, grid, kAccThreads, smem, st, t.acc_tab(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
             cfg.gradient_scale, maxv, t.acc_tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row,
             t.fwd_cache());
@@ -3488,6 +3489,7 @@ struct ExchangeImpl {
     {
       StoreImpl::Prof pr(store, "k_ex_prereduce", st);
       auto go = [&](auto kern) {
+        allow_dynamic_smem(kern, size_t(tile) * size_t(dim) * 4);
         pdl(kern, grid_for(n, tile, 0x7fffffffu), kAccThreads, size_t(tile) * size_t(dim) * 4, st, dense,
             static_cast<const void *>(dws.inverse), int(SE_KEY_UINT32), n, static_cast<const uint32_t *>(nullptr),
             grads, gdt, 1.0f, INFINITY, tile, hbits, dd_ctr + 6, dd_ctr + 7, static_cast<const uint32_t *>(nullptr),
