@@ -65,6 +65,7 @@ __device__ __forceinline__ uint32_t cached_row(const FwdCache &fc, size_t pos, u
 
 constexpr uint32_t kAccThreads = 256;
 constexpr uint32_t kAccMaxTile = 256;        // rows per block of k_acc_atomic
+static_assert(kAccMaxTile <= kAccThreads, "k_acc_atomic gives each entry and each distinct key its own thread");
 constexpr uint64_t kAccSmemBytes = 32768;    // shared-memory sums per block
 constexpr uint32_t kAccMaxDim = 8192;        // longest row of an atomic-mode table (one row per tile)
 
@@ -81,16 +82,14 @@ __device__ __forceinline__ uint32_t acc_find_or_claim(const AccTab &a, uint64_t 
   }
   uint32_t s = uint32_t(__umul64hi(splitmix64(key), uint64_t(G)));
   for (uint32_t probe = 0; probe < G; ++probe) {
-    const unsigned long long k = __ldcg(a.keys + s);
-    if (k == key) return s;
-    if (k == kEmptyKey) {
-      const unsigned long long old = atomicCAS(a.keys + s, kEmptyKey, key);
-      if (old == kEmptyKey) {
-        claimed = true;
-        return s;
-      }
-      if (old == key) return s;
+    // one L2 round trip per slot: the CAS both claims a free slot and
+    // reports the key already there
+    const unsigned long long old = atomicCAS(a.keys + s, kEmptyKey, key);
+    if (old == kEmptyKey) {
+      claimed = true;
+      return s;
     }
+    if (old == key) return s;
     s = (s + 1u) & a.mask;
   }
   return kNoRow;
@@ -154,7 +153,8 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
-  __shared__ uint32_t s_lrow[kAccMaxTile];            // tile position, then cached row, of each local key
+  __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each local key from the forward's cache, or kNoRow
+  __shared__ uint32_t s_erow[kAccMaxTile];            // the same, per entry
   __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok;
   __shared__ __align__(8) uint64_t s_bar;
   pdl_wait();
@@ -169,6 +169,16 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   const uint32_t gsize = gdt == SE_FLOAT32 ? 4u : 2u;
   const uint32_t row_bytes = dim * gsize;
   const uint32_t units = dim / VEC;
+  const uint32_t lane = tid & 31u;
+  // The entry of this thread (tile <= blockDim): its key and the row the
+  // forward cached for it, loaded first so their latency overlaps the set-up.
+  const bool has_entry = tid < m;
+  uint64_t my_key = kEmptyKey;
+  uint32_t my_row = kNoRow;
+  if (has_entry) {
+    my_key = load_key(keys, kdt, i0 + tid);
+    if (!kDirect) my_row = cached_row(fc, i0 + tid, my_key);
+  }
   // 0. stage the gradient rows
   const uint8_t *gsrc = static_cast<const uint8_t *>(grads);
   const bool tma = row_bytes % 16u == 0u && (reinterpret_cast<uintptr_t>(gsrc) & 15u) == 0u;
@@ -201,8 +211,10 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __syncthreads();
   // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
   //    takes slot H)
-  for (uint32_t j = tid; j < m; j += blockDim.x) {
-    const uint64_t key = load_key(keys, kdt, i0 + j);
+  if (has_entry) {
+    const uint32_t j = tid;
+    const uint64_t key = my_key;
+    s_erow[j] = my_row;
     uint32_t h = H;
     if (key == kEmptyKey) {
       s_spec = 1u;
@@ -219,39 +231,52 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_ent[j] = h;
   }
   __syncthreads();
-  // 2. a local index per distinct key
-  for (uint32_t h = tid; h <= H; h += blockDim.x) {
-    const bool used = h < H ? s_hkey[h] != kEmptyKey : s_spec != 0u;
+  // 2. a local index per distinct key (one counter atomic per warp)
+  for (uint32_t h0 = 0; h0 <= H; h0 += blockDim.x) {
+    const uint32_t h = h0 + tid;
+    const bool used = h < H ? s_hkey[h] != kEmptyKey : (h == H && s_spec != 0u);
+    const unsigned ballot = __ballot_sync(0xffffffffu, used);
+    uint32_t base = 0;
+    if (ballot && lane == uint32_t(__ffs(ballot) - 1)) base = atomicAdd(&s_nloc, uint32_t(__popc(ballot)));
+    base = __shfl_sync(0xffffffffu, base, ballot ? __ffs(ballot) - 1 : 0);
     if (used) {
-      const uint32_t q = atomicAdd(&s_nloc, 1u);
+      const uint32_t q = base + __popc(ballot & ((1u << lane) - 1u));
       s_hloc[h] = q;
       s_lkey[q] = h < H ? s_hkey[h] : kEmptyKey;
-      s_lrow[q] = s_hpos[h];  // the entry's tile position until step 3 turns it into a row
+      s_lrow[q] = s_erow[s_hpos[h]];
     }
   }
   __syncthreads();
   const uint32_t nloc = s_nloc;
   // 3. each entry joins its key's list; each distinct key finds (or claims)
   //    its table slot (its L2 round trips overlap the lists and the copy)
-  for (uint32_t j = tid; j < m; j += blockDim.x) {
-    const uint32_t q = s_hloc[s_ent[j]];
-    s_next[j] = atomicExch(&s_head[q], int32_t(j));
+  if (has_entry) {
+    const uint32_t q = s_hloc[s_ent[tid]];
+    s_next[tid] = atomicExch(&s_head[q], int32_t(tid));
   }
-  for (uint32_t q = tid; q < nloc; q += blockDim.x) {
-    const uint64_t key = s_lkey[q];
-    if constexpr (kDirect) {
-      s_gslot[q] = uint32_t(key);
-      s_crank[q] = kNoRow;
-      continue;
-    }
+  {  // nloc <= tile <= blockDim: one local key per thread at most
+    const uint32_t q = tid;
+    const bool mine = q < nloc;
     bool claimed = false;
-    const uint32_t slot = acc_find_or_claim(a, key, claimed);
-    s_gslot[q] = slot;
-    s_crank[q] = claimed ? atomicAdd(&s_nclaim, 1u) : kNoRow;
-    // the claimant lists the key's row when lookup_or_insert left it cached,
-    // so optimizer_step need not probe the directory for it
-    if (claimed) s_lrow[q] = cached_row(fc, i0 + s_lrow[q], key);
-    if (slot == kNoRow) raise_status(status, kStatusTableFull);
+    uint32_t slot = kNoRow;
+    if (mine) {
+      const uint64_t key = s_lkey[q];
+      if (kDirect) {
+        slot = uint32_t(key);
+      } else {
+        slot = acc_find_or_claim(a, key, claimed);
+        if (slot == kNoRow) raise_status(status, kStatusTableFull);
+      }
+      s_gslot[q] = slot;
+    }
+    // ranks among the block's claims (one counter atomic per warp); the
+    // claimant lists the row lookup_or_insert cached for its key, so
+    // optimizer_step need not probe the directory for it
+    const unsigned ballot = __ballot_sync(0xffffffffu, claimed);
+    uint32_t base = 0;
+    if (ballot && lane == uint32_t(__ffs(ballot) - 1)) base = atomicAdd(&s_nclaim, uint32_t(__popc(ballot)));
+    base = __shfl_sync(0xffffffffu, base, ballot ? __ffs(ballot) - 1 : 0);
+    if (mine) s_crank[q] = claimed ? base + __popc(ballot & ((1u << lane) - 1u)) : kNoRow;
   }
   __syncthreads();
   if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);

@@ -6,9 +6,9 @@
 
 #include <atomic>
 #include <cstdint>
+#include <map>
 #include <mutex>
-#include <set>
-#include <tuple>
+#include <utility>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -115,21 +115,23 @@ inline void pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t 
 }
 
 // Lets `kernel` take up to `bytes` of dynamic shared memory (beyond the
-// default 48 KB of static plus dynamic). The attribute is set once per
-// kernel, device and size (the first call; a graph capture then finds it set).
+// default 48 KB of static plus dynamic). The attribute only grows: it is
+// set when a launch needs more than any before on this device (the first
+// such call; a graph capture of the same sizes then finds it set).
 template <class... KArgs>
 inline void allow_dynamic_smem(void (*kernel)(KArgs...), size_t bytes) {
   static std::mutex mu;
-  static std::set<std::tuple<const void *, int, size_t>> done;
+  static std::map<std::pair<const void *, int>, size_t> allowed;
   int dev = 0;
   cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
-  const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), dev, bytes);
+  const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count(key)) return;
+  auto it = allowed.find(key);
+  if (it != allowed.end() && it->second >= bytes) return;
   cuda_check(cudaFuncSetAttribute(reinterpret_cast<const void *>(kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(bytes)),
              "cudaFuncSetAttribute");
-  done.insert(key);
+  allowed[key] = bytes;
 }
 
 inline unsigned grid_for(size_t work_items, unsigned per_block, unsigned cap = 1u << 20) {
