@@ -34,16 +34,36 @@
 namespace se_gpu {
 
 // Hash table of one store table's gradient sums for the current window.
+// A slot holds (key, dense row) in one 16-byte word, claimed by one 128-bit
+// CAS, so a block that finds the key learns its dense row in the same
+// round trip. The sums live in `vals` by dense row: each block reserves one
+// dense row per entry of its tile up front, and a claim takes the row
+// reserved for that key; the rows in use stay in the front of `vals`, the
+// same region every window (L2-resident from one step to the next).
 struct AccTab {
-  unsigned long long *keys;  // [G] key of each slot, kEmptyKey when free
-  float *vals;               // [(G + 1) * dim] fp32 sums, zero when free; slot G holds the all-ones key
+  ulonglong2 *slots;         // [G + 1] (key, dense row); free: all ones; slot G holds the all-ones key
+  float *vals;               // [vcap][dim] fp32 sums by dense row, zero when free
   uint32_t *cnt;             // [G + 1] gradient rows summed into each slot
-  uint4 *list;               // [G + 1] claimed slots in claim order: (slot, row, erase epoch, 0)
-  uint32_t *ctr;             // [0] claimed slots, [1] claim flag of slot G, [2] finished apply blocks
+  uint4 *list;               // [G + 1] claimed slots in claim order: (slot, cached row, erase epoch, dense row)
+  uint32_t *ctr;             // [0] claimed slots, [2] finished apply blocks, [3] dense rows reserved
   const uint32_t *epoch;     // the table's erase epoch (bumped by every erase)
   uint32_t mask;             // G - 1; G is a power of two
   uint32_t dim;
+  uint32_t vcap;             // dense rows `vals` holds
 };
+
+constexpr unsigned long long kAccFree = ~0ull;  // dense-row half of a free slot
+
+// 128-bit compare-and-swap of a slot (sm_90+): returns the old word.
+__device__ __forceinline__ ulonglong2 cas_slot(ulonglong2 *p, ulonglong2 expect, ulonglong2 desire) {
+  ulonglong2 old;
+  asm volatile("{\n .reg .b128 c, v, o;\n mov.b128 c, {%2, %3};\n mov.b128 v, {%4, %5};\n"
+               " atom.global.cas.b128 o, [%6], c, v;\n mov.b128 {%0, %1}, o;\n}"
+               : "=l"(old.x), "=l"(old.y)
+               : "l"(expect.x), "l"(expect.y), "l"(desire.x), "l"(desire.y), "l"(p)
+               : "memory");
+  return old;
+}
 
 // Keys and rows the last lookup_or_insert resolved, by batch position (the
 // accumulate of the same batch finds its rows here instead of probing the
@@ -69,27 +89,33 @@ static_assert(kAccMaxTile <= kAccThreads, "k_acc_atomic gives each entry and eac
 constexpr uint64_t kAccSmemBytes = 32768;    // shared-memory sums per block
 constexpr uint32_t kAccMaxDim = 8192;        // longest row of an atomic-mode table (one row per tile)
 
-// Slot of `key`, claiming a free one if the key has none; `claimed` tells
-// the caller to list the slot. Linear probing from the high bits of the
-// SplitMix64 hash (hash-partitioned GPUs share the low bits). kNoRow when
-// every slot is taken (the host sizes the table at twice the window's rows).
-__device__ __forceinline__ uint32_t acc_find_or_claim(const AccTab &a, uint64_t key, bool &claimed) {
+// Slot of `key`, claiming a free one with dense row `rank` if the key has
+// none (`claimed` tells the caller to list the slot); *vrow receives the
+// key's dense row either way. Linear probing from the high bits of the
+// SplitMix64 hash (hash-partitioned GPUs share the low bits); the all-ones
+// key has slot G. kNoRow when every slot is taken (the host sizes the table
+// at twice the window's rows).
+__device__ __forceinline__ uint32_t acc_find_or_claim(const AccTab &a, uint64_t key, uint32_t rank, bool &claimed,
+                                                      uint32_t &vrow) {
   claimed = false;
   const uint32_t G = a.mask + 1u;
-  if (key == kEmptyKey) {
-    claimed = atomicCAS(a.ctr + 1, 0u, 1u) == 0u;
-    return G;
-  }
-  uint32_t s = uint32_t(__umul64hi(splitmix64(key), uint64_t(G)));
+  const ulonglong2 free_word = make_ulonglong2(kEmptyKey, kAccFree);
+  const ulonglong2 mine = make_ulonglong2(key, rank);
+  uint32_t s = key == kEmptyKey ? G : uint32_t(__umul64hi(splitmix64(key), uint64_t(G)));
   for (uint32_t probe = 0; probe < G; ++probe) {
-    // one L2 round trip per slot: the CAS both claims a free slot and
-    // reports the key already there
-    const unsigned long long old = atomicCAS(a.keys + s, kEmptyKey, key);
-    if (old == kEmptyKey) {
+    // one L2 round trip per slot: the CAS claims a free slot or reports the
+    // key (and its dense row) already there
+    const ulonglong2 old = cas_slot(a.slots + s, free_word, mine);
+    if (old.x == kEmptyKey && old.y == kAccFree) {
       claimed = true;
+      vrow = rank;
       return s;
     }
-    if (old == key) return s;
+    if (old.x == key) {
+      vrow = uint32_t(old.y);
+      return s;
+    }
+    if (s == G) break;  // slot G holds only the all-ones key
     s = (s + 1u) & a.mask;
   }
   return kNoRow;
@@ -152,10 +178,11 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ int32_t s_head[kAccMaxTile];             // first entry of each local key
   __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
+  __shared__ uint32_t s_vrow[kAccMaxTile];            // dense sum row of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
   __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each local key from the forward's cache, or kNoRow
   __shared__ uint32_t s_erow[kAccMaxTile];            // the same, per entry
-  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok;
+  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok, s_rank_base;
   __shared__ __align__(8) uint64_t s_bar;
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
@@ -207,6 +234,8 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_nclaim = 0u;
     s_epoch = a.epoch ? __ldcg(a.epoch) : 0u;
     s_copy_ok = 1u;
+    // dense sum rows for the tile's keys that this block may claim
+    s_rank_base = kDirect ? 0u : atomicAdd(a.ctr + 3, m);
   }
   __syncthreads();
   // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
@@ -258,16 +287,18 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     const uint32_t q = tid;
     const bool mine = q < nloc;
     bool claimed = false;
-    uint32_t slot = kNoRow;
+    uint32_t slot = kNoRow, vrow = kNoRow;
     if (mine) {
       const uint64_t key = s_lkey[q];
       if (kDirect) {
-        slot = uint32_t(key);
+        slot = vrow = uint32_t(key);
       } else {
-        slot = acc_find_or_claim(a, key, claimed);
+        const uint32_t rank = s_rank_base + q;
+        if (rank < a.vcap) slot = acc_find_or_claim(a, key, rank, claimed, vrow);
         if (slot == kNoRow) raise_status(status, kStatusTableFull);
       }
       s_gslot[q] = slot;
+      s_vrow[q] = vrow;
     }
     // ranks among the block's claims (one counter atomic per warp); the
     // claimant lists the row lookup_or_insert cached for its key, so
@@ -301,7 +332,8 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   }
   if (!s_copy_ok) return;
   for (uint32_t q = tid; q < nloc; q += blockDim.x)
-    if (s_crank[q] != kNoRow) a.list[s_claim_base + s_crank[q]] = make_uint4(s_gslot[q], s_lrow[q], s_epoch, 0u);
+    if (s_crank[q] != kNoRow)
+      a.list[s_claim_base + s_crank[q]] = make_uint4(s_gslot[q], s_lrow[q], s_epoch, s_vrow[q]);
   // 4. per (distinct key, chunk): the sum of its entries' chunks, validated
   //    and scaled on entry, added into the table
   bool bad = false;
@@ -330,7 +362,7 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
       }
     }
     if (slot == kNoRow) continue;
-    float *dst = a.vals + size_t(slot) * dim + e;
+    float *dst = a.vals + size_t(s_vrow[q]) * dim + e;
     if constexpr (VEC == 4) red_add_v4(dst, acc[0], acc[1], acc[2], acc[3]);
     else atomicAdd(dst, acc[0]);
     if (!kDirect && w.u == 0u) atomicAdd(a.cnt + slot, count);
@@ -357,25 +389,25 @@ k_acc_check(const void *__restrict__ grads, int gdt, size_t elems, float scale, 
 }
 
 // Moves every claimed slot into a larger table (the window outgrew the old
-// one between accumulate calls). One thread per listed slot.
+// one between accumulate calls), keeping its dense row; the host copies the
+// dense sums. One thread per listed slot.
 __global__ void __launch_bounds__(256) k_acc_move(AccTab from, AccTab to, uint32_t *status) {
   const uint32_t G = from.mask + 1u;
   const uint32_t n = min(*from.ctr, G + 1u);
+  if (blockIdx.x == 0 && threadIdx.x == 0) to.ctr[3] = from.ctr[3];  // dense rows stay where they are
   for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < n; g += gridDim.x * blockDim.x) {
     const uint4 ent = from.list[g];
     const uint32_t slot = ent.x;
-    const uint64_t key = slot == G ? kEmptyKey : from.keys[slot];
+    const uint64_t key = from.slots[slot].x;
     bool claimed = false;
-    const uint32_t ns = acc_find_or_claim(to, key, claimed);
+    uint32_t vrow = kNoRow;
+    const uint32_t ns = acc_find_or_claim(to, key, ent.w, claimed, vrow);
     if (ns == kNoRow) {
       raise_status(status, kStatusTableFull);
       continue;
     }
-    to.list[atomicAdd(to.ctr, 1u)] = make_uint4(ns, ent.y, ent.z, 0u);
+    to.list[atomicAdd(to.ctr, 1u)] = make_uint4(ns, ent.y, ent.z, ent.w);
     to.cnt[ns] = from.cnt[slot];
-    const float *s = from.vals + size_t(slot) * from.dim;
-    float *d = to.vals + size_t(ns) * to.dim;
-    for (uint32_t e = 0; e < from.dim; ++e) d[e] = s[e];
   }
 }
 

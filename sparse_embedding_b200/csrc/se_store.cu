@@ -1021,12 +1021,11 @@ k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in
   for (size_t g = t / LANES; g < nslots; g += groups) {
     const uint4 ent = __ldcg(a.list + g);
     const uint32_t slot = ent.x;
-    float *acc = a.vals + size_t(slot) * L.dim;
+    float *acc = a.vals + size_t(ent.w) * L.dim;  // the slot's dense sum row
     // the row the accumulate listed (from lookup_or_insert) while no erase
     // happened since; else the key is resolved in the directory now
     uint32_t row = ent.z == epoch ? ent.y : kNoRow;
-    if (lane == 0 && apply && row == kNoRow)
-      row = dir_find<false>(d, slot == G ? kEmptyKey : uint64_t(__ldcg(a.keys + slot)));
+    if (lane == 0 && apply && row == kNoRow) row = dir_find<false>(d, uint64_t(__ldcg(&a.slots[slot].x)));
     row = __shfl_sync(mask, row, 0, LANES);
     if (apply && row == kNoRow) {
       if (lane == 0) atomicAdd(dropped, (unsigned long long)__ldcg(a.cnt + slot));
@@ -1070,15 +1069,15 @@ k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in
     }
     if (lane == 0) {
       a.cnt[slot] = 0u;
-      if (slot != G) a.keys[slot] = kEmptyKey;
+      a.slots[slot] = make_ulonglong2(kEmptyKey, kAccFree);
     }
   }
-  // every block has read the claim counter: the last one resets it
+  // every block has read the claim counter: the last one resets the counters
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(a.ctr + 2, 1u) == gridDim.x - 1) {
     a.ctr[0] = 0u;
-    a.ctr[1] = 0u;
     a.ctr[2] = 0u;
+    a.ctr[3] = 0u;
   }
 }
 
@@ -1732,13 +1731,14 @@ struct Table {
   bool atomic = false;
   uint32_t acc_tile = 0, acc_hbits = 0;  // rows per block of k_acc_atomic, its hash-set bits
   uint64_t acc_slots = 0;                // G (0: not allocated yet)
-  unsigned long long *acc_keys = nullptr;
+  uint64_t acc_vcap = 0;                 // dense sum rows
+  ulonglong2 *acc_keys = nullptr;        // slots: (key, dense row)
   float *acc_vals = nullptr;
   uint32_t *acc_cnt = nullptr, *acc_ctr = nullptr;
   uint4 *acc_list = nullptr;
   AccTab acc_tab() const {
     return AccTab{acc_keys, acc_vals, acc_cnt, acc_list, acc_ctr, ctr + kCtrEraseEpoch, uint32_t(acc_slots - 1),
-                  uint32_t(dim)};
+                  uint32_t(dim), uint32_t(acc_vcap)};
   }
 
   Dir dir() const { return Dir{buckets, nbuckets, ctr + kCtrSpecialClaim}; }
@@ -2064,17 +2064,21 @@ struct StoreImpl {
                                   "step of the same size before capturing");
     if (need > (1ull << 31)) throw Error(SE_ERR_RUNTIME, "more than 2^30 gradient rows in one window");
     const uint64_t G = next_pow2(std::max<uint64_t>(need, 1024));
-    auto *nk = dalloc<unsigned long long>(G);
-    auto *nv = dalloc<float>(size_t(G + 1) * size_t(t.dim));
+    const uint64_t V = G / 2;  // dense sum rows: one per gradient row of the window at most
+    auto *nk = dalloc<ulonglong2>(G + 1);
+    auto *nv = dalloc<float>(size_t(V) * size_t(t.dim));
     auto *nc = dalloc<uint32_t>(G + 1);
     auto *nl = dalloc<uint4>(G + 1);
     auto *nctr = dalloc<uint32_t>(4);
-    cuda_check(cudaMemsetAsync(nk, 0xff, G * 8, st), "memset sums");
-    cuda_check(cudaMemsetAsync(nv, 0, size_t(G + 1) * size_t(t.dim) * 4, st), "memset sums");
+    cuda_check(cudaMemsetAsync(nk, 0xff, (G + 1) * sizeof(ulonglong2), st), "memset sums");  // all free
+    cuda_check(cudaMemsetAsync(nv, 0, size_t(V) * size_t(t.dim) * 4, st), "memset sums");
     cuda_check(cudaMemsetAsync(nc, 0, (G + 1) * 4, st), "memset sums");
     cuda_check(cudaMemsetAsync(nctr, 0, 16, st), "memset sums");
-    const AccTab to{nk, nv, nc, nl, nctr, t.ctr + kCtrEraseEpoch, uint32_t(G - 1), uint32_t(t.dim)};
+    const AccTab to{nk, nv, nc, nl, nctr, t.ctr + kCtrEraseEpoch, uint32_t(G - 1), uint32_t(t.dim), uint32_t(V)};
     if (t.acc_slots) {
+      // the claimed slots move; their dense sums are copied as they are
+      cuda_check(cudaMemcpyAsync(nv, t.acc_vals, size_t(t.acc_vcap) * size_t(t.dim) * 4, cudaMemcpyDeviceToDevice,
+                                 st), "grow sums");
       k_acc_move<<<grid_for(t.acc_slots + 1, 256, 148 * 8), 256, 0, st>>>(t.acc_tab(), to, t.ctr + kCtrStatus);
       launched("k_acc_move");
     }
@@ -2090,6 +2094,7 @@ struct StoreImpl {
     t.acc_list = nl;
     t.acc_ctr = nctr;
     t.acc_slots = G;
+    t.acc_vcap = V;
   }
 
   void ensure_bc(uint64_t steps) {
@@ -3040,8 +3045,8 @@ struct StoreImpl {
       cuda_check(cudaMemsetAsync(t.ctr + kCtrSpecialRow, 0xff, 4, st), "clear special");
       cuda_check(cudaMemsetAsync(t.row_cnt, 0, t.capacity * 4, st), "clear row counters");
       if (t.acc_slots) {
-        cuda_check(cudaMemsetAsync(t.acc_keys, 0xff, t.acc_slots * 8, st), "clear sums");
-        cuda_check(cudaMemsetAsync(t.acc_vals, 0, size_t(t.acc_slots + 1) * size_t(t.dim) * 4, st), "clear sums");
+        cuda_check(cudaMemsetAsync(t.acc_keys, 0xff, (t.acc_slots + 1) * sizeof(ulonglong2), st), "clear sums");
+        cuda_check(cudaMemsetAsync(t.acc_vals, 0, size_t(t.acc_vcap) * size_t(t.dim) * 4, st), "clear sums");
         cuda_check(cudaMemsetAsync(t.acc_cnt, 0, (t.acc_slots + 1) * 4, st), "clear sums");
         cuda_check(cudaMemsetAsync(t.acc_ctr, 0, 16, st), "clear sums");
       }
@@ -3484,7 +3489,7 @@ struct ExchangeImpl {
     while (tile < kAccMaxTile && uint64_t(tile) * 2 * uint64_t(dim) * 4 <= kAccSmemBytes) tile <<= 1;
     uint32_t hbits = 1;
     while ((1u << hbits) < 2 * tile) ++hbits;
-    const AccTab dense{nullptr, dd_pre, nullptr, nullptr, nullptr, nullptr, 0u, uint32_t(dim)};
+    const AccTab dense{nullptr, dd_pre, nullptr, nullptr, nullptr, nullptr, 0u, uint32_t(dim), uint32_t(M)};
     const bool vec4 = dim % 4 == 0 && uintptr_t(grads) % (gdt == SE_FLOAT32 ? 16 : 8) == 0;
     {
       StoreImpl::Prof pr(store, "k_ex_prereduce", st);
