@@ -77,6 +77,12 @@ def args_parse():
     p.add_argument("--accumulation", choices=["atomic", "ordered"], default="ordered",
                    help="how accumulate_gradients sums each key's rows: per-key fp32 sums with vector "
                         "reductions (atomic) or kept rows summed in arrival order at the step (ordered)")
+    p.add_argument("--capacity", action="store_true",
+                   help="N >= 8, p2p: after the train step, run the 1.5e9-key capacity configuration "
+                        "(~160 GB per GPU)")
+    p.add_argument("--dlrm", action="store_true",
+                   help="N > 1, p2p: after the train step, run the DLRM configuration sharded (26 tables up to "
+                        "4e7 rows, fast_range, global batch of 8,192 samples)")
     p.add_argument("--bag-only", type=int, default=0, metavar="SAMPLES",
                    help="run only the DLRM-shaped embedding-bag step with this many samples per batch "
                         "(a small case for profiling) and print its JSON")
@@ -493,8 +499,15 @@ def run_ours(args):
             api.close()
             api = store
         wide = forward_wide_sharded_bench(se, torch, world, rank, local, args.wide_keys)
+    dlrm = None
+    if args.dlrm and world > 1 and args.transport == "p2p":
+        if api is not store:
+            api.close()
+            api = store
+        dlrm = dlrm_sharded_bench(se, torch, world, rank, local, peak)
+    finding = encode_keys_finding(se, torch, world) if rank == 0 and not args.no_forward else None
     capacity = None
-    if world >= 8 and not args.no_forward and args.transport == "p2p":
+    if args.capacity and world >= 8 and args.transport == "p2p":
         # the capacity table needs the device's memory: the train step's store goes first
         del step, e2e_step, keys_d, grads_d
         store = api = None
@@ -530,6 +543,11 @@ def run_ours(args):
         result["summary"]["forward_wide_frac_of_hbm"] = wide.get("frac", wide.get("hbm_frac"))
         if "nvlink_frac" in wide:
             result["summary"]["forward_wide_nvlink_frac"] = wide["nvlink_frac"]
+    if dlrm:
+        result["dlrm_sharded"] = dlrm
+        result["summary"]["dlrm_sharded_ids_per_s"] = dlrm["value"]
+    if finding:
+        result["encode_keys_fast_range"] = finding
     if capacity:
         result["capacity"] = capacity
         if "value" in capacity:
@@ -758,31 +776,32 @@ def unique_bench(se, torch, num_keys):
                         "Zipf 1.05 + 5% new), device-resident", "batches": out}
 
 
-def dlrm_bag_bench(se, torch, peak, samples: int = 8192, capacity: int = 8_000_000):
-    """DLRM-shaped embedding-bag step: 26 tables' pre-mixed u64 keys in one
-    dim-128 fp32 store with Adam(1e-3); 8,192 samples x 26 tables x
-    max(1, Poisson(20)) ids (~4.3M ids per step) drawn Zipf(1.2) over each
-    table's rows (1e3..2e6 rows per table, log-uniform: the reference config's
-    shape with its row ranges scaled down so the batches are generated in
-    seconds); step = embedding_bag with insert -> embedding_bag_backward of
-    N(0, 1e-3) pooled gradients -> optimizer_step(1). Eager calls, CUDA events."""
+def dlrm_bag_bench(se, torch, peak, samples: int = 8192, capacity: int = 0):
+    """DLRM-shaped embedding-bag step on one GPU: 26 tables' pre-mixed u64
+    keys in one dim-128 fp32 store with Adam(1e-3); `samples` samples x 26
+    tables x max(1, Poisson(20)) ids (~4.3M ids per step at 8,192 samples)
+    drawn Zipf(1.2) over each table's rows (1e3..4e7 rows per table,
+    log-uniform, seeded; generated on the device); step = embedding_bag with
+    insert -> embedding_bag_backward of N(0, 1e-3) pooled gradients ->
+    optimizer_step(1). Eager calls, CUDA events."""
     from sparse_embedding_b200.workloads import DlrmWorkload
 
-    wl = DlrmWorkload(max_rows=2_000_000, batch=samples)
+    wl = DlrmWorkload(batch=samples)
     dim = wl.dim
-    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", initial_capacity=capacity),
-                              optimizer_config=se.Adam(lr=1e-3))
     steps, warm = 4, 2
     batches = []
     for s in range(warm + steps):
         # the first warm-up batch is 10% larger, so the store's step buffers
         # (sized by the largest window so far) are grown before the timed steps
-        src = DlrmWorkload(max_rows=2_000_000, batch=samples + samples // 10) if s == 0 else wl
-        k, o, g = src.make_bags(s)
-        batches.append((torch.from_numpy(k.view(np.int64)).cuda().view(torch.uint64), torch.from_numpy(o).cuda(),
-                        torch.from_numpy(g).cuda()))
+        src = DlrmWorkload(batch=samples + samples // 10) if s == 0 else wl
+        k, o, _, g = src.device_bags(s, torch)
+        batches.append((k, o, g))
     ids = [int(b[0].numel()) for b in batches[warm:]]
     uniq = [int(torch.unique(b[0].view(torch.int64)).numel()) for b in batches[warm:]]
+    if capacity <= 0:  # every distinct key of all the batches, with room
+        capacity = int(1.2 * sum(int(torch.unique(b[0].view(torch.int64)).numel()) for b in batches)) + (1 << 20)
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", initial_capacity=capacity),
+                              optimizer_config=se.Adam(lr=1e-3))
 
     def step(b):
         k, o, g = b
@@ -816,7 +835,7 @@ def dlrm_bag_bench(se, torch, peak, samples: int = 8192, capacity: int = 8_000_0
     pool_bytes = sum(uniq) / len(uniq) * R + sum(ids) / len(ids) * 4 + nb * R
     pool_gbs = pool_bytes / (kern.get("k_bag_pool", float("nan")) / 1e6) / 1e9
     out = {"workload": f"DLRM-shaped bag step: 26 tables, {samples:,} samples, dim 128 fp32, Adam; "
-                       "rows per table 1e3..2e6 (scaled down from 4e7)",
+                       "rows per table 1e3..4e7 (seeded log-uniform), ids generated on the device",
            "ids_per_step": int(sum(ids) / len(ids)), "unique_ids_per_step": int(sum(uniq) / len(uniq)),
            "bags_per_step": nb, "us_per_step": round(el / steps * 1e6, 1),
            "value": sum(ids) / el, "unit": "ids/s", "kernel_us": kern, "rows": store.total_size(),
@@ -935,6 +954,99 @@ def forward_wide_sharded_bench(se, torch, world, rank, local, num_keys):
             "nvlink_frac": round(link_gbs / NVLINK_PEER_GBS, 4),
             "nvlink_peak_source": "measured peer copy 770 GB/s per direction per GPU",
             "timing": "eager exchange calls, CUDA events, max over ranks"}
+
+
+def encode_keys_finding(se, torch, world):
+    """fast_range over the reference's encode_keys layout, measured: the
+    share of each shard for 26 tables' ids (table id in the top 16 bits),
+    for raw ids, and for the pre-mixed keys the DLRM step uses."""
+    from sparse_embedding_b200.workloads import DlrmWorkload
+
+    wl = DlrmWorkload(batch=512)
+    keys, _, bag, _ = wl.device_bags(0, torch)
+    table = bag % wl.tables
+    # the raw ids behind the pre-mixed keys are not kept: draw ids of the same
+    # tables uniformly below each table's row count
+    rows = torch.as_tensor(wl.table_rows(), dtype=torch.int64, device="cuda")
+    raw_ids = (torch.rand(table.numel(), device="cuda", dtype=torch.float64) * rows[table]).to(torch.int64)
+    encoded = torch.zeros_like(raw_ids)
+    for t in range(wl.tables):
+        sel = table == t
+        encoded[sel] = DlrmWorkload.encode_keys_like(raw_ids[sel], t)
+    part = se.FastRangePartitioner(num_shards=max(world, 8))
+
+    def shares(k):
+        p = part.partition(k).to(torch.int64)
+        h = torch.bincount(p, minlength=part.num_shards).double()
+        return [round(float(x), 4) for x in (h / h.sum()).tolist()]
+
+    return {"shards": part.num_shards, "ids": int(table.numel()),
+            "encode_keys_16bit_prefix": shares(encoded.view(torch.uint64)),
+            "raw_ids": shares(raw_ids.view(torch.uint64)),
+            "premixed_fmix64": shares(keys),
+            "note": "fast_range(key, n) = (key * n) >> 64 keeps the top bits: table ids < 2^16 / n in the top 16 "
+                    "bits, and ids < 2^64 / n, all land on shard 0; the step's pre-mixed keys spread evenly"}
+
+
+def dlrm_sharded_bench(se, torch, world, rank, local, peak, samples: int = 8192, steps: int = 4, warm: int = 2):
+    """The DLRM configuration at its stated scale: 26 tables with 1e3..4e7
+    rows (log-uniform, seeded), dim 128 fp32, Adam(1e-3), fast_range
+    partitioner over the GPUs; a global batch of `samples` samples split over
+    the ranks (strong scaling), per (sample, table) max(1, Poisson(20)) ids
+    drawn Zipf(1.2), generated on the device. Step per rank: sharded
+    lookup_or_insert of its ids through the peer-memory exchange (sender-side
+    dedupe, atomic accumulation) -> sum-pool per (sample, table) in torch ->
+    pooled N(0, 1e-3) gradients broadcast back to each id ->
+    accumulate_gradients -> optimizer_step(1). Time = max over ranks."""
+    from sparse_embedding_b200.sharded import ShardedEmbeddingStore
+    from sparse_embedding_b200.workloads import DlrmWorkload
+
+    per_rank = max(1, samples // world)
+    wl = DlrmWorkload(batch=per_rank, max_rows=40_000_000, rank=rank)
+    dim = wl.dim
+    batches = [wl.device_bags(s, torch) for s in range(warm + steps)]
+    n_max = max(int(b[0].numel()) for b in batches)
+    ids = sum(int(b[0].numel()) for b in batches[warm:]) / steps
+    capacity = int(1.3 * n_max * (warm + steps)) + (1 << 20)  # rows this rank may own after all batches
+    store = se.EmbeddingStore(se.EmbeddingConfig(dims=[dim], key_dtype="uint64", device=local,
+                                                 initial_capacity=capacity, accumulation="atomic"),
+                              optimizer_config=se.Adam(lr=1e-3))
+    api = ShardedEmbeddingStore(store, "sparse_embedding.fast_range", transport="p2p",
+                                max_keys_per_rank=n_max + n_max // 8, dedupe=True)
+
+    def step(b):
+        k, o, bag, g = b
+        rows = api.lookup_or_insert(k, dim)
+        pooled = torch.zeros((g.shape[0], dim), dtype=torch.float32, device="cuda").index_add_(0, bag, rows)
+        grads = g.index_select(0, bag)
+        api.accumulate_gradients(k, grads)
+        api.optimizer_step(1)
+        return pooled
+
+    for b in batches[:warm]:
+        step(b)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for b in batches[warm:]:
+        step(b)
+    e.record()
+    torch.cuda.synchronize()
+    el = max_over_ranks(a.elapsed_time(e) / 1e3, world)
+    api.check()
+    held = store.total_size()
+    api.close()
+    total_ids = sum_over_ranks(ids, world)
+    del store, api, batches
+    torch.cuda.empty_cache()
+    return {"workload": f"DLRM: 26 tables, rows 1e3..4e7 per table (seeded log-uniform), dim 128 fp32, Adam(1e-3), "
+                        f"fast_range over {world} GPUs, global batch {per_rank * world:,} samples "
+                        f"({per_rank:,} per GPU), max(1, Poisson(20)) ids per bag, Zipf(1.2), pre-mixed u64 keys",
+            "value": total_ids * steps / el, "unit": "ids/s (all GPUs)", "ms_per_step": el / steps * 1e3,
+            "ids_per_step_all_gpus": int(total_ids), "rows_held_rank0": int(held),
+            "step": "sharded lookup_or_insert -> torch sum-pool -> pooled grads to ids -> accumulate -> Adam step",
+            "timing": "eager calls, CUDA events, max over ranks", "scaling": "strong (global batch fixed)"}
 
 
 def capacity_bench(se, torch, world, rank, local, total_keys: int = 1_500_000_000, steps: int = 10, warmup: int = 3):
@@ -1118,8 +1230,7 @@ def main():
 
         peak, _ = measured_hbm()
         # room for the rows in use plus one batch of keys (the insert bound)
-        cap = min(8_000_000, max(2_000_000, args.bag_only * 26 * 40))
-        print(json.dumps(dlrm_bag_bench(se, torch, peak, samples=args.bag_only, capacity=cap)), flush=True)
+        print(json.dumps(dlrm_bag_bench(se, torch, peak, samples=args.bag_only)), flush=True)
         return
     if args.impl == "reference":
         out = run_reference(args)

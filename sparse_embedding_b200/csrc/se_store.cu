@@ -311,7 +311,7 @@ __device__ __forceinline__ void count_entries(const CountWs &c, bool valid, uint
 // With kBag the gradient row of entry i is row grad_row[i] of `grads` (the
 // backward of a sum-pooled bag: every key of bag b gets the bag's gradient).
 template <int VEC, bool kBag = false>
-__global__ void __launch_bounds__(256, 4)  // 4 blocks per SM: its 148 x 4 grid in one wave
+__global__ void __launch_bounds__(256)
 k_accumulate(Dir d, const void *__restrict__ keys, int kdt, size_t n_max, const uint32_t *n_dev,
              const void *__restrict__ grads, int gdt, uint32_t dim, float scale, float maxv,
              unsigned long long *__restrict__ pkeys_base, uint32_t *__restrict__ prows_base,

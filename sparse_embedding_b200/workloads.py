@@ -160,6 +160,49 @@ class DlrmWorkload:
         offsets[1:] = np.cumsum(np.bincount(bag, minlength=self.batch * self.tables))
         return keys[order], offsets, pooled
 
+    def device_bags(self, step: int, torch, device="cuda"):
+        """One batch grouped by bag, generated on the device (the stated row
+        ranges up to 4e7 per table without host-side samplers): (keys uint64
+        [n] ordered by bag = sample * tables + table; offsets int64
+        [batch * tables + 1]; bag of each id int64 [n]; pooled grads
+        [batch * tables, dim] float32). Same laws as make_bags, other draws:
+        counts max(1, Poisson(mean_ids)); the Zipf(alpha) rank of an id by the
+        continuous inverse CDF over the table's rows n_t,
+        rank = ((n_t^(1-a) - 1) u + 1)^(1/(1-a)), and the rank goes to row
+        fmix64((t << 40) | rank) mod n_t, which scatters each table's hot
+        rows without a stored permutation."""
+        gen = torch.Generator(device=device).manual_seed((self.seed << 24) ^ (step << 8) ^ self.rank)
+        T, B = self.tables, self.batch
+        rows = torch.as_tensor(self.table_rows(), dtype=torch.int64, device=device)
+        lam = torch.full((B, T), float(self.mean_ids), dtype=torch.float32, device=device)
+        counts = torch.poisson(lam, generator=gen).to(torch.int64).clamp_(min=1).reshape(-1)
+        offsets = torch.zeros(B * T + 1, dtype=torch.int64, device=device)
+        torch.cumsum(counts, 0, out=offsets[1:])
+        bag = torch.repeat_interleave(torch.arange(B * T, dtype=torch.int64, device=device), counts)
+        table = bag % T
+        n_t = rows[table]
+        u = torch.rand(bag.numel(), generator=gen, device=device, dtype=torch.float64)
+        a1 = 1.0 - self.alpha
+        r = (((n_t.to(torch.float64) ** a1 - 1.0) * u + 1.0) ** (1.0 / a1)).floor()
+        rank = torch.minimum(r.to(torch.int64), n_t).clamp_(min=1) - 1
+        mixed = CapacityWorkload._fmix64_t((table << 40) | rank)
+        ids = (mixed & 0x7FFFFFFFFFFFFFFF) % n_t
+        keys = CapacityWorkload._fmix64_t((table << 40) | ids)
+        pooled = torch.randn((B * T, self.dim), generator=gen, device=device) * self.sigma
+        return keys.view(torch.uint64), offsets, bag, pooled
+
+    @staticmethod
+    def encode_keys_like(ids, table: int, slot_bits: int = 16):
+        """The reference's encode_keys layout, (table << (64 - slot_bits)) |
+        (id & mask), on an int64 tensor of raw ids (returned as int64 bit
+        patterns): the table-prefixed keys that fast_range sends to one
+        shard."""
+        mask = (1 << (64 - slot_bits)) - 1
+        prefix = table << (64 - slot_bits)
+        if prefix >= 1 << 63:
+            prefix -= 1 << 64
+        return (ids & mask) | prefix
+
 
 @dataclass
 class CapacityWorkload:
