@@ -1229,7 +1229,6 @@ def main():
         import sparse_embedding_b200 as se
 
         peak, _ = measured_hbm()
-        # room for the rows in use plus one batch of keys (the insert bound)
         print(json.dumps(dlrm_bag_bench(se, torch, peak, samples=args.bag_only)), flush=True)
         return
     if args.impl == "reference":
