@@ -387,19 +387,20 @@ def run_ours(args):
         rooflines.append({"kernel": label, "ms_total": ms, "algorithmic_bytes_per_launch": int(nbytes),
                           "achieved_gbs": round(nbytes / per / 1e9, 1)})
     dom = max(rooflines, key=lambda k: k["ms_total"])
-    # DRAM bytes (read + write) per launch from one ncu --set full capture of
-    # the same kernels on the same 65,536-key batch shape with a 2M-key table
-    # (profiles/train_step_2M_dim64_full.md; the 10M-key table is too large
-    # to capture under the capture-size rule). Below the algorithmic bytes:
-    # every hot key's row is read once and served from L2 after that.
-    dram = {"k_group_apply+k_group_hot": 23.881e6 + 6.710e6, "k_lookup_or_insert": 9.461e6,
-            "k_accumulate": 22.183e6 + 0.011e6}
-    local = world == 1 and not args.loopback  # the captured kernels are the local store's
-    traffic = dram.get(dom["kernel"]) if local else None
+    # DRAM bytes (read + write) per launch, copied from ncu --set full
+    # captures of the same kernels on the same 65,536-key batch shape with a
+    # 2M-key table (the 10M-key table is above the capture-size rule); not
+    # measured by this run. Cold-cache replays: each capture starts with an
+    # empty L2, so hot keys' rows and the accumulation tables miss once.
+    dram = {"k_group_apply+k_group_hot": 23.881e6 + 6.710e6, "k_accumulate": 22.183e6 + 0.011e6,
+            "k_lookup_or_insert": 9.531e6 + 0.071e6, "k_acc_atomic": 26.451e6, "k_acc_apply": 20.057e6 + 0.048e6}
+    local_store = world == 1 and not args.loopback  # the captured kernels are the local store's
+    traffic = dram.get(dom["kernel"]) if local_store else None
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": dom["achieved_gbs"], "peak": peak,
                 "unit": "GB/s", "frac": round(dom["achieved_gbs"] / peak, 4), "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, 2M-key table, "
-                                  "same batch shape" if traffic else None,
+                "traffic_source": ("copied, not measured in this run: ncu dram__bytes_read.sum + "
+                                   "dram__bytes_write.sum of one cold-cache launch of this kernel, 2M-key table, "
+                                   "same 65,536-key batch shape") if traffic else None,
                 "peak_source": peak_kind, "per_kernel": rooflines}
     step_bytes = units["k_lookup_or_insert"][1] + BATCH * (KEY_BYTES + R) + mean_u * 4 * R
     step_roof = {"algorithmic_bytes_per_step_per_gpu": int(step_bytes),

@@ -20,7 +20,8 @@ CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libse_gpu.so"
 SOURCES = ["se_store.cu", "se_partition.cu", "se_unique.cu"]
-HEADERS = ["se_common.cuh", "se_host.hpp", "se_store_kernels.cuh", "se_partition.cuh", "se_exchange.cuh"]
+HEADERS = ["se_common.cuh", "se_host.hpp", "se_store_kernels.cuh", "se_partition.cuh", "se_exchange.cuh",
+           "se_accum.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
