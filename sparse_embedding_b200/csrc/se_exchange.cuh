@@ -571,22 +571,62 @@ struct DedupeWs {
 
 // Distinct keys of the batch, claim order: ukeys[idx] is the idx-th claimed
 // key (same dtype as the batch), pos_slot[i] the set slot of position i.
-// Bounded probing; the set holds at least twice the batch.
+// Each block first folds its 256 positions' keys in a shared-memory set, so
+// only one thread per (block, distinct key) goes to the global set: a Zipf
+// batch's hottest key costs one global CAS per block instead of one per
+// position. Bounded probing; the global set holds at least twice the batch.
+constexpr uint32_t kDedupeBlock = 256;
 template <class K>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDedupeBlock)
 k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__restrict__ ukeys) {
+  constexpr uint32_t H = 2 * kDedupeBlock;         // block set slots; H itself: the all-ones key
+  __shared__ unsigned long long s_key[H];
+  __shared__ uint32_t s_gslot[H + 1];              // global set slot of each block slot
+  __shared__ bool s_failed;
   pdl_wait();
   pdl_trigger();
-  if (ex_failed(x)) return;
-  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint32_t tid = threadIdx.x;
+  for (uint32_t h = tid; h < H; h += blockDim.x) s_key[h] = kEmptyKey;
+  if (tid == 0) s_failed = ex_failed(x);
+  __syncthreads();
+  if (s_failed) return;  // whole block
+  const size_t i = size_t(blockIdx.x) * blockDim.x + tid;
   const uint32_t D = w.mask + 1u;
-  bool claimed = false;
-  uint32_t slot = kNoRow;
   K k{};
+  uint64_t key = kEmptyKey;
+  uint32_t hl = kNoRow;  // block slot of this position's key
+  bool leader = false;   // first position of the key in this block
   if (i < n) {
     k = keys[i];
-    const uint64_t key = key_u64(k);
+    key = key_u64(k);
     if (key == kEmptyKey) {
+      hl = H;
+    } else {
+      uint32_t h = uint32_t(splitmix64(key) >> 32) & (H - 1u);
+      for (uint32_t probe = 0; probe < H; ++probe) {  // at most half full: ends at the key or a free slot
+        const unsigned long long old = atomicCAS(&s_key[h], kEmptyKey, key);
+        if (old == kEmptyKey || old == key) {
+          leader = old == kEmptyKey;
+          hl = h;
+          break;
+        }
+        h = (h + 1u) & (H - 1u);
+      }
+    }
+  }
+  // the all-ones key's block leader: its first position in the block
+  const unsigned spec_mask = __ballot_sync(0xffffffffu, hl == H);
+  __shared__ uint32_t s_spec_first;
+  if (tid == 0) s_spec_first = kNoRow;
+  __syncthreads();
+  if (spec_mask && (tid & 31u) == uint32_t(__ffs(spec_mask) - 1)) atomicMin(&s_spec_first, tid);
+  __syncthreads();
+  if (hl == H) leader = tid == s_spec_first;
+  // leaders find or claim the key's global slot
+  bool claimed = false;
+  if (leader) {
+    uint32_t slot = kNoRow;
+    if (hl == H) {
       slot = D;
       claimed = atomicCAS(w.spec, 0u, 1u) == 0u;
     } else {
@@ -601,21 +641,25 @@ k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__res
         h = (h + 1u) & w.mask;
       }
     }
-    w.pos_slot[i] = slot;
+    s_gslot[hl] = slot;
   }
   // one counter atomic per warp for its claims
-  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t lane = tid & 31u;
   const unsigned claims = __ballot_sync(0xffffffffu, claimed);
-  if (claims == 0u) return;
-  uint32_t base = 0;
-  if (lane == uint32_t(__ffs(claims) - 1)) base = atomicAdd(w.count, uint32_t(__popc(claims)));
-  base = __shfl_sync(0xffffffffu, base, __ffs(claims) - 1);
-  if (claimed) {
-    const uint32_t idx = base + __popc(claims & ((1u << lane) - 1u));
-    w.set_idx[slot] = idx;
-    w.uslot[idx] = slot;
-    ukeys[idx] = k;
+  if (claims) {
+    uint32_t base = 0;
+    if (lane == uint32_t(__ffs(claims) - 1)) base = atomicAdd(w.count, uint32_t(__popc(claims)));
+    base = __shfl_sync(0xffffffffu, base, __ffs(claims) - 1);
+    if (claimed) {
+      const uint32_t idx = base + __popc(claims & ((1u << lane) - 1u));
+      const uint32_t slot = s_gslot[hl];
+      w.set_idx[slot] = idx;
+      w.uslot[idx] = slot;
+      ukeys[idx] = k;
+    }
   }
+  __syncthreads();
+  if (i < n) w.pos_slot[i] = hl == kNoRow ? kNoRow : s_gslot[hl];
 }
 
 // inverse[i]: the distinct-key index of position i.
@@ -630,24 +674,44 @@ __global__ void __launch_bounds__(256) k_ex_dedupe_inverse(ExView x, size_t n, D
 }
 
 // Requester of a deduplicated forward: waits for the rows of every owner
-// (stream order), then out[i] = row buffer[inverse[i]] in units U; also
-// empties the dedupe set for the next forward, and its last block resets
-// the previous forward's counters.
+// (stream order), then out[i] = row buffer[inverse[i]] in units U (a team of
+// `team` lanes per position, kIlp positions in flight); also empties the
+// dedupe set for the next forward, and its last block resets the previous
+// forward's counters.
 template <class U>
 __global__ void __launch_bounds__(256)
-k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, DedupeWs w) {
+k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, DedupeWs w, uint32_t team) {
   pdl_wait();
   pdl_trigger();
-  const bool failed = ex_failed(x);
+  __shared__ bool s_failed;
+  if (threadIdx.x == 0) s_failed = ex_failed(x);
+  __syncthreads();
   const U *src = reinterpret_cast<const U *>(x.rows(x.me));
-  const size_t total = n * units;
-  const size_t stride = size_t(gridDim.x) * blockDim.x;
   const size_t tid = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (!failed) {
-    for (size_t c = tid; c < total; c += stride) {
-      const size_t i = c / units, u = c - i * units;
-      const uint32_t idx = __ldcg(w.inverse + i);
-      out[c] = __ldcg(src + size_t(min(idx, x.M - 1u)) * units + u);
+  const size_t stride = size_t(gridDim.x) * blockDim.x;
+  if (!s_failed) {
+    constexpr int kIlp = 4;
+    const uint32_t lane = threadIdx.x & 31u, sub = lane & (team - 1u), per = 32u / team;
+    const size_t step = (stride >> 5) * per;
+    for (size_t i0 = (tid >> 5) * per + lane / team; i0 < n; i0 += step * kIlp) {
+      const U *s[kIlp];
+      U *d[kIlp];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k) {
+        const size_t i = i0 + k * step;
+        const uint32_t idx = i < n ? __ldcg(w.inverse + i) : 0u;
+        s[k] = i < n ? src + size_t(min(idx, x.M - 1u)) * units : nullptr;
+        d[k] = i < n ? out + i * units : nullptr;
+      }
+      for (uint32_t c = sub; c < units; c += team) {
+        U v[kIlp];
+#pragma unroll
+        for (int k = 0; k < kIlp; ++k)
+          if (s[k]) v[k] = __ldcg(s[k] + c);
+#pragma unroll
+        for (int k = 0; k < kIlp; ++k)
+          if (d[k]) d[k][c] = v[k];
+      }
     }
   }
   const uint32_t nd = min(__ldcg(w.count), x.M);
@@ -669,30 +733,67 @@ k_ex_rows_out_dedupe(ExView x, U *__restrict__ out, size_t n, uint32_t units, De
 // Pre-reduced gradient rows of a deduplicated forward's keys: distinct key
 // u's fp32 sum (pre[u], `dim` floats) goes to slot key_slot[u] of owner
 // key_pid[u]'s gradient inbox, in the gradient dtype; the sum is zeroed for
-// the next call. One warp per row.
+// the next call. kVec (fp32 gradients, dim % 4 == 0): a team of `team`
+// lanes moves one row in 16-byte units and keeps kIlp rows in flight;
+// otherwise one warp per row, one value per lane.
+template <bool kVec>
 __global__ void __launch_bounds__(256)
 k_ex_scatter_prerows(ExView x, const uint32_t *__restrict__ key_pid, const uint32_t *__restrict__ key_slot,
-                     const uint32_t *count_dev, size_t n_max, float *__restrict__ pre, uint32_t dim, int gdt) {
+                     const uint32_t *count_dev, size_t n_max, float *__restrict__ pre, uint32_t dim, int gdt,
+                     uint32_t team) {
   pdl_wait();
   pdl_trigger();
   __shared__ uint8_t *inbox_of[kExMaxRanks];
-  if (ex_failed(x)) return;
+  __shared__ bool s_failed;
+  if (threadIdx.x == 0) s_failed = ex_failed(x);
   for (uint32_t p = threadIdx.x; p < x.W; p += blockDim.x) inbox_of[p] = x.ingrads(p);
   __syncthreads();
-  const size_t nd = min(size_t(*count_dev), n_max);
+  if (s_failed) return;
+  const size_t nd = min(size_t(__ldcg(count_dev)), n_max);
   const uint32_t inbox = x.W * x.M;
   const uint32_t lane = threadIdx.x & 31u;
+  const size_t warp = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const size_t warps = (size_t(gridDim.x) * blockDim.x) >> 5;
-  for (size_t u = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < nd; u += warps) {
-    const uint32_t slot = key_slot[u];
-    float *src = pre + u * dim;
-    uint8_t *dst = slot < inbox ? inbox_of[key_pid[u]] + size_t(slot) * x.grad_bytes : nullptr;
-    for (uint32_t e = lane; e < dim; e += 32) {
-      const float v = src[e];
-      src[e] = 0.0f;
-      if (dst == nullptr) continue;
-      if (gdt == SE_FLOAT32) reinterpret_cast<float *>(dst)[e] = v;
-      else reinterpret_cast<uint16_t *>(dst)[e] = uint16_t(f_to_bits(gdt, v));
+  if constexpr (kVec) {
+    constexpr int kIlp = 4;
+    const uint32_t sub = lane & (team - 1u), per = 32u / team, units = dim / 4u;
+    const size_t step = warps * per;
+    for (size_t u0 = warp * per + lane / team; u0 < nd; u0 += step * kIlp) {
+      float4 *src[kIlp];
+      float4 *dst[kIlp];
+#pragma unroll
+      for (int k = 0; k < kIlp; ++k) {
+        const size_t u = u0 + k * step;
+        const uint32_t slot = u < nd ? __ldcg(key_slot + u) : inbox;
+        src[k] = u < nd ? reinterpret_cast<float4 *>(pre + u * dim) : nullptr;
+        dst[k] = slot < inbox ? reinterpret_cast<float4 *>(inbox_of[__ldcg(key_pid + u)] + size_t(slot) * x.grad_bytes)
+                              : nullptr;
+      }
+      for (uint32_t c = sub; c < units; c += team) {
+        float4 v[kIlp];
+#pragma unroll
+        for (int k = 0; k < kIlp; ++k)
+          if (src[k]) v[k] = __ldcg(src[k] + c);
+#pragma unroll
+        for (int k = 0; k < kIlp; ++k) {
+          if (!src[k]) continue;
+          src[k][c] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (dst[k]) dst[k][c] = v[k];
+        }
+      }
+    }
+  } else {
+    for (size_t u = warp; u < nd; u += warps) {
+      const uint32_t slot = __ldcg(key_slot + u);
+      float *src = pre + u * dim;
+      uint8_t *dst = slot < inbox ? inbox_of[__ldcg(key_pid + u)] + size_t(slot) * x.grad_bytes : nullptr;
+      for (uint32_t e = lane; e < dim; e += 32) {
+        const float v = __ldcg(src + e);
+        src[e] = 0.0f;
+        if (dst == nullptr) continue;
+        if (gdt == SE_FLOAT32) reinterpret_cast<float *>(dst)[e] = v;
+        else reinterpret_cast<uint16_t *>(dst)[e] = uint16_t(f_to_bits(gdt, v));
+      }
     }
   }
 }

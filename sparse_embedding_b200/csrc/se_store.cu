@@ -3402,8 +3402,11 @@ struct ExchangeImpl {
       const size_t units = bytes / sizeof(U);
       StoreImpl::Prof pr(store, "k_ex_rows_out", st);
       if (dd) {  // expand the distinct keys' rows to the batch's positions
-        pdl(k_ex_rows_out_dedupe<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), n,
-            uint32_t(view.row_bytes / sizeof(U)), dws);
+        const uint32_t row_units = uint32_t(view.row_bytes / sizeof(U));
+        uint32_t team = 1;
+        while (team < 32 && team < row_units) team <<= 1;
+        pdl(k_ex_rows_out_dedupe<U>, grid_for(n * team, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), n,
+            row_units, dws, team);
       } else {
         pdl(k_ex_rows_out<U>, grid_for(units, 256, 148 * 8), 256, 0, st, view, static_cast<U *>(out), units);
       }
@@ -3505,8 +3508,15 @@ struct ExchangeImpl {
       launched("k_acc_atomic");
     }
     StoreImpl::Prof pr(store, "k_ex_scatter_rows", st);
-    pdl(k_ex_scatter_prerows, grid_for(n * 32, 256, 148 * 8), 256, 0, st, view, key_pid, key_slot, dws.count, size_t(M),
-        dd_pre, uint32_t(dim), gdt);
+    if (gdt == SE_FLOAT32 && dim % 4 == 0) {  // 16-byte units: team lanes per row
+      uint32_t team = 1;
+      while (team < 32 && team < uint32_t(dim / 4)) team <<= 1;
+      pdl(k_ex_scatter_prerows<true>, grid_for(n * team, 256, 148 * 8), 256, 0, st, view, key_pid, key_slot,
+          dws.count, size_t(M), dd_pre, uint32_t(dim), gdt, team);
+    } else {
+      pdl(k_ex_scatter_prerows<false>, grid_for(n * 32, 256, 148 * 8), 256, 0, st, view, key_pid, key_slot,
+          dws.count, size_t(M), dd_pre, uint32_t(dim), gdt, 32u);
+    }
     launched("k_ex_scatter_prerows");
   }
 
