@@ -12,6 +12,9 @@ Workload ("train step", one step per data-parallel batch, per GPU):
   the GPUs by the hash partitioner (N > 1: keys, rows and gradients cross
   NVLink through the library's peer-memory exchange kernels).
   Weak scaling: 65,536 keys per GPU per step.
+  Accumulation (--accumulation): "atomic" (default; per-key fp32 sums with
+  vector reductions, updates within 1e-5 of the ordered sum) or "ordered"
+  (each key's rows summed in arrival order, bit-exact with the reference).
 
 Also reported (rank 0, 1 GPU): the forward-lookup workload - dim-32 fp32
 store warmed with 1,000,000 uint64 keys, 400 batches of 4,096 keys Zipf(1.1).
@@ -74,7 +77,7 @@ def args_parse():
                    help="N = 1: route the step through a one-rank peer-memory exchange (its kernels on one GPU)")
     p.add_argument("--no-dedupe", action="store_true",
                    help="N > 1, p2p: route every position's key (no sender-side dedupe and pre-reduction)")
-    p.add_argument("--accumulation", choices=["atomic", "ordered"], default="ordered",
+    p.add_argument("--accumulation", choices=["atomic", "ordered"], default="atomic",
                    help="how accumulate_gradients sums each key's rows: per-key fp32 sums with vector "
                         "reductions (atomic) or kept rows summed in arrival order at the step (ordered)")
     p.add_argument("--capacity", action="store_true",
