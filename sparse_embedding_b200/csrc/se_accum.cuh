@@ -76,11 +76,14 @@ struct FwdCache {
 };
 
 // Row of key `key` at batch position pos from the cache, or kNoRow.
+// The count, the key and the row are loaded together (one round trip): every
+// position below cap is inside the cache's arrays.
 __device__ __forceinline__ uint32_t cached_row(const FwdCache &fc, size_t pos, uint64_t key) {
-  if (fc.n == nullptr || fc.keys == nullptr) return kNoRow;
-  const size_t cached = min(size_t(__ldcg(fc.n)), size_t(fc.cap));
-  if (pos >= cached || __ldcg(fc.keys + pos) != key) return kNoRow;
-  return __ldcg(fc.rows + pos);
+  if (fc.n == nullptr || fc.keys == nullptr || pos >= size_t(fc.cap)) return kNoRow;
+  const uint32_t cached = __ldcg(fc.n);
+  const unsigned long long k = __ldcg(fc.keys + pos);
+  const uint32_t row = __ldcg(fc.rows + pos);
+  return pos < size_t(cached) && k == key ? row : kNoRow;
 }
 
 constexpr uint32_t kAccThreads = 256;
@@ -172,8 +175,6 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   extern __shared__ __align__(16) uint8_t s_rows[];   // [tile][row bytes] the tile's gradient rows
   __shared__ unsigned long long s_hkey[2 * kAccMaxTile];  // hash set of the tile's keys
   __shared__ uint32_t s_hloc[2 * kAccMaxTile + 1];    // local index of each set slot; [H]: the all-ones key
-  __shared__ uint32_t s_hpos[2 * kAccMaxTile + 1];    // an entry (tile position) of each set slot
-  __shared__ uint32_t s_ent[kAccMaxTile];             // set slot of each entry
   __shared__ int32_t s_next[kAccMaxTile];             // next entry of the same key, -1 at the end
   __shared__ int32_t s_head[kAccMaxTile];             // first entry of each local key
   __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
@@ -181,7 +182,6 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ uint32_t s_vrow[kAccMaxTile];            // dense sum row of each local index
   __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
   __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each local key from the forward's cache, or kNoRow
-  __shared__ uint32_t s_erow[kAccMaxTile];            // the same, per entry
   __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok, s_rank_base;
   __shared__ __align__(8) uint64_t s_bar;
   pdl_wait();
@@ -238,50 +238,58 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     s_rank_base = kDirect ? 0u : atomicAdd(a.ctr + 3, m);
   }
   __syncthreads();
-  // 1. the tile's distinct keys (the all-ones key, the set's empty marker,
-  //    takes slot H)
-  if (has_entry) {
-    const uint32_t j = tid;
-    const uint64_t key = my_key;
-    s_erow[j] = my_row;
-    uint32_t h = H;
-    if (key == kEmptyKey) {
-      s_spec = 1u;
-      s_hpos[H] = j;
+  // 1. the tile's distinct keys. The lanes of a warp holding the same key
+  //    find each other (match); the lowest of them inserts the key into the
+  //    block's hash set (the all-ones key, the set's empty marker, takes slot
+  //    H), and the warp that inserts a key first gives it its local index.
+  const unsigned entries = __ballot_sync(0xffffffffu, has_entry);
+  const unsigned peers = __match_any_sync(0xffffffffu, my_key) & entries;
+  const uint32_t leader = peers ? uint32_t(__ffs(peers) - 1) : lane;
+  bool first = false;
+  uint32_t h = H;
+  if (has_entry && lane == leader) {
+    if (my_key == kEmptyKey) {
+      first = atomicCAS(&s_spec, 0u, 1u) == 0u;
     } else {
-      h = uint32_t(splitmix64(key) >> 32) & (H - 1u);
+      h = uint32_t(splitmix64(my_key) >> 32) & (H - 1u);
       for (uint32_t probe = 0; probe < H; ++probe) {  // at most half full: ends at the key or a free slot
-        const unsigned long long old = atomicCAS(&s_hkey[h], kEmptyKey, key);
-        if (old == kEmptyKey) s_hpos[h] = j;
-        if (old == kEmptyKey || old == key) break;
+        const unsigned long long old = atomicCAS(&s_hkey[h], kEmptyKey, my_key);
+        if (old == kEmptyKey || old == my_key) {
+          first = old == kEmptyKey;
+          break;
+        }
         h = (h + 1u) & (H - 1u);
       }
     }
-    s_ent[j] = h;
   }
-  __syncthreads();
-  // 2. a local index per distinct key (one counter atomic per warp)
-  for (uint32_t h0 = 0; h0 <= H; h0 += blockDim.x) {
-    const uint32_t h = h0 + tid;
-    const bool used = h < H ? s_hkey[h] != kEmptyKey : (h == H && s_spec != 0u);
-    const unsigned ballot = __ballot_sync(0xffffffffu, used);
+  {  // local indices of the keys this warp inserted first (one counter atomic per warp)
+    const unsigned ballot = __ballot_sync(0xffffffffu, first);
     uint32_t base = 0;
     if (ballot && lane == uint32_t(__ffs(ballot) - 1)) base = atomicAdd(&s_nloc, uint32_t(__popc(ballot)));
     base = __shfl_sync(0xffffffffu, base, ballot ? __ffs(ballot) - 1 : 0);
-    if (used) {
+    if (first) {
       const uint32_t q = base + __popc(ballot & ((1u << lane) - 1u));
       s_hloc[h] = q;
-      s_lkey[q] = h < H ? s_hkey[h] : kEmptyKey;
-      s_lrow[q] = s_erow[s_hpos[h]];
+      s_lkey[q] = my_key;
+      s_lrow[q] = my_row;
     }
   }
+  h = __shfl_sync(0xffffffffu, h, leader);
   __syncthreads();
   const uint32_t nloc = s_nloc;
-  // 3. each entry joins its key's list; each distinct key finds (or claims)
-  //    its table slot (its L2 round trips overlap the lists and the copy)
-  if (has_entry) {
-    const uint32_t q = s_hloc[s_ent[tid]];
-    s_next[tid] = atomicExch(&s_head[q], int32_t(tid));
+  // 3. each warp's entries of a key join the key's list as one chain (lanes
+  //    in order, linked by the group's leader with one exchange); each
+  //    distinct key finds (or claims) its table slot (its L2 round trips
+  //    overlap the lists and the copy)
+  {
+    const uint32_t q = has_entry ? s_hloc[h] : 0u;
+    int32_t old = -1;
+    if (has_entry && lane == leader) old = atomicExch(&s_head[q], int32_t(tid));
+    old = __shfl_sync(0xffffffffu, old, leader);
+    if (has_entry) {
+      const unsigned above = peers & ~((2u << lane) - 1u);  // group lanes after this one
+      s_next[tid] = above ? int32_t((tid & ~31u) + uint32_t(__ffs(above) - 1)) : old;
+    }
   }
   {  // nloc <= tile <= blockDim: one local key per thread at most
     const uint32_t q = tid;

@@ -2835,7 +2835,9 @@ struct StoreImpl {
     auto go = [&](auto lanes_tag, auto vec_tag) {
       constexpr int LN = decltype(lanes_tag)::value;
       constexpr int VC = decltype(vec_tag)::value;
-      const unsigned grid = grid_for(slots * LN, 256, 148 * 16);
+      // one wave (3 blocks per SM); the groups stride over the slots, so no
+      // block of a later wave starts only to find nothing to do
+      const unsigned grid = grid_for(slots * LN, 256, 148 * 3);
       Prof pr(this, "k_acc_apply", st);
       auto launch = [&](auto kern) {
         pdl(kern, grid, 256, 0, st, t.acc_tab(), t.dir(), t.L, t.slabs, o, apply ? 1 : 0, dropped);

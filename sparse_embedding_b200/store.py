@@ -356,6 +356,7 @@ class EmbeddingStore:
         self._score_policy = score_policy
         self._thread_budget = cfg.thread_budget if cfg.thread_budget > 0 else max(1, os.cpu_count() or 1)
         self._device = _default_device() if cfg.device is None else int(cfg.device)
+        self._lens_cache = {}  # dim -> one-element int64 device tensor (row_lengths of device batches)
         self._operational = True
 
         dims = (C.c_int64 * len(cfg.dims))(*cfg.dims)
@@ -452,11 +453,23 @@ class EmbeddingStore:
         fn = self._lib.se_lookup_or_insert_dim if insert else self._lib.se_forward_lookup_dim
         N.check(fn(self._h, k.ptr, n, dim, data_ptr(out), self._stream(k)))
         if lens is None:
-            from ._tensors import torch_mod
-
-            torch = torch_mod()
-            lens = torch.full((n,), dim, dtype=torch.int64, device=f"cuda:{self._device}")
+            lens = self._device_lens(n, dim)
         return out, lens
+
+    def _device_lens(self, n: int, dim: int):
+        """row_lengths of a device batch: every row has `dim` values. A
+        broadcast view (stride 0) of one cached element per dim, so the call
+        launches no fill kernel between the library's kernels; torch rejects
+        in-place writes to such a view, so the shared element cannot be
+        changed through it."""
+        from ._tensors import torch_mod
+
+        torch = torch_mod()
+        one = self._lens_cache.get(dim)
+        if one is None:
+            one = torch.full((1,), dim, dtype=torch.int64, device=f"cuda:{self._device}")
+            self._lens_cache[dim] = one
+        return one.expand(n)
 
     def lookup(self, keys, dim: int):
         """forward_lookup: (values[n*dim], row_lengths[n]); absent keys read as zeros."""
