@@ -44,8 +44,8 @@ struct AccTab {
   ulonglong2 *slots;         // [G + 1] (key, dense row); free: all ones; slot G holds the all-ones key
   float *vals;               // [vcap][dim] fp32 sums by dense row, zero when free
   uint32_t *cnt;             // [G + 1] gradient rows summed into each slot
-  uint4 *list;               // [G + 1] claimed slots in claim order: (slot, cached row, erase epoch, dense row)
-  uint32_t *ctr;             // [0] claimed slots, [2] finished apply blocks, [3] dense rows reserved
+  uint4 *list;               // [G + 1] (slot, cached row, erase epoch, dense row) of each claim; slot kNoRow: a hole
+  uint32_t *ctr;             // [0] list entries, [2] finished apply blocks, [3] dense rows reserved
   const uint32_t *epoch;     // the table's erase epoch (bumped by every erase)
   uint32_t mask;             // G - 1; G is a power of two
   uint32_t dim;
@@ -180,9 +180,9 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   __shared__ unsigned long long s_lkey[kAccMaxTile];  // key of each local index
   __shared__ uint32_t s_gslot[kAccMaxTile];           // table slot of each local index
   __shared__ uint32_t s_vrow[kAccMaxTile];            // dense sum row of each local index
-  __shared__ uint32_t s_crank[kAccMaxTile];           // rank among the block's claims, or kNoRow
+  __shared__ uint32_t s_crank[kAccMaxTile];           // 1: this block claimed the local key's slot
   __shared__ uint32_t s_lrow[kAccMaxTile];            // row of each local key from the forward's cache, or kNoRow
-  __shared__ uint32_t s_nloc, s_spec, s_nclaim, s_claim_base, s_epoch, s_copy_ok, s_rank_base;
+  __shared__ uint32_t s_nloc, s_spec, s_claim_base, s_epoch, s_copy_ok, s_rank_base;
   __shared__ __align__(8) uint64_t s_bar;
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
@@ -231,7 +231,6 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
   if (tid == 0) {
     s_nloc = 0u;
     s_spec = 0u;
-    s_nclaim = 0u;
     s_epoch = a.epoch ? __ldcg(a.epoch) : 0u;
     s_copy_ok = 1u;
     // dense sum rows for the tile's keys that this block may claim
@@ -292,6 +291,11 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     }
   }
   {  // nloc <= tile <= blockDim: one local key per thread at most
+    // optimizer_step's list positions for the tile's distinct keys, reserved
+    // while the keys are claimed (one entry per local key: a key another
+    // block claimed leaves a hole, which optimizer_step skips)
+    uint32_t list_base = 0;
+    if (!kDirect && tid == 0) list_base = atomicAdd(a.ctr, nloc);
     const uint32_t q = tid;
     const bool mine = q < nloc;
     bool claimed = false;
@@ -307,18 +311,17 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
       }
       s_gslot[q] = slot;
       s_vrow[q] = vrow;
+      s_crank[q] = claimed ? 1u : 0u;
     }
-    // ranks among the block's claims (one counter atomic per warp); the
-    // claimant lists the row lookup_or_insert cached for its key, so
-    // optimizer_step need not probe the directory for it
-    const unsigned ballot = __ballot_sync(0xffffffffu, claimed);
-    uint32_t base = 0;
-    if (ballot && lane == uint32_t(__ffs(ballot) - 1)) base = atomicAdd(&s_nclaim, uint32_t(__popc(ballot)));
-    base = __shfl_sync(0xffffffffu, base, ballot ? __ffs(ballot) - 1 : 0);
-    if (mine) s_crank[q] = claimed ? base + __popc(ballot & ((1u << lane) - 1u)) : kNoRow;
+    if (!kDirect && tid == 0) s_claim_base = list_base;
   }
   __syncthreads();
-  if (tid == 0 && s_nclaim) s_claim_base = atomicAdd(a.ctr, s_nclaim);
+  // the claimant lists the row lookup_or_insert cached for its key, so
+  // optimizer_step need not probe the directory for it
+  if (!kDirect)
+    for (uint32_t q = tid; q < nloc; q += blockDim.x)
+      a.list[s_claim_base + q] = s_crank[q] ? make_uint4(s_gslot[q], s_lrow[q], s_epoch, s_vrow[q])
+                                            : make_uint4(kNoRow, kNoRow, 0u, kNoRow);
   if (tma) {  // every thread waits for the rows (bounded; the copy is local and completes)
     uint32_t polls = 0;
     while (!mbar_try_wait(&s_bar, 0u)) {
@@ -339,9 +342,6 @@ k_acc_atomic(AccTab a, const void *__restrict__ keys, int kdt, size_t n_max, con
     }
   }
   if (!s_copy_ok) return;
-  for (uint32_t q = tid; q < nloc; q += blockDim.x)
-    if (s_crank[q] != kNoRow)
-      a.list[s_claim_base + s_crank[q]] = make_uint4(s_gslot[q], s_lrow[q], s_epoch, s_vrow[q]);
   // 4. per (distinct key, chunk): the sum of its entries' chunks, validated
   //    and scaled on entry, added into the table
   bool bad = false;
@@ -406,6 +406,7 @@ __global__ void __launch_bounds__(256) k_acc_move(AccTab from, AccTab to, uint32
   for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < n; g += gridDim.x * blockDim.x) {
     const uint4 ent = from.list[g];
     const uint32_t slot = ent.x;
+    if (slot == kNoRow) continue;  // a hole: the key was claimed by another block's entry
     const uint64_t key = from.slots[slot].x;
     bool claimed = false;
     uint32_t vrow = kNoRow;

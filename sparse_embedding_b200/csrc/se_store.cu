@@ -1011,66 +1011,74 @@ k_acc_apply(AccTab a, Dir d, Layout L, uint8_t *__restrict__ slabs, OptSpec o_in
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   const uint32_t G = a.mask + 1u;
-  const uint32_t nslots = min(__ldcg(a.ctr), G + 1u);
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
   const unsigned mask = group_mask<LANES>();
+  // the group's first list entry is loaded with the entry count (one round
+  // trip; the list holds G + 1 entries, so the load stays inside it), each
+  // next one at the end of the iteration before it
+  size_t g = t / LANES;
+  uint4 ent = g <= size_t(G) ? __ldcg(a.list + g) : make_uint4(kNoRow, kNoRow, 0u, kNoRow);
+  const uint32_t nslots = min(__ldcg(a.ctr), G + 1u);
   const bool run = apply && *o.poison == 0u;
   const uint32_t epoch = __ldcg(a.epoch);
-  for (size_t g = t / LANES; g < nslots; g += groups) {
-    const uint4 ent = __ldcg(a.list + g);
+  while (g < nslots) {
     const uint32_t slot = ent.x;
-    float *acc = a.vals + size_t(ent.w) * L.dim;  // the slot's dense sum row
-    // the row the accumulate listed (from lookup_or_insert) while no erase
-    // happened since; else the key is resolved in the directory now
-    uint32_t row = ent.z == epoch ? ent.y : kNoRow;
-    if (lane == 0 && apply && row == kNoRow) row = dir_find<false>(d, uint64_t(__ldcg(&a.slots[slot].x)));
-    row = __shfl_sync(mask, row, 0, LANES);
-    if (apply && row == kNoRow) {
-      if (lane == 0) atomicAdd(dropped, (unsigned long long)__ldcg(a.cnt + slot));
-    } else if (run) {
-      uint8_t *slab = slabs + size_t(row) * L.stride;
-      uint32_t step = 0;
-      if (o.kind == SE_OPT_ADAM) {
-        if (lane == 0) step = next_step(L, slab);
-        step = __shfl_sync(mask, step, 0, LANES);
-      }
-      // kChunks chunks per lane and pass: every load of the pass (sum,
-      // parameters, state) is in flight before the first update
-      constexpr int kChunks = 4;
-      for (uint32_t e0 = lane * VEC; e0 < L.dim; e0 += LANES * VEC * kChunks) {
-        float gs[kChunks][VEC];
-        RowState<VEC> rs[kChunks];
-#pragma unroll
-        for (int k = 0; k < kChunks; ++k) {
-          const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
-          if (e >= L.dim) continue;
-          if constexpr (VEC == 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(acc + e));
-            gs[k][0] = v.x; gs[k][1] = v.y; gs[k][2] = v.z; gs[k][3] = v.w;
-          } else {
-            gs[k][0] = __ldcg(acc + e);
+    if (slot != kNoRow) {  // else a hole left by a key another block claimed
+      float *acc = a.vals + size_t(ent.w) * L.dim;  // the slot's dense sum row
+      // the row the accumulate listed (from lookup_or_insert) while no erase
+      // happened since; else the key is resolved in the directory now
+      uint32_t row = ent.z == epoch ? ent.y : kNoRow;
+      if (lane == 0 && apply && row == kNoRow) row = dir_find<false>(d, uint64_t(__ldcg(&a.slots[slot].x)));
+      row = __shfl_sync(mask, row, 0, LANES);
+      if (apply && row == kNoRow) {
+        if (lane == 0) atomicAdd(dropped, (unsigned long long)__ldcg(a.cnt + slot));
+      } else if (run) {
+        uint8_t *slab = slabs + size_t(row) * L.stride;
+        uint32_t step = 0;
+        if (o.kind == SE_OPT_ADAM) {
+          if (lane == 0) step = next_step(L, slab);
+          step = __shfl_sync(mask, step, 0, LANES);
+        }
+        // kChunks chunks per lane and pass: every load of the pass (sum,
+        // parameters, state) is in flight before the first update
+        constexpr int kChunks = 4;
+        for (uint32_t e0 = lane * VEC; e0 < L.dim; e0 += LANES * VEC * kChunks) {
+          float gs[kChunks][VEC];
+          RowState<VEC> rs[kChunks];
+  #pragma unroll
+          for (int k = 0; k < kChunks; ++k) {
+            const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
+            if (e >= L.dim) continue;
+            if constexpr (VEC == 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4 *>(acc + e));
+              gs[k][0] = v.x; gs[k][1] = v.y; gs[k][2] = v.z; gs[k][3] = v.w;
+            } else {
+              gs[k][0] = __ldcg(acc + e);
+            }
+            load_state<VEC>(L, slab, o, e, rs[k]);
           }
-          load_state<VEC>(L, slab, o, e, rs[k]);
-        }
-        // the sum is fp32; the ordered mode's is rounded to the gradient
-        // dtype after every add
-#pragma unroll
-        for (int k = 0; k < kChunks; ++k) {
-          const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
-          if (e < L.dim) apply_loaded<VEC, kDyn>(L, slab, o, step, e, gs[k], rs[k]);
+          // the sum is fp32; the ordered mode's is rounded to the gradient
+          // dtype after every add
+  #pragma unroll
+          for (int k = 0; k < kChunks; ++k) {
+            const uint32_t e = e0 + uint32_t(k) * LANES * VEC;
+            if (e < L.dim) apply_loaded<VEC, kDyn>(L, slab, o, step, e, gs[k], rs[k]);
+          }
         }
       }
+      for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
+        if constexpr (VEC == 4) *reinterpret_cast<float4 *>(acc + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+        else acc[e] = 0.0f;
+      }
+      if (lane == 0) {
+        a.cnt[slot] = 0u;
+        a.slots[slot] = make_ulonglong2(kEmptyKey, kAccFree);
+      }
     }
-    for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) {
-      if constexpr (VEC == 4) *reinterpret_cast<float4 *>(acc + e) = make_float4(0.f, 0.f, 0.f, 0.f);
-      else acc[e] = 0.0f;
-    }
-    if (lane == 0) {
-      a.cnt[slot] = 0u;
-      a.slots[slot] = make_ulonglong2(kEmptyKey, kAccFree);
-    }
+    g += groups;
+    if (g < nslots) ent = __ldcg(a.list + g);
   }
   // every block has read the claim counter: the last one resets the counters
   __syncthreads();
