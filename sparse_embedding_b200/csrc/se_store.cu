@@ -69,6 +69,77 @@ k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row
   }
 }
 
+// forward_lookup of wide rows through the TMA (rows of 512..1,024 bytes, a
+// multiple of 16, 16-byte aligned slabs and output). Each warp takes 32
+// consecutive batch positions per round: every lane resolves one key, the
+// rows found are brought into the warp's shared-memory buffer with one bulk
+// copy each (cp.async.bulk, completion counted in bytes on the warp's
+// mbarrier), rows of absent keys are zero-filled there, and the warp's 32
+// rows - consecutive in the output - leave with one bulk store. The waits
+// are bounded: a copy that never lands raises kStatusCopyTimeout.
+constexpr uint32_t kBulkWarps = 4;  // warps per block; shared memory = 4 x 32 rows
+constexpr uint32_t kBulkMinRow = 512, kBulkMaxRow = 1024;
+
+__global__ void __launch_bounds__(kBulkWarps * 32)
+k_lookup_bulk(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row_bytes,
+              const void *__restrict__ keys, int kdt, size_t n, uint8_t *__restrict__ out, uint32_t *status) {
+  extern __shared__ __align__(128) uint8_t s_buf[];  // [kBulkWarps][32][row_bytes]
+  __shared__ __align__(8) uint64_t s_bar[kBulkWarps];
+  pdl_wait();
+  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  uint8_t *buf = s_buf + size_t(warp) * 32u * row_bytes;
+  uint8_t *slot = buf + size_t(lane) * row_bytes;
+  uint64_t *bar = &s_bar[warp];
+  if (lane == 0) mbar_init(bar, 1);
+  __syncwarp();
+  uint32_t parity = 0;
+  const size_t step = size_t(gridDim.x) * kBulkWarps * 32u;
+  for (size_t i0 = (size_t(blockIdx.x) * kBulkWarps + warp) * 32u; i0 < n; i0 += step) {
+    const uint32_t cnt = uint32_t(min(size_t(32), n - i0));
+    uint32_t row = kNoRow;
+    if (lane < cnt) row = dir_find<false>(d, load_key(keys, kdt, i0 + lane));
+    const unsigned found = __ballot_sync(0xffffffffu, row != kNoRow);
+    // the bytes to come are announced before any copy can complete
+    if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(__popc(found)) * row_bytes);
+    __syncwarp();
+    if (row != kNoRow) {
+      bulk_copy_g2s(slot, slabs + size_t(row) * stride, row_bytes, bar);
+    } else if (lane < cnt) {
+      for (uint32_t u = 0; u < row_bytes / 16u; ++u) reinterpret_cast<uint4 *>(slot)[u] = make_uint4(0, 0, 0, 0);
+      fence_proxy_async_smem();  // the zeros are seen by the bulk store
+    }
+    uint32_t polls = 0;
+    bool landed = true;
+    while (!mbar_try_wait(bar, parity)) {
+      if (++polls > kCopySpinLimit) {
+        landed = false;
+        break;
+      }
+    }
+    if (!__all_sync(0xffffffffu, landed)) {
+      if (lane == 0) {
+        raise_status(status, kStatusCopyTimeout);
+        // the copies still in flight land before the block's shared memory is released
+        for (uint32_t w = 0; w < kCopySpinLimit && !mbar_try_wait(bar, parity); ++w) __nanosleep(64);
+      }
+      __syncwarp();
+      return;
+    }
+    parity ^= 1u;
+    __syncwarp();
+    if (lane == 0) {
+      bulk_store_s2g(out + i0 * row_bytes, buf, cnt * row_bytes);
+      bulk_wait_read();  // the buffer is free for the next round
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    bulk_wait_all();
+    mbar_inval(bar);
+  }
+}
+
 template <int VEC>
 __device__ __forceinline__ void zero_elems(void *dst, int dt, size_t e) {
   float z[VEC];
@@ -1612,6 +1683,13 @@ uint64_t next_pow2(uint64_t x) {
 // Lanes per key of the gathers: as few as keep each lane's share of the row
 // at <= 8 units, so a warp probes 8 keys at once and each lane keeps its
 // loads of the row in flight together.
+// The TMA path of forward_lookup: rows of 512..1,024 bytes in 16-byte units,
+// slabs and output 16-byte aligned.
+bool bulk_lookup_fits(size_t row_bytes, uint32_t stride, const void *out, const void *slabs) {
+  return row_bytes >= kBulkMinRow && row_bytes <= kBulkMaxRow && row_bytes % 16 == 0 && stride % 16 == 0 &&
+         uintptr_t(out) % 16 == 0 && uintptr_t(slabs) % 16 == 0;
+}
+
 uint32_t gather_lanes(uint64_t units) {
   uint32_t l = 4;
   while (l < 32 && uint64_t(l) * 8 < units) l <<= 1;
@@ -2148,7 +2226,21 @@ struct StoreImpl {
     const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
     const bool host_out = !is_device_ptr(out);
     void *dout = host_out ? stage_vals.get(out_bytes) : out;
-    if (!insert) {
+    if (!insert && bulk_lookup_fits(size_t(dim) * vb, t.L.stride, dout, t.slabs)) {
+      const size_t row_bytes = size_t(dim) * vb;
+      const size_t smem = size_t(kBulkWarps) * 32u * row_bytes;
+      // 32 positions per warp and round, warps striding over the batch; one
+      // wave of resident blocks at most
+      const uint32_t per_sm = uint32_t(std::max<size_t>(1, (227u * 1024u) / (smem + 1024u)));
+      const size_t rounds = (n + 31) / 32;
+      const unsigned grid = unsigned(std::min<size_t>((rounds + kBulkWarps - 1) / kBulkWarps, size_t(148) * per_sm));
+      allow_dynamic_smem(k_lookup_bulk, smem);
+      Prof pr(this, "k_lookup_bulk", st);
+      pdl(k_lookup_bulk, grid, kBulkWarps * 32, smem, st, t.dir(), t.slabs, t.L.stride, uint32_t(row_bytes), dkeys,
+          cfg.key_dtype, n, static_cast<uint8_t *>(dout), t.ctr + kCtrStatus);
+      launched("k_lookup_bulk");
+      if (cfg.score_policy == SE_SCORE_LFU || cfg.score_policy == SE_SCORE_LRU) touch_scores(t, dkeys, n, st);
+    } else if (!insert) {
       const size_t row_bytes = size_t(dim) * vb;
       const uintptr_t al = uintptr_t(dout) | uintptr_t(row_bytes);
       const Dir d = t.dir();

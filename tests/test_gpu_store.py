@@ -463,3 +463,28 @@ def test_large_window_sorted_placement():
     got, _ = gpu.lookup(pool, dim)
     np.testing.assert_allclose(got, orc.lookup(pool, dim), rtol=RTOL_FP32, atol=ATOL_FP32)
     np.testing.assert_array_equal(bits(got), bits(twin.lookup(pool, dim)[0]))
+
+
+@pytest.mark.parametrize("dim,value_dtype", [(128, "float32"), (256, "bfloat16"), (200, "float32"),
+                                             (256, "float32"), (400, "float16"), (129, "float32")])
+def test_wide_row_lookup_bit_exact(dim, value_dtype):
+    """forward_lookup of rows of 512..1,024 bytes goes through the TMA bulk
+    path (bulk copies per row into shared memory, one bulk store per 32
+    positions); a 516-byte row (dim 129 fp32) takes the plain path. Absent
+    keys read as zeros; batches not a multiple of 32; device and host
+    outputs."""
+    gpu, orc = pair([dim], key_dtype="int64", value_dtype=value_dtype, opt="none")
+    rng = np.random.default_rng(dim)
+    present = rng.integers(-2**63, 2**63 - 1, size=3000, dtype=np.int64)
+    gpu.lookup_or_insert(present, dim)
+    orc.lookup_or_insert(present, dim)
+    absent = rng.integers(-2**63, 2**63 - 1, size=500, dtype=np.int64)
+    for n in (1, 31, 33, 1000, 3457):
+        keys = rng.choice(np.concatenate([present, absent]), size=n)
+        want = orc.lookup(keys, dim)
+        got, lens = gpu.lookup(keys, dim)
+        np.testing.assert_array_equal(bits(got).ravel(), bits(want).ravel())
+        assert np.all(np.asarray(lens) == dim)
+        dev, dlens = gpu.lookup(torch.from_numpy(keys).cuda(), dim)
+        np.testing.assert_array_equal(bits(dev).ravel(), bits(want).ravel())
+        assert int(dlens.min()) == dim and dlens.shape == (n,)
