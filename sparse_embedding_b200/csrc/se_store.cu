@@ -75,10 +75,17 @@ k_lookup(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row
 // rows found are brought into the warp's shared-memory buffer with one bulk
 // copy each (cp.async.bulk, completion counted in bytes on the warp's
 // mbarrier), rows of absent keys are zero-filled there, and the warp's 32
-// rows - consecutive in the output - leave with one bulk store. The waits
-// are bounded: a copy that never lands raises kStatusCopyTimeout.
+// rows - consecutive in the output - leave with one bulk store. The next
+// round's keys are resolved while this round's copies are in flight, so the
+// buffer holds rows in flight for most of the kernel. The waits are bounded:
+// a copy that never lands raises kStatusCopyTimeout.
 constexpr uint32_t kBulkWarps = 4;  // warps per block; shared memory = 4 x 32 rows
 constexpr uint32_t kBulkMinRow = 512, kBulkMaxRow = 1024;
+
+__device__ __forceinline__ uint32_t bulk_probe(const Dir &d, const void *keys, int kdt, size_t i0, size_t n,
+                                               uint32_t lane) {
+  return i0 + lane < n ? dir_find<false>(d, load_key(keys, kdt, i0 + lane)) : kNoRow;
+}
 
 __global__ void __launch_bounds__(kBulkWarps * 32)
 k_lookup_bulk(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_t row_bytes,
@@ -95,10 +102,10 @@ k_lookup_bulk(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_
   __syncwarp();
   uint32_t parity = 0;
   const size_t step = size_t(gridDim.x) * kBulkWarps * 32u;
-  for (size_t i0 = (size_t(blockIdx.x) * kBulkWarps + warp) * 32u; i0 < n; i0 += step) {
+  size_t i0 = (size_t(blockIdx.x) * kBulkWarps + warp) * 32u;
+  uint32_t row = bulk_probe(d, keys, kdt, i0, n, lane);
+  for (; i0 < n; i0 += step) {
     const uint32_t cnt = uint32_t(min(size_t(32), n - i0));
-    uint32_t row = kNoRow;
-    if (lane < cnt) row = dir_find<false>(d, load_key(keys, kdt, i0 + lane));
     const unsigned found = __ballot_sync(0xffffffffu, row != kNoRow);
     // the bytes to come are announced before any copy can complete
     if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(__popc(found)) * row_bytes);
@@ -109,6 +116,8 @@ k_lookup_bulk(Dir d, const uint8_t *__restrict__ slabs, uint32_t stride, uint32_
       for (uint32_t u = 0; u < row_bytes / 16u; ++u) reinterpret_cast<uint4 *>(slot)[u] = make_uint4(0, 0, 0, 0);
       fence_proxy_async_smem();  // the zeros are seen by the bulk store
     }
+    // the next round's keys while the copies are in flight
+    row = i0 + step < n ? bulk_probe(d, keys, kdt, i0 + step, n, lane) : kNoRow;
     uint32_t polls = 0;
     bool landed = true;
     while (!mbar_try_wait(bar, parity)) {
