@@ -13,6 +13,7 @@
 #include <cub/device/device_scan.cuh>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -1878,6 +1879,14 @@ struct ProfRec {
 
 struct StoreImpl {
   se_store_config cfg{};
+  // forward_lookup of 512..1,024-byte rows through the TMA bulk kernel
+  // (SE_GPU_WIDE_GATHER=bulk when the store is created); the default is the
+  // vector-load gather, which measured faster on B200 at 512-byte rows
+  // (82 % against 70 % of the HBM copy peak)
+  bool bulk_gather = [] {
+    const char *v = std::getenv("SE_GPU_WIDE_GATHER");
+    return v != nullptr && std::string(v) == "bulk";
+  }();
   std::vector<int64_t> dims;
   int device = 0;
   cudaStream_t own = nullptr;
@@ -2235,7 +2244,7 @@ struct StoreImpl {
     const void *dkeys = stage_in(stage_keys, keys, n * key_bytes(cfg.key_dtype), st);
     const bool host_out = !is_device_ptr(out);
     void *dout = host_out ? stage_vals.get(out_bytes) : out;
-    if (!insert && bulk_lookup_fits(size_t(dim) * vb, t.L.stride, dout, t.slabs)) {
+    if (!insert && bulk_gather && bulk_lookup_fits(size_t(dim) * vb, t.L.stride, dout, t.slabs)) {
       const size_t row_bytes = size_t(dim) * vb;
       const size_t smem = size_t(kBulkWarps) * 32u * row_bytes;
       // 32 positions per warp and round, warps striding over the batch; one

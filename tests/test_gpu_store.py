@@ -465,20 +465,31 @@ def test_large_window_sorted_placement():
     np.testing.assert_array_equal(bits(got), bits(twin.lookup(pool, dim)[0]))
 
 
+@pytest.mark.parametrize("gather", ["vector", "bulk"])
 @pytest.mark.parametrize("dim,value_dtype", [(128, "float32"), (256, "bfloat16"), (200, "float32"),
                                              (256, "float32"), (400, "float16"), (129, "float32")])
-def test_wide_row_lookup_bit_exact(dim, value_dtype):
-    """forward_lookup of rows of 512..1,024 bytes goes through the TMA bulk
-    path (bulk copies per row into shared memory, one bulk store per 32
-    positions); a 516-byte row (dim 129 fp32) takes the plain path. Absent
-    keys read as zeros; batches not a multiple of 32; device and host
-    outputs."""
+def test_wide_row_lookup_bit_exact(dim, value_dtype, gather, monkeypatch):
+    """forward_lookup of rows of 512..1,024 bytes: the default vector-load
+    gather, and the TMA bulk kernel (SE_GPU_WIDE_GATHER=bulk: bulk copies
+    per row into shared memory, one bulk store per 32 positions); a 516-byte
+    row (dim 129 fp32) always takes the vector path. Absent keys read as
+    zeros; batches not a multiple of 32; device and host outputs."""
+    if gather == "bulk":
+        monkeypatch.setenv("SE_GPU_WIDE_GATHER", "bulk")
+    else:
+        monkeypatch.delenv("SE_GPU_WIDE_GATHER", raising=False)
     gpu, orc = pair([dim], key_dtype="int64", value_dtype=value_dtype, opt="none")
     rng = np.random.default_rng(dim)
     present = rng.integers(-2**63, 2**63 - 1, size=3000, dtype=np.int64)
     gpu.lookup_or_insert(present, dim)
     orc.lookup_or_insert(present, dim)
     absent = rng.integers(-2**63, 2**63 - 1, size=500, dtype=np.int64)
+    gpu.profile(True)
+    gpu.lookup(present[:64], dim)
+    _, bulk_launches = gpu.profile_read("k_lookup_bulk")
+    gpu.profile(False)
+    eligible = 512 <= dim * (4 if value_dtype == "float32" else 2) <= 1024
+    assert bulk_launches == (1 if gather == "bulk" and eligible else 0)
     for n in (1, 31, 33, 1000, 3457):
         keys = rng.choice(np.concatenate([present, absent]), size=n)
         want = orc.lookup(keys, dim)
