@@ -513,6 +513,8 @@ def run_ours(args):
     capacity = None
     if args.capacity and world >= 8 and args.transport == "p2p":
         # the capacity table needs the device's memory: the train step's store goes first
+        if api is not store:
+            api.close()
         del step, e2e_step, keys_d, grads_d
         store = api = None
         torch.cuda.empty_cache()
