@@ -1693,6 +1693,16 @@ uint64_t next_pow2(uint64_t x) {
 // Lanes per key of the gathers: as few as keep each lane's share of the row
 // at <= 8 units, so a warp probes 8 keys at once and each lane keeps its
 // loads of the row in flight together.
+// Threads per block of a one-thread-per-work-item kernel of up to 256-thread
+// blocks: fewer (a multiple of 32, at least 64) when the work fills about
+// one wave, so that every SM holds the same number of blocks (4 on each of
+// the 148 SMs) instead of 3 on some and 4 on others.
+unsigned balanced_block(size_t threads) {
+  const size_t per = (threads + 148 * 4 - 1) / (148 * 4);
+  const size_t bt = (per + 31) / 32 * 32;
+  return unsigned(std::min<size_t>(256, std::max<size_t>(64, bt)));
+}
+
 // The TMA path of forward_lookup: rows of 512..1,024 bytes in 16-byte units,
 // slabs and output 16-byte aligned.
 bool bulk_lookup_fits(size_t row_bytes, uint32_t stride, const void *out, const void *slabs) {
@@ -2308,7 +2318,8 @@ struct StoreImpl {
         constexpr int LN = decltype(lanes_tag)::value;
         constexpr int VC = decltype(vec_tag)::value;
         Prof pr(this, "k_lookup_or_insert", st);
-        pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, 256, 0x7fffffffu), 256, 0, st,
+        const unsigned bt = balanced_block(n * LN);
+        pdl(k_lookup_or_insert<LN, VC>, grid_for(n * LN, bt, 0x7fffffffu), bt, 0, st,
             t.dir(), t.L, t.slabs, t.alloc(), init, dkeys, cfg.key_dtype, n,
             dout, t.ctr + kCtrFwdDeferred, dpos, dword, t.ctr + kCtrStatus, t.ctr + kCtrFwdDone, fc);
         launched("k_lookup_or_insert");
@@ -2922,12 +2933,15 @@ struct StoreImpl {
     }
     {
       Prof pr(this, "k_acc_atomic", st);
-      const unsigned grid = grid_for(n, t.acc_tile, 0x7fffffffu);
+      // rows per block: the table's tile, or fewer so that a batch of about
+      // one wave spreads evenly (4 resident blocks on each of the 148 SMs)
+      const uint32_t tile = uint32_t(std::min<size_t>(t.acc_tile, std::max<size_t>(32, (n + 591) / 592)));
+      const unsigned grid = grid_for(n, tile, 0x7fffffffu);
       const size_t smem = size_t(t.acc_tile) * size_t(dim) * 4;
       auto go = [&](auto kern) {
         allow_dynamic_smem(kern, smem);
         pdl(kern, grid, kAccThreads, smem, st, t.acc_tab(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
-            cfg.gradient_scale, maxv, t.acc_tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row,
+            cfg.gradient_scale, maxv, tile, t.acc_hbits, status_word, t.ctr + kCtrStatus, grad_row,
             t.fwd_cache());
       };
       if (grad_row) {
