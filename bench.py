@@ -83,6 +83,9 @@ def args_parse():
     p.add_argument("--capacity", action="store_true",
                    help="N >= 8, p2p: after the train step, run the 1.5e9-key capacity configuration "
                         "(~160 GB per GPU)")
+    p.add_argument("--configs-only", action="store_true",
+                   help="N > 1: run only the sharded DLRM configuration and, on 8 GPUs, the capacity "
+                        "configuration (no train step of the headline workload)")
     p.add_argument("--dlrm", action="store_true",
                    help="N > 1, p2p: after the train step, run the DLRM configuration sharded (26 tables up to "
                         "4e7 rows, fast_range, global batch of 8,192 samples)")
@@ -265,8 +268,10 @@ def run_ours(args):
     mine = owned_keys(warm, world, rank)
     # Room for every row the run can create (5 % new keys per batch, twice
     # over), plus the headroom an insert call checks for while it is being
-    # captured: one batch from every rank.
-    cap = int(len(mine) + (W + 4 * K + 8) * BATCH * 0.1 + (world + 1) * BATCH)
+    # captured: the bound of the rows in use carries the previous call's
+    # room for one batch from every rank, and the captured call asks for the
+    # same again.
+    cap = int(len(mine) + (W + 4 * K + 8) * BATCH * 0.1 + (2 * world + 1) * BATCH)
     store = se.EmbeddingStore(
         se.EmbeddingConfig(dims=[DIM], key_dtype="int64", device=local, initial_capacity=cap,
                            accumulation=args.accumulation),
@@ -1227,6 +1232,28 @@ def run_reference(args):
             "e2e": {"value": value, "unit": "keys/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_configs(args):
+    """The sharded DLRM configuration, then (8 GPUs) the capacity one, each
+    on a fresh store; rank 0 returns their lines."""
+    import torch
+
+    import sparse_embedding_b200 as se
+
+    world, rank, local = dist_setup(args)
+    peak, _ = measured_hbm()
+    out = {"metric": "configuration runs (DLRM sharded, capacity)", "n_gpus": world, "data": "synthetic"}
+    if world > 1:
+        out["dlrm_sharded"] = dlrm_sharded_bench(se, torch, world, rank, local, peak)
+        torch.cuda.empty_cache()
+    if world >= 8:
+        out["capacity"] = capacity_bench(se, torch, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
 def main():
     args = args_parse()
     if args.bag_only > 0 and args.impl == "ours":
@@ -1237,7 +1264,9 @@ def main():
         peak, _ = measured_hbm()
         print(json.dumps(dlrm_bag_bench(se, torch, peak, samples=args.bag_only)), flush=True)
         return
-    if args.impl == "reference":
+    if args.configs_only and args.impl == "ours":
+        out = run_configs(args)
+    elif args.impl == "reference":
         out = run_reference(args)
     else:
         out = run_ours(args)
