@@ -488,7 +488,8 @@ def test_wide_row_lookup_bit_exact(dim, value_dtype, gather, monkeypatch):
     gpu.lookup(present[:64], dim)
     _, bulk_launches = gpu.profile_read("k_lookup_bulk")
     gpu.profile(False)
-    eligible = 512 <= dim * (4 if value_dtype == "float32" else 2) <= 1024
+    row_bytes = dim * (4 if value_dtype == "float32" else 2)
+    eligible = 512 <= row_bytes <= 1024 and row_bytes % 16 == 0
     assert bulk_launches == (1 if gather == "bulk" and eligible else 0)
     for n in (1, 31, 33, 1000, 3457):
         keys = rng.choice(np.concatenate([present, absent]), size=n)
