@@ -401,7 +401,7 @@ def run_ours(args):
     # measured by this run. Cold-cache replays: each capture starts with an
     # empty L2, so hot keys' rows and the accumulation tables miss once.
     dram = {"k_group_apply+k_group_hot": 23.881e6 + 6.710e6, "k_accumulate": 22.183e6 + 0.011e6,
-            "k_lookup_or_insert": 9.531e6 + 0.071e6, "k_acc_atomic": 26.451e6, "k_acc_apply": 20.057e6 + 0.048e6}
+            "k_lookup_or_insert": 9.486e6 + 0.055e6, "k_acc_atomic": 26.442e6, "k_acc_apply": 20.491e6 + 0.079e6}
     local_store = world == 1 and not args.loopback  # the captured kernels are the local store's
     traffic = dram.get(dom["kernel"]) if local_store else None
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": dom["achieved_gbs"], "peak": peak,
