@@ -2937,7 +2937,7 @@ struct StoreImpl {
       // one wave spreads evenly (4 resident blocks on each of the 148 SMs)
       const uint32_t tile = uint32_t(std::min<size_t>(t.acc_tile, std::max<size_t>(32, (n + 591) / 592)));
       const unsigned grid = grid_for(n, tile, 0x7fffffffu);
-      const size_t smem = size_t(t.acc_tile) * size_t(dim) * 4;
+      const size_t smem = size_t(tile) * size_t(dim) * 4;  // the tile's rows (fp32 or 16-bit)
       auto go = [&](auto kern) {
         allow_dynamic_smem(kern, smem);
         pdl(kern, grid, kAccThreads, smem, st, t.acc_tab(), dkeys, kdt, n, n_dev, dgrads, cfg.gradient_dtype,
