@@ -1096,7 +1096,8 @@ def capacity_bench(se, torch, world, rank, local, total_keys: int = 1_500_000_00
     chunk = 1 << 26
     for s0 in range(0, total_keys, chunk):
         keys = wl.device_keys(s0, min(chunk, total_keys - s0), torch)
-        mine = keys[part.filter(keys, rank)]
+        # boolean indexing has no CUDA kernel for uint64: select on the int64 view
+        mine = keys.view(torch.int64)[part.filter(keys, rank)].view(torch.uint64)
         if mine.numel():
             store.lookup_or_insert(mine, dim)
         del keys, mine
@@ -1245,6 +1246,8 @@ def run_configs(args):
     if world > 1:
         out["dlrm_sharded"] = dlrm_sharded_bench(se, torch, world, rank, local, peak)
         torch.cuda.empty_cache()
+        if rank == 0:  # on record before the capacity run
+            print(json.dumps({"dlrm_sharded": out["dlrm_sharded"], "n_gpus": world}), flush=True)
     if world >= 8:
         out["capacity"] = capacity_bench(se, torch, world, rank, local)
     if world > 1:
