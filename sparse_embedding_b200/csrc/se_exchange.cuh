@@ -210,10 +210,15 @@ __global__ void k_ex_sync(ExView x, int kind, int total_word) {
 // with max(tiles, 1) blocks of kExTile keys.
 // count_dev: when not null, the batch holds min(*count_dev, count) keys (the
 // sender's distinct keys, counted on the device).
+// With a deduplicated batch (pos_slot not null) the same grid also writes
+// inverse[i], the distinct-key index of each of the npos batch positions
+// (set_idx of the position's set slot), which the dedupe kernel's claims
+// completed before this launch.
 template <class K>
 __global__ void __launch_bounds__(kRouteThreads)
 k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint32_t *__restrict__ tile_counts,
-           const uint32_t *count_dev) {
+           const uint32_t *count_dev, const uint32_t *__restrict__ pos_slot, const uint32_t *set_idx,
+           uint32_t *__restrict__ inverse, size_t npos) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
   extern __shared__ uint32_t hist[];  // [W]
@@ -223,6 +228,11 @@ k_ex_count(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, uint3
   __syncthreads();
   const size_t i = size_t(blockIdx.x) * kRouteThreads + threadIdx.x;
   if (i < count) atomicAdd(&hist[partition_of<K>(s, keys[i])], 1u);
+  if (pos_slot)
+    for (size_t j = i; j < npos; j += size_t(gridDim.x) * kRouteThreads) {
+      const uint32_t slot = pos_slot[j];
+      inverse[j] = slot == kNoRow ? 0u : __ldcg(set_idx + slot);
+    }
   __syncthreads();
   for (uint32_t p = threadIdx.x; p < s.n; p += blockDim.x) tile_counts[size_t(blockIdx.x) * s.n + p] = hist[p];
 }
@@ -370,13 +380,25 @@ k_ex_scatter(PartSpec s, ExView x, const K *__restrict__ keys, size_t count, con
 // buffer at the requester's batch position. Keys claimed by another group of
 // the same launch go to the deferred list. Absent keys of a plain lookup get
 // a zero row.
+// Insert mode: the launch's last block (a GPU-scope fence and a counter in
+// every block) then serves the deferred keys, whose claimants have all
+// published their rows by then, and resets the counters for the next launch.
+template <int LANES, int VEC>
+__device__ __forceinline__ void ex_owner_deferred(const Layout &L, const uint8_t *slabs, const ExView &x,
+                                                  uint32_t *def_count, const uint32_t *def_idx,
+                                                  const unsigned long long *def_word, uint32_t *status);
+
 template <int LANES, int VEC, bool kInsert>
 __global__ void __launch_bounds__(256)
 k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec init,
-           ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status) {
+           ExView x, uint32_t *def_count, uint32_t *def_idx, unsigned long long *def_word, uint32_t *status,
+           uint32_t *done) {
   pdl_wait();
   pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
-  if (ex_failed(x)) return;
+  __shared__ bool s_failed, s_last;
+  if (threadIdx.x == 0) s_failed = ex_failed(x);
+  __syncthreads();
+  if (s_failed) return;  // whole block (the counters stay as they are: the exchange must be recreated)
   const uint32_t *prefix = x.prefix();  // written by the KEYS wait
   const uint32_t total = __ldcg(prefix + x.W);
   const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -444,28 +466,43 @@ k_ex_owner(Dir d, Layout L, uint8_t *__restrict__ slabs, RowAlloc ra, InitSpec i
       for (uint32_t e = lane * VEC; e < L.dim; e += LANES * VEC) zero_elems<VEC>(out_row, L.pdt, e);
     }
   }
+  if constexpr (kInsert) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      ex_owner_deferred<LANES, VEC>(L, slabs, x, def_count, def_idx, def_word, status);
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        *def_count = 0u;
+        *done = 0u;
+      }
+    }
+  }
 }
 
-// Deferred keys of k_ex_owner: their claimant has published the row by now.
+// Deferred keys of k_ex_owner (one block): their claimant has published the
+// row by now.
 template <int LANES, int VEC>
-__global__ void __launch_bounds__(256)
-k_ex_owner_deferred(Layout L, const uint8_t *__restrict__ slabs, ExView x, const uint32_t *def_count,
-                    const uint32_t *def_idx, const unsigned long long *def_word, uint32_t *status) {
-  pdl_wait();
-  pdl_trigger();  // the next kernel may launch; its pdl_wait still waits for this one
-  const size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t groups = size_t(gridDim.x) * blockDim.x / LANES;
+__device__ __forceinline__ void ex_owner_deferred(const Layout &L, const uint8_t *slabs, const ExView &x,
+                                                  uint32_t *def_count, const uint32_t *def_idx,
+                                                  const unsigned long long *def_word, uint32_t *status) {
+  const size_t t = threadIdx.x;
+  const size_t groups = blockDim.x / LANES;
   const uint32_t lane = uint32_t(t % LANES);
-  if (ex_failed(x)) return;
-  const uint32_t count = *def_count;
+  const uint32_t count = __ldcg(def_count);
   for (size_t j = t / LANES; j < count; j += groups) {
-    const uint32_t i = def_idx[j];
+    const uint32_t i = __ldcg(def_idx + j);
     uint32_t src = 0;
     while (src + 1 < x.W && __ldcg(x.prefix() + src + 1) <= i) ++src;
     uint32_t pos = __ldcg(x.inpos(x.me) + i);
     if (pos >= x.M) pos = 0;  // reported by k_ex_owner
     void *out_row = x.rows(src) + size_t(pos) * x.row_bytes;
-    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(def_word[j]));
+    const uint32_t row = __ldcg(reinterpret_cast<const uint32_t *>(__ldcg(def_word + j)));
     if (lane == 0) x.inrow()[i] = row;
     if (row == kNoRow) {
       if (lane == 0) raise_status(status, kStatusTableFull);
@@ -660,17 +697,6 @@ k_ex_dedupe(ExView x, const K *__restrict__ keys, size_t n, DedupeWs w, K *__res
   }
   __syncthreads();
   if (i < n) w.pos_slot[i] = hl == kNoRow ? kNoRow : s_gslot[hl];
-}
-
-// inverse[i]: the distinct-key index of position i.
-__global__ void __launch_bounds__(256) k_ex_dedupe_inverse(ExView x, size_t n, DedupeWs w) {
-  pdl_wait();
-  pdl_trigger();
-  if (ex_failed(x)) return;
-  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
-    const uint32_t slot = w.pos_slot[i];
-    w.inverse[i] = slot == kNoRow ? 0u : __ldcg(w.set_idx + slot);
-  }
 }
 
 // Requester of a deduplicated forward: waits for the rows of every owner

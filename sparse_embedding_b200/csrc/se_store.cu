@@ -1786,6 +1786,7 @@ enum Ctr : int {
   kCtrFwdN = 20,       // keys cached by the last lookup_or_insert (FwdCache::n)
   kCtrFwdDeferred = 21,  // k_lookup_or_insert's deferred positions (zero between launches)
   kCtrEraseEpoch = 22,   // erases so far (rows listed by the atomic accumulate carry it)
+  kCtrOwnerDone = 23,    // blocks of the running k_ex_owner (insert) that have finished
   kCtrWords = 24,
 };
 
@@ -3429,11 +3430,13 @@ struct ExchangeImpl {
   // count_dev: the batch's size on the device (at most n), or null.
   template <class K>
   const uint32_t *run_route(const K *keys, size_t n, int dir, int kind, cudaStream_t st,
-                            const uint32_t *count_dev = nullptr) {
+                            const uint32_t *count_dev = nullptr, const DedupeWs *dws = nullptr) {
     const uint32_t tiles = std::max(uint32_t((n + kExTile - 1) / kExTile), 1u);
     uint32_t *tile_counts = route[dir], *tile_offsets = tile_counts + size_t(tiles_cap) * W;
     uint32_t *counts = tile_offsets + size_t(tiles_cap) * W;
-    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, keys, n, tile_counts, count_dev);
+    pdl(k_ex_count<K>, tiles, kRouteThreads, W * 4, st, spec, view, keys, n, tile_counts, count_dev,
+        dws ? static_cast<const uint32_t *>(dws->pos_slot) : nullptr,
+        dws ? static_cast<const uint32_t *>(dws->set_idx) : nullptr, dws ? dws->inverse : nullptr, n);
     launched("k_ex_count");
     pdl(k_ex_sync_counts, 1, kRouteThreads, 0, st, view, kind, tiles, tile_counts, tile_offsets, counts);
     launched("k_ex_sync_counts");
@@ -3463,6 +3466,10 @@ struct ExchangeImpl {
     const bool dd = dedupe && n > 0;
     if (dd) parity ^= 1u;
     const DedupeWs dws = dedupe_ws();
+    if (insert) {  // the owner kernel's deferred keys and finished blocks (here, not between the KEYS wait and it)
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
+      cuda_check(cudaMemsetAsync(t.ctr + kCtrOwnerDone, 0, 4, st), "memset");
+    }
     dispatch_key(store->cfg.key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
@@ -3472,12 +3479,11 @@ struct ExchangeImpl {
         pdl(k_ex_dedupe<K>, grid_for(n, 256, 0x7fffffffu), 256, 0, st, view, k, n, dws,
             reinterpret_cast<K *>(dd_ukeys));
         launched("k_ex_dedupe");
-        pdl(k_ex_dedupe_inverse, grid_for(n, 256, 148 * 8), 256, 0, st, view, n, dws);
-        launched("k_ex_dedupe_inverse");
         k = reinterpret_cast<const K *>(dd_ukeys);
         count_dev = dws.count;
       }
-      const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st, count_dev);
+      // the route count of a deduplicated batch also writes its inverse
+      const uint32_t *counts = run_route<K>(k, n, 0, kExCounts, st, count_dev, dd ? &dws : nullptr);
       StoreImpl::Prof pr(store, "k_ex_scatter_keys", st);
       pdl(k_ex_scatter<K, false, uint4>, std::max(tiles, 1u), kRouteThreads, (kRouteWarps + 1) * W * 4, st,
           spec, view, k, n, route[0] + size_t(tiles_cap) * W, counts, nullptr, key_pid, key_slot, count_dev);
@@ -3487,10 +3493,7 @@ struct ExchangeImpl {
     sync(kExKeys, st);
     // owner side: at most W * M keys arrive
     const uint64_t WM = uint64_t(W) * M;
-    if (insert) {
-      store->ensure_rows(t, WM, st);
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
-    }
+    if (insert) store->ensure_rows(t, WM, st);
     uint32_t *def_idx = t.def_pos.get(WM);
     unsigned long long *def_word = t.def_word.get(WM);
     const InitSpec init = init_spec();
@@ -3502,15 +3505,12 @@ struct ExchangeImpl {
       if (insert) {
         pdl(k_ex_owner<LN, VC, true>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.alloc(),
                                                         init, view, t.ctr + kCtrDeferred, def_idx, def_word,
-                                                        t.ctr + kCtrStatus);
+                                                        t.ctr + kCtrStatus, t.ctr + kCtrOwnerDone);
         launched("k_ex_owner");
-        pdl(k_ex_owner_deferred<LN, VC>, 148, 256, 0, st, t.L, t.slabs, view, t.ctr + kCtrDeferred, def_idx,
-                                                             def_word, t.ctr + kCtrStatus);
-        launched("k_ex_owner_deferred");
       } else {
         pdl(k_ex_owner<LN, VC, false>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.alloc(),
                                                          init, view, nullptr, nullptr, nullptr,
-                                                         t.ctr + kCtrStatus);
+                                                         t.ctr + kCtrStatus, nullptr);
         launched("k_ex_owner");
       }
     };
