@@ -1787,7 +1787,8 @@ enum Ctr : int {
   kCtrFwdDeferred = 21,  // k_lookup_or_insert's deferred positions (zero between launches)
   kCtrEraseEpoch = 22,   // erases so far (rows listed by the atomic accumulate carry it)
   kCtrOwnerDone = 23,    // blocks of the running k_ex_owner (insert) that have finished
-  kCtrWords = 24,
+  kCtrOwnerDeferred = 24,  // k_ex_owner's deferred keys (zero between launches)
+  kCtrWords = 32,
 };
 
 struct Table {
@@ -3393,6 +3394,12 @@ struct ExchangeImpl {
 
   void finish_connect() {
     cuda_check(cudaMemcpy(d_peers, peers.data(), W * sizeof(uint8_t *), cudaMemcpyHostToDevice), "upload peers");
+    {  // the owner kernel's counters start at zero (its last block resets them after every launch)
+      std::lock_guard<std::mutex> lock(store->mu);
+      Table &t = store->table(dim);
+      cuda_check(cudaMemset(t.ctr + kCtrOwnerDeferred, 0, 4), "memset");
+      cuda_check(cudaMemset(t.ctr + kCtrOwnerDone, 0, 4), "memset");
+    }
     view.peer = d_peers;
     connected = true;
   }
@@ -3466,10 +3473,6 @@ struct ExchangeImpl {
     const bool dd = dedupe && n > 0;
     if (dd) parity ^= 1u;
     const DedupeWs dws = dedupe_ws();
-    if (insert) {  // the owner kernel's deferred keys and finished blocks (here, not between the KEYS wait and it)
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrDeferred, 0, 4, st), "memset");
-      cuda_check(cudaMemsetAsync(t.ctr + kCtrOwnerDone, 0, 4, st), "memset");
-    }
     dispatch_key(store->cfg.key_dtype, [&](auto tag) {
       using K = decltype(tag);
       const K *k = static_cast<const K *>(keys);
@@ -3504,7 +3507,7 @@ struct ExchangeImpl {
       StoreImpl::Prof pr(store, "k_ex_owner", st);
       if (insert) {
         pdl(k_ex_owner<LN, VC, true>, grid, 256, 0, st, t.dir(), t.L, t.slabs, t.alloc(),
-                                                        init, view, t.ctr + kCtrDeferred, def_idx, def_word,
+                                                        init, view, t.ctr + kCtrOwnerDeferred, def_idx, def_word,
                                                         t.ctr + kCtrStatus, t.ctr + kCtrOwnerDone);
         launched("k_ex_owner");
       } else {
