@@ -51,3 +51,31 @@ def test_graph_replay_matches_eager():
     b, _ = graphed.lookup(probe, 64)
     assert torch.equal(a.view(torch.int32), b.view(torch.int32))
     assert eager.total_size() == graphed.total_size()
+
+
+def test_insert_captured_after_eager_calls_finds_room():
+    """The table's row bound carries every insert call's whole batch (new
+    rows are known only on the device). After eager calls that bring the
+    bound near the capacity, a call of the same size captured next in a CUDA
+    graph - which can neither read the rows in use nor grow the arena - still
+    finds its room: every uncaptured call leaves room for one more of its
+    size, reading the rows in use again when the bound leaves less."""
+    n, used = 65_536, 100_000
+    cap = used + 5 * n // 2
+    st = se.EmbeddingStore(se.EmbeddingConfig(dims=[16], key_dtype="int64", initial_capacity=cap),
+                           optimizer_config=se.Sgd(lr=0.01))
+    keys = torch.arange(1, used + 1, dtype=torch.int64, device="cuda")
+    st.lookup_or_insert(keys, 16)
+    batch = keys[:n].clone()
+    for _ in range(2):
+        st.lookup_or_insert(batch, 16)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        rows, _ = st.lookup_or_insert(batch, 16)
+    g.replay()
+    torch.cuda.synchronize()
+    want, _ = st.lookup(batch, 16)
+    assert torch.equal(rows.view(torch.int32), want.view(torch.int32))
+    assert st.total_size() == used
+    del g
