@@ -2099,22 +2099,19 @@ struct StoreImpl {
     uint64_t need = t.rows_bound + extra;
     const auto dir_limit = [&](uint64_t nb) { return uint64_t(double(nb) * kMaxLoadPerBucket); };
     // The bound carries each call's whole batch (the new rows are known only
-    // on the device), so it drifts above the rows in use. After this call
-    // there is room for one more call of the same size, so that a call
-    // captured next in a CUDA graph - which can neither read the rows in use
-    // nor grow - finds it: the rows in use are read again (a sync) when the
-    // bound leaves less, and the arena grows when they do.
+    // on the device), so it drifts above the rows in use. When it leaves no
+    // room for one more call of this size after this one, the rows in use
+    // are read again (a sync): a call captured next in a CUDA graph, which
+    // can neither read them nor grow the arena, then finds its room whenever
+    // the rows in use leave it. The arena grows only when this call needs it.
     // Directory slots in use: at most the rows ever taken plus the erased
     // keys' tombstones (a rehash drops those).
     if (need + extra > t.capacity || need + extra + t.tombs > dir_limit(t.nbuckets)) {
       t.rows_bound = read_rows_used(t, st);
       need = t.rows_bound + extra;
       if (need > 0xfffffff0ull) throw Error(SE_ERR_TABLE_FULL, "table exceeds 2^32 rows");
-      if (need + extra > t.capacity) {
-        // row numbers are 32-bit: near that limit only the call itself keeps its room
-        const uint64_t ncap = std::max<uint64_t>(need, std::min<uint64_t>(std::max<uint64_t>(need + extra,
-                                                                                            t.capacity * 2),
-                                                                          0xfffffff0ull));
+      if (need > t.capacity) {
+        const uint64_t ncap = std::max<uint64_t>(need, t.capacity * 2);
         uint8_t *ns = dalloc<uint8_t>(size_t(ncap) * t.L.stride);
         cuda_check(cudaMemcpyAsync(ns, t.slabs, size_t(t.rows_bound) * t.L.stride,
                                    cudaMemcpyDeviceToDevice, st), "grow arena");
@@ -2125,9 +2122,9 @@ struct StoreImpl {
         t.capacity = ncap;
         alloc_row_arrays(t, ncap, old_cap, st);
       }
-      if (need + extra + t.tombs > dir_limit(t.nbuckets)) {
+      if (need + t.tombs > dir_limit(t.nbuckets)) {
         uint64_t nb = t.nbuckets;
-        while (dir_limit(nb) < std::max(need + extra, t.capacity)) nb *= 2;
+        while (dir_limit(nb) < std::max(need, t.capacity)) nb *= 2;
         Bucket *nbk = dalloc<Bucket>(nb);
         cuda_check(cudaMemsetAsync(nbk, 0xff, nb * sizeof(Bucket), st), "memset directory");
         Dir nd{nbk, nb, t.ctr + kCtrSpecialClaim};
